@@ -1,0 +1,579 @@
+"""Benchmark of the snapmind KV-cache hot path on B200.
+
+Headline workload (one "step" = one decode step of the KV path over one batch):
+paged GQA decode at the Llama-3-8B KV shape — 32 layers x (append one token per
+sequence into the paged pool + paged GQA decode attention over the whole
+context), 32 q heads / 8 kv heads, head_dim 128, bf16, block_size 16, 128
+sequences per GPU with contexts uniform in [1024, 8192], shuffled block tables.
+``value`` = decode tok/s of the whole job (sequences x steps / max-over-ranks
+time); the projections and MLP GEMMs of a full model are not part of the path.
+
+Secondary workload in the same line (``kv_append_gather``): the isolated paged
+KV append + full gather at the same KV shape, 64 sequences with contexts
+uniform in [512, 4096], pool = total blocks + 10%, in HBM GB/s of algorithmic
+bytes.
+
+Multi-GPU: one process per GPU (torchrun), each rank owns its own sequences,
+pool and block tables — sequence sharding with no data-path collective
+(weak scaling; the only collectives are the timing barrier and max).
+
+``--impl reference`` times the reference algorithm on the host CPU instead:
+the oracle port (per-token store loop, per-block fetch concatenation,
+repeat_interleave + matmul + softmax + matmul) of the same workload over a
+bounded sample of sequences, spread over all host cores with a spawn pool.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s/GPU (paged KV, Llama-3-8B shape); KV append/gather HBM GB/s"
+L, HQ, H, D, BS = 32, 32, 8, 128, 16
+DECODE_BATCH, DECODE_CTX = 128, (1024, 8192)
+AG_BATCH, AG_CTX = 64, (512, 4096)
+ELEM = 2  # bf16
+
+
+# ----------------------------------------------------------------------------- helpers
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def profile_traffic(kernel: str) -> dict | None:
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    return json.loads(p.read_text()).get(kernel)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict | None:
+        rows = []
+        for ln in getattr(self, "lines", []):
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def seeded_lengths(seed: int, n: int, lo: int, hi: int) -> np.ndarray:
+    return np.random.RandomState(seed).randint(lo, hi + 1, size=n).astype(np.int64)
+
+
+def shuffled_tables(seed: int, lens: np.ndarray, growth: int, slack: float = 1.1):
+    """Block tables over a randomly permuted shared pool of total blocks + slack."""
+    need = (lens + growth + BS - 1) // BS
+    nb = int(math.ceil(need.sum() * slack))
+    perm = np.random.RandomState(seed + 1).permutation(nb).astype(np.int32)
+    width = int(need.max())
+    tables = np.zeros((len(lens), width), np.int32)
+    off = 0
+    for b, n in enumerate(lens):
+        k = (int(n) + BS - 1) // BS
+        tables[b, :k] = perm[off:off + k]
+        off += k
+    return nb, width, tables, perm[off:]
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def run_b200(args, rank: int, world: int, dist) -> dict | None:
+    import torch
+
+    from snapmind_b200 import PagedKVPool
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    steps, warmup = args.steps, args.warmup
+    seed = 1234 + 7919 * rank
+
+    # ---------------- decode workload ----------------
+    lens = seeded_lengths(seed, DECODE_BATCH, *DECODE_CTX)
+    growth = steps + warmup + 16
+    nb, width, tables, free = shuffled_tables(seed, lens, growth)
+    pool = PagedKVPool(L, H, D, nb, max_seqs=DECODE_BATCH, max_blocks_per_seq=width, block_size=BS,
+                       dtype=torch.bfloat16, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    pool.k.normal_(generator=g)
+    pool.v.normal_(generator=g)
+    pool.set_state(tables, lens, free)
+    q_all = torch.randn((L, DECODE_BATCH, HQ, D), device=dev, generator=g).to(torch.bfloat16)
+    k_all = torch.randn((L, DECODE_BATCH, H, D), device=dev, generator=g).to(torch.bfloat16)
+    v_all = torch.randn((L, DECODE_BATCH, H, D), device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty((L, DECODE_BATCH, HQ, D), device=dev, dtype=torch.bfloat16)
+    max_len = int(lens.max()) + growth
+    split = 0
+
+    def decode_step(events=None):
+        pool.reserve(1, batch=DECODE_BATCH)
+        for layer in range(L):
+            pool.append(layer, k_all[layer], v_all[layer])
+            if events is not None:
+                events[layer][0].record()
+            pool.decode(layer, q_all[layer], out=out[layer], max_seq_len=max_len, split_tokens=split)
+            if events is not None:
+                events[layer][1].record()
+
+    for _ in range(warmup):
+        decode_step()
+    pool.check()
+    launches_per_step = 1 + 2 * L
+    kv_tokens_before = int(pool.host_lens[:DECODE_BATCH].sum())
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+          for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(dist)
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clocks:
+        t0.record()
+        for s in range(steps):
+            decode_step(ev[s])
+        t1.record()
+        torch.cuda.synchronize()
+    barrier(dist)
+    ms = t0.elapsed_time(t1)
+    pool.check()
+    ms_max = reduce_max(dist, ms, dev)
+    kernel_ms = [e0.elapsed_time(e1) for row in ev for (e0, e1) in row]
+    # algorithmic bytes of one decode launch: every cached K and V row once, q in, out back;
+    # step s (1-based) attends over kv_tokens_before + s * batch tokens
+    mean_ctx_tokens = kv_tokens_before + DECODE_BATCH * (steps + 1) / 2.0
+    bytes_per_launch = mean_ctx_tokens * H * D * ELEM * 2 + 2 * DECODE_BATCH * HQ * D * ELEM
+    kernel_avg_ms = statistics.fmean(kernel_ms)
+    achieved_gbs = bytes_per_launch / (kernel_avg_ms * 1e-3) / 1e9
+    pk = peaks()
+    traffic = profile_traffic("paged_decode")
+    value = DECODE_BATCH * world * steps / (ms_max * 1e-3)
+
+    # ---------------- e2e: host buffers through the public API ----------------
+    q_h = torch.empty_like(q_all, device="cpu").pin_memory()
+    k_h = torch.empty_like(k_all, device="cpu").pin_memory()
+    v_h = torch.empty_like(v_all, device="cpu").pin_memory()
+    o_h = torch.empty_like(out, device="cpu").pin_memory()
+    q_h.copy_(q_all)
+    k_h.copy_(k_all)
+    v_h.copy_(v_all)
+    q_d, k_d, v_d = torch.empty_like(q_all), torch.empty_like(k_all), torch.empty_like(v_all)
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        k_d.copy_(k_h, non_blocking=True)
+        v_d.copy_(v_h, non_blocking=True)
+        pool.reserve(1, batch=DECODE_BATCH)
+        for layer in range(L):
+            pool.append(layer, k_d[layer], v_d[layer])
+            pool.decode(layer, q_d[layer], out=out[layer], max_seq_len=max_len, split_tokens=split)
+        o_h.copy_(out, non_blocking=True)
+
+    e2e_steps = max(1, min(steps, 10))
+    e2e_step()
+    barrier(dist)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(dist)
+    pool.check()
+    e2e_ms = reduce_max(dist, e0.elapsed_time(e1) / e2e_steps, dev)
+    h2d = (q_all.numel() + k_all.numel() + v_all.numel()) * ELEM
+    d2h = out.numel() * ELEM
+    del pool, q_all, k_all, v_all, out, q_d, k_d, v_d
+    torch.cuda.empty_cache()
+
+    # ---------------- append + gather workload ----------------
+    ag = run_append_gather(args, dev, seed, dist, world)
+
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": round(ms_max / steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V/q, seeded context lengths and shuffled block tables)",
+        "config": {
+            "workload": "paged GQA decode step, Llama-3-8B KV shape: 32 layers x (append 1 token/seq + "
+                        "paged decode attention); 32 q / 8 kv heads, head_dim 128, bf16, block 16, "
+                        "ctx U[1024,8192], shuffled block tables",
+            "batch_per_gpu": DECODE_BATCH,
+            "global_batch": DECODE_BATCH * world,
+            "layers": L,
+            "parallelism": f"dp{world} (sequence sharding, no data-path collective)",
+            "l2": "inputs larger than L2 (about 2.4 GB of K/V per decode launch)",
+        },
+        "roofline": {
+            "kernel": "paged_gqa_decode",
+            "bound": "hbm",
+            "achieved": round(achieved_gbs, 1),
+            "peak": pk["hbm_gbs"],
+            "peak_source": pk["source"],
+            "unit": "GB/s",
+            "frac": round(achieved_gbs / pk["hbm_gbs"], 4),
+            "traffic": None if traffic is None else traffic.get("bytes_per_launch_scaled"),
+            "algorithmic_bytes_per_launch": int(bytes_per_launch),
+            "kernel_ms_avg": round(kernel_avg_ms, 4),
+        },
+        "e2e": {
+            "value": round(DECODE_BATCH * world / (e2e_ms * 1e-3), 2),
+            "unit": "tok/s",
+            "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h),
+        },
+        "kv_append_gather": ag,
+        "gpu_launches": launches_per_step * steps,
+        "clocks": clocks.summary(),
+    }
+    return line
+
+
+def run_append_gather(args, dev, seed, dist, world) -> dict:
+    import torch
+
+    from snapmind_b200 import PagedKVPool
+
+    steps, warmup = args.steps, args.warmup
+    lens = seeded_lengths(seed + 17, AG_BATCH, *AG_CTX)
+    nb, width, tables, free = shuffled_tables(seed + 17, lens, steps + warmup + 4)
+    pool = PagedKVPool(L, H, D, nb, max_seqs=AG_BATCH, max_blocks_per_seq=width, block_size=BS,
+                       dtype=torch.bfloat16, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed + 17)
+    pool.k.normal_(generator=g)
+    pool.v.normal_(generator=g)
+    pool.set_state(tables, lens, free)
+    k_new = torch.randn((L, AG_BATCH, H, 1, D), device=dev, generator=g).to(torch.bfloat16)
+    v_new = torch.randn((L, AG_BATCH, H, 1, D), device=dev, generator=g).to(torch.bfloat16)
+    max_tokens = int(lens.sum()) + AG_BATCH * (steps + warmup + 1)
+    k_out = torch.empty((L, max_tokens * H * D), dtype=torch.bfloat16, device=dev)
+    v_out = torch.empty_like(k_out)
+
+    # the packed output of each layer is contiguous: a per-step view of the right size
+    def step(evs=None):
+        pool.reserve(1, batch=AG_BATCH)
+        if evs is not None:
+            evs[0].record()
+        pool.append(None, k_new, v_new)
+        if evs is not None:
+            evs[1].record()
+        per_layer = int(pool.host_lens[:AG_BATCH].sum()) * H * D
+        ko = k_out.view(-1)[: L * per_layer].view(L, per_layer)
+        vo = v_out.view(-1)[: L * per_layer].view(L, per_layer)
+        pool.gather(batch=AG_BATCH, out=(ko, vo))
+        if evs is not None:
+            evs[2].record()
+
+    for _ in range(warmup):
+        step()
+    pool.check()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    tok_before = int(pool.host_lens[:AG_BATCH].sum())
+    barrier(dist)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for s in range(steps):
+        step(evs[s])
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(dist)
+    pool.check()
+    ms = reduce_max(dist, t0.elapsed_time(t1), dev)
+    tok_after = int(pool.host_lens[:AG_BATCH].sum())
+    row = H * D * ELEM  # bytes of one token's K (or V) in one layer
+    append_bytes = 2 * 2 * AG_BATCH * L * row  # K and V, read + write
+    mean_tokens = (tok_before + AG_BATCH + tok_after) / 2.0
+    gather_bytes = 2 * 2 * mean_tokens * L * row
+    total_bytes = (append_bytes + gather_bytes) * steps
+    append_ms = statistics.fmean(e[0].elapsed_time(e[1]) for e in evs)
+    gather_ms = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
+    pk = peaks()
+    gather_gbs = gather_bytes / (gather_ms * 1e-3) / 1e9
+    traffic = profile_traffic("kv_gather")
+    res = {
+        "value": round(total_bytes * world / (ms * 1e-3) / 1e9, 1),
+        "unit": "GB/s",
+        "workload": "paged KV append (1 token/seq, all 32 layers, one launch) + full gather of all "
+                    "layers, Llama-3-8B KV shape, 64 seqs/GPU, ctx U[512,4096], pool = blocks + 10%",
+        "ms_per_step": round(ms / steps, 4),
+        "append_ms": round(append_ms, 4),
+        "gather_ms": round(gather_ms, 4),
+        "append_gbs": round(append_bytes / (append_ms * 1e-3) / 1e9, 1),
+        "roofline": {
+            "kernel": "kv_gather",
+            "bound": "hbm",
+            "achieved": round(gather_gbs, 1),
+            "peak": pk["hbm_gbs"],
+            "peak_source": pk["source"],
+            "unit": "GB/s",
+            "frac": round(gather_gbs / pk["hbm_gbs"], 4),
+            "traffic": None if traffic is None else traffic.get("bytes_per_launch_scaled"),
+            "algorithmic_bytes_per_launch": int(gather_bytes),
+        },
+        "gpu_launches": 3 * steps,
+    }
+    del pool, k_out, v_out
+    torch.cuda.empty_cache()
+    return res
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def reduce_max(dist, x: float, dev) -> float:
+    if dist is None:
+        return x
+    import torch
+
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- CPU (reference algorithm)
+def _cpu_build(seed: int, lens: list[int], n_layer_pools: int):
+    """Reference-layout paged data (a few layer pools) for each sequence of ``lens``."""
+    import oracle.paged as op
+
+    rng = np.random.RandomState(seed)
+    caches = []
+    for n in lens:
+        layers = []
+        for _ in range(n_layer_pools):
+            c = op.PagedKVCacheOracle(max_seq_len=n + 64, n_layers=1, n_heads=H, head_dim=D, block_size=BS)
+            k = rng.standard_normal((1, H, n, D)).astype(np.float32)
+            v = rng.standard_normal((1, H, n, D)).astype(np.float32)
+            # prefill without the per-token loop (not timed), same slot layout as store()
+            nbk = (n + BS - 1) // BS
+            blocks = [c.free_blocks.pop() for _ in range(nbk)]
+            c.block_tables[0] = blocks
+            for j, p in enumerate(blocks):
+                t0, t1 = j * BS, min(n, (j + 1) * BS)
+                c.k[p, : t1 - t0] = k[0, :, t0:t1].transpose(1, 0, 2)
+                c.v[p, : t1 - t0] = v[0, :, t0:t1].transpose(1, 0, 2)
+            c.slot_counts[0] = n
+            layers.append(c)
+        caches.append(layers)
+    q = rng.standard_normal((1, HQ, 1, D)).astype(np.float32)
+    kv = rng.standard_normal((1, H, 1, D)).astype(np.float32)
+    return caches, q, kv
+
+
+def _cpu_decode(caches, q, kv):
+    """One decode step of each sequence over all layers: store + fetch + GQA math (reference path)."""
+    import oracle.gqa as og
+
+    for layers in caches:
+        for layer in range(L):
+            c = layers[layer % len(layers)]
+            c.store(0, kv, kv, 0)
+            k, v = c.fetch(0)
+            og.gqa_attention(q, k, v, D ** -0.5, dtype=np.float32)
+            c.slot_counts[0] -= 1  # the sample's context stays fixed across steps
+
+
+def _cpu_worker(conn, seed: int, lens: list[int]):
+    caches, q, kv = _cpu_build(seed, lens, 2)
+    conn.send("ready")
+    while conn.recv() == "step":
+        _cpu_decode(caches, q, kv)
+        conn.send("done")
+
+
+def cpu_reference_timing(n_seqs: int, steps: int, warmup: int, seed: int = 99) -> dict:
+    """Time the reference algorithm on ``n_seqs`` sampled sequences, one worker
+    process per core (each owning a fixed share of the sample)."""
+    import multiprocessing as mp
+
+    cores = os.cpu_count() or 1
+    workers = max(1, min(cores, n_seqs))
+    lens = seeded_lengths(seed, n_seqs, *DECODE_CTX).tolist()
+    ctx = mp.get_context("spawn")
+    procs, conns = [], []
+    # one BLAS thread per worker process: the workers themselves cover the cores
+    thread_vars = ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS")
+    saved = {k: os.environ.get(k) for k in thread_vars}
+    os.environ.update({k: "1" for k in thread_vars})
+    try:
+        for w in range(workers):
+            parent, child = ctx.Pipe()
+            p = ctx.Process(target=_cpu_worker, args=(child, seed + w, lens[w::workers]), daemon=True)
+            p.start()
+            procs.append(p)
+            conns.append(parent)
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    try:
+        for c in conns:
+            c.recv()
+        times = []
+        for i in range(warmup + steps):
+            t = time.perf_counter()
+            for c in conns:
+                c.send("step")
+            for c in conns:
+                c.recv()
+            if i >= warmup:
+                times.append(time.perf_counter() - t)
+    finally:
+        for c in conns:
+            try:
+                c.send("stop")
+            except OSError:
+                pass
+        for p in procs:
+            p.join(timeout=10)
+            if p.is_alive():
+                p.terminate()
+    step_s = statistics.median(times)
+    return {"value": round(n_seqs / step_s, 3), "unit": "tok/s", "cores": workers, "kind": "port",
+            "sample": f"{n_seqs} sequences (ctx U[1024,8192]) x 32 layers per step, reference algorithm "
+                      f"(per-token store, per-block fetch concat, repeat_interleave/matmul/softmax/matmul, fp32) "
+                      f"in {workers} worker processes; median of {steps} steps",
+            "step_s": round(step_s, 3)}
+
+
+def run_reference_arm(args, rank: int, world: int) -> dict | None:
+    if rank != 0:
+        return None
+    res = cpu_reference_timing(n_seqs=args.cpu_sample, steps=args.steps, warmup=min(args.warmup, 1))
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": res["value"],
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(res["step_s"] * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "reference paged KV decode path on the host CPU (oracle port of "
+                               "snapmind/kv_cache/paged.py + snapmind/layers/attention/gqa.py), Llama-3-8B KV shape",
+                   "batch_sample": args.cpu_sample, "layers": L},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-sample", type=int, default=min(128, max(8, os.cpu_count() or 8)))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+
+    if args.impl == "reference":
+        line = run_reference_arm(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    # the CPU baseline's spawn pool starts before any CUDA work on this process
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference_timing(n_seqs=args.cpu_sample, steps=3, warmup=1)
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as tdist
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist = tdist
+    try:
+        line = run_b200(args, rank, world, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+    if rank == 0 and line is not None:
+        if cpu is not None:
+            line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

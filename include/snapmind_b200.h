@@ -1,0 +1,180 @@
+/*
+ * snapmind_b200 — C ABI of the B200 (sm_100a) KV-cache hot path of snapmind.
+ *
+ * Plain C: device pointers, element strides, sizes, a cudaStream_t passed as
+ * `void *`.  Every entry point returns an int status; on failure the message
+ * of the calling host thread's last error is returned by snapmind_last_error().
+ * No entry point allocates device memory; callers own every buffer.
+ *
+ * Paged pool layout (one pool for K, one for V):
+ *     pool[layer][block][head][slot][dim]      (dim contiguous)
+ * A (block, head) tile of block_size x head_dim elements is contiguous, so a
+ * gather moves whole tiles and the decode kernel stages one tile per TMA copy.
+ * `pool_layer_stride` is the element distance between consecutive layers
+ * (0 when a call covers a single layer).
+ *
+ * Block tables are int32 rows of physical block ids: entry j of sequence b
+ * (layer l when tables are per layer) lives at
+ *     block_tables[l * table_stride_layer + b * table_stride_seq + j].
+ *
+ * Device error word: kernels never trap.  An out-of-range block id, table
+ * entry or split skips the access and ORs a SNAPMIND_DEVERR_* bit into
+ * `*err_word` (a device int32 the caller owns and may pass as NULL).
+ */
+#ifndef SNAPMIND_B200_H_
+#define SNAPMIND_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SNAPMIND_API __attribute__((visibility("default")))
+#else
+#define SNAPMIND_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define SNAPMIND_OK 0
+#define SNAPMIND_ERR_OUT_OF_BLOCKS 1 /* "PagedKVCache: out of blocks" */
+#define SNAPMIND_ERR_BAD_ARGUMENT 2
+#define SNAPMIND_ERR_CUDA 3
+#define SNAPMIND_ERR_TIMEOUT 4
+#define SNAPMIND_ERR_UNSUPPORTED 5
+
+/* element types */
+#define SNAPMIND_DTYPE_F32 0
+#define SNAPMIND_DTYPE_BF16 1
+#define SNAPMIND_DTYPE_F16 2
+
+/* device error word bits */
+#define SNAPMIND_DEVERR_BLOCK_ID 1      /* physical block id outside [0, num_blocks) */
+#define SNAPMIND_DEVERR_TABLE 2         /* logical block index outside the table row */
+#define SNAPMIND_DEVERR_SPLIT 4         /* sequence longer than the split plan covers */
+#define SNAPMIND_DEVERR_OUT_OF_BLOCKS 8 /* reserve found too few free blocks */
+#define SNAPMIND_DEVERR_TIMEOUT 16      /* a bounded device wait gave up */
+
+/* decode flags */
+#define SNAPMIND_DECODE_FORCE_GENERIC 1 /* use the CUDA-core kernel even where the tensor-core one applies */
+
+SNAPMIND_API int snapmind_abi_version(void);
+SNAPMIND_API const char *snapmind_last_error(void);
+
+/*
+ * Append n_tokens K/V rows per sequence into the paged pools.
+ * Replaces the per-token slice writes of PagedKVCache.store
+ * (snapmind/kv_cache/paged.py:34-54): token t of sequence b goes to slot
+ * s = slot_start(b) + t, block table entry s / block_size, row s % block_size.
+ * slot_start(b) = slot_starts[b] + slot_start0 when slot_starts != NULL, else
+ * slot_start0.  Input element (layer, b, head, t, d) is read at
+ * k_new + layer*in_stride_layer + b*in_stride_seq + head*in_stride_head
+ *       + t*in_stride_tok + d.
+ * Input and pool dtypes may differ (values are converted, round to nearest even).
+ * Table entries must already exist (the host or snapmind_kv_reserve grows them).
+ */
+SNAPMIND_API int snapmind_kv_append(void *k_pool, void *v_pool, int pool_dtype, int64_t pool_layer_stride,
+                       const void *k_new, const void *v_new, int in_dtype,
+                       int64_t in_stride_layer, int64_t in_stride_seq, int64_t in_stride_head,
+                       int64_t in_stride_tok,
+                       const int32_t *block_tables, int64_t table_stride_seq,
+                       int64_t table_stride_layer, int32_t table_width,
+                       const int32_t *slot_starts, int32_t slot_start0,
+                       int32_t n_layers, int32_t batch, int32_t n_tokens, int32_t n_heads,
+                       int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                       int32_t *err_word, void *stream);
+
+/*
+ * Gather the first seq_len(b) tokens of every sequence out of the paged pools.
+ * Replaces PagedKVCache.fetch (snapmind/kv_cache/paged.py:56-78): the output of
+ * each layer is the concatenation over b of (n_heads, seq_len(b), head_dim)
+ * blocks — for one sequence exactly the (1, H, T, D) tensor fetch returns.
+ * seq_len(b) = seq_lens[b] when seq_lens != NULL, else seq_len0.
+ * Output layer l starts at k_out + l*out_layer_stride and holds
+ * out_layer_capacity elements; when the lengths need more, nothing is written
+ * and SNAPMIND_DEVERR_TABLE is set.  batch <= 8192.
+ */
+SNAPMIND_API int snapmind_kv_gather(const void *k_pool, const void *v_pool, int dtype, int64_t pool_layer_stride,
+                       void *k_out, void *v_out, int64_t out_layer_stride,
+                       int64_t out_layer_capacity,
+                       const int32_t *block_tables, int64_t table_stride_seq,
+                       int64_t table_stride_layer, int32_t table_width,
+                       const int32_t *seq_lens, int32_t seq_len0,
+                       int32_t n_layers, int32_t batch, int32_t n_heads, int32_t head_dim,
+                       int32_t block_size, int32_t num_blocks, int32_t *err_word, void *stream);
+
+/*
+ * Move n token rows (all heads, K and V) inside one layer's pools, reading
+ * every source row before writing any destination row.  Replaces the
+ * clone-then-assign compaction loop of PagedKVCache.evict
+ * (snapmind/kv_cache/paged.py:96-113).  The four index arrays are HOST arrays
+ * of n entries (copied into the launch parameters); n <= 64.
+ */
+SNAPMIND_API int snapmind_kv_copy_slots(void *k_pool, void *v_pool, int dtype,
+                           const int32_t *src_blocks, const int32_t *src_rows,
+                           const int32_t *dst_blocks, const int32_t *dst_rows, int32_t n,
+                           int32_t n_heads, int32_t head_dim, int32_t block_size,
+                           int32_t num_blocks, int32_t *err_word, void *stream);
+
+/*
+ * Reserve room for n_new tokens in each of `batch` sequences sharing one pool
+ * (the batched form of the block growth in PagedKVCache.store,
+ * snapmind/kv_cache/paged.py:38-42).  Sequences that cross a block boundary
+ * take blocks from the top of the device free stack in ascending sequence
+ * order; seq_lens[b] += n_new.  All or nothing: when the stack holds too few
+ * blocks or a table row is too short, nothing changes and the matching
+ * SNAPMIND_DEVERR_* bit is set.
+ */
+SNAPMIND_API int snapmind_kv_reserve(int32_t *block_tables, int64_t table_stride_seq, int32_t table_width,
+                        int32_t *seq_lens, int32_t batch, int32_t n_new, int32_t block_size,
+                        int32_t *free_stack, int32_t *free_top, int32_t num_blocks,
+                        int32_t *err_word, void *stream);
+
+/*
+ * Return the blocks of the listed sequences to the device free stack (in
+ * list order, each sequence's blocks in table order) and set their length to 0.
+ * seq_ids is a device array of n_release sequence indices.
+ */
+SNAPMIND_API int snapmind_kv_release(int32_t *block_tables, int64_t table_stride_seq, int32_t table_width,
+                        int32_t *seq_lens, const int32_t *seq_ids, int32_t n_release,
+                        int32_t block_size, int32_t *free_stack, int32_t *free_top,
+                        int32_t num_blocks, int32_t *err_word, void *stream);
+
+/*
+ * Paged GQA decode attention: one query token per sequence against the
+ * seq_lens[b] cached tokens reached through the block table.  Computes
+ * softmax(q k^T * scale) v per query head, query head h reading kv head
+ * h / (n_q_heads / n_kv_heads) — the math of GroupedQueryAttention.forward
+ * (snapmind/layers/attention/gqa.py:69-82: repeat_interleave, matmul, softmax,
+ * matmul) over the tokens PagedKVCache.fetch would return, without
+ * materialising either.  q, pools and out share `dtype`; accumulation is fp32.
+ *
+ * Long sequences are split into chunks of split_tokens tokens (a multiple of
+ * block_size; <= 0 picks snapmind_paged_gqa_decode_split_tokens) processed by
+ * separate CTAs; the last CTA of a sequence merges the partial softmax states.
+ * `workspace` must hold snapmind_paged_gqa_decode_workspace_bytes(...) bytes
+ * and be zero-filled once before its first use; each call leaves it reusable.
+ * Calls sharing one workspace must not overlap on the GPU.
+ */
+SNAPMIND_API int32_t snapmind_paged_gqa_decode_split_tokens(int32_t batch, int32_t n_kv_heads,
+                                               int32_t max_seq_len, int32_t block_size);
+SNAPMIND_API int64_t snapmind_paged_gqa_decode_workspace_bytes(int32_t batch, int32_t n_q_heads,
+                                                  int32_t n_kv_heads, int32_t head_dim,
+                                                  int32_t max_seq_len, int32_t split_tokens);
+SNAPMIND_API int snapmind_paged_gqa_decode(const void *q, int64_t q_stride_seq, int64_t q_stride_head,
+                              const void *k_pool, const void *v_pool, int dtype,
+                              const int32_t *block_tables, int64_t table_stride_seq,
+                              int32_t table_width, const int32_t *seq_lens,
+                              void *out, int64_t out_stride_seq, int64_t out_stride_head,
+                              float scale, int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
+                              int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                              int32_t max_seq_len, int32_t split_tokens, int32_t flags,
+                              void *workspace, int64_t workspace_bytes, int32_t *err_word,
+                              void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SNAPMIND_B200_H_ */

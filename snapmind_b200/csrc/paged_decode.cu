@@ -1,0 +1,315 @@
+// Paged GQA decode attention (split-K flash decoding) for sm_100a.
+//
+// Math: for each sequence b and query head h (kv head h / G, G = Hq / H),
+//     out[b, h] = softmax(q[b, h] . K[b, kv]^T * scale) V[b, kv]
+// over the seq_lens[b] tokens reached through the block table — the
+// repeat_interleave / matmul / softmax / matmul sequence of
+// GroupedQueryAttention.forward (snapmind/layers/attention/gqa.py:69-82)
+// applied to what PagedKVCache.fetch (snapmind/kv_cache/paged.py:56-78) would
+// return, without materialising either.
+//
+// Work split: CTA (split s, kv head, sequence b) covers tokens
+// [s*split_tokens, (s+1)*split_tokens).  Every CTA keeps an online-softmax
+// state (m, l, acc) per query head of its group; a sequence with one split
+// writes the output directly, otherwise each CTA stores its partial state in
+// the workspace and the CTA that takes the last ticket of the (b, kv head)
+// counter merges the partials and resets the counter (no CTA ever waits).
+#include <cfloat>
+
+#include "common.cuh"
+#include "paged_decode.cuh"
+
+namespace snapmind {
+
+// ---------------------------------------------------------------------------
+// generic CUDA-core kernel: any head_dim <= 256, any group size <= 16
+// ---------------------------------------------------------------------------
+constexpr int kGenericWarps = 4;
+
+template <typename T, int NI, int GMAX>
+__global__ void __launch_bounds__(kGenericWarps * 32)
+    paged_decode_generic_kernel(DecodeParams p) {
+  const int s = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = p.group;
+  const int D = p.head_dim;
+
+  int len = p.seq_lens[b];
+  if (len < 0) len = 0;
+  int n_splits = (len + p.split_tokens - 1) / p.split_tokens;
+  if (n_splits > p.max_splits) {
+    if (s == 0 && threadIdx.x == 0) flag_error(p.err, SNAPMIND_DEVERR_SPLIT);
+    n_splits = p.max_splits;
+    len = p.max_splits * p.split_tokens;
+  }
+  if (len == 0) {
+    // softmax over zero keys: the reference's matmul over an empty dim gives 0
+    if (s == 0) {
+      for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+        const int g = e / D, d = e - g * D;
+        T* o = reinterpret_cast<T*>(p.out) + (int64_t)b * p.out_stride_seq +
+               (int64_t)(kvh * G + g) * p.out_stride_head;
+        o[d] = Conv<T>::from_f(0.f);
+      }
+    }
+    return;
+  }
+  if (s >= n_splits) return;
+  const int t0 = s * p.split_tokens;
+  const int t1 = min(len, t0 + p.split_tokens);
+
+  const T* qb = reinterpret_cast<const T*>(p.q) + (int64_t)b * p.q_stride_seq;
+  float qr[GMAX][NI];
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int d = lane + 32 * i;
+      qr[g][i] = (g < G && d < D)
+                     ? Conv<T>::to_f(qb[(int64_t)(kvh * G + g) * p.q_stride_head + d])
+                     : 0.f;
+    }
+  }
+  float m[GMAX], l[GMAX], acc[GMAX][NI];
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) acc[g][i] = 0.f;
+  }
+
+  const T* kpool = reinterpret_cast<const T*>(p.k_pool);
+  const T* vpool = reinterpret_cast<const T*>(p.v_pool);
+  const int32_t* table = p.tables + (int64_t)b * p.table_stride;
+  for (int t = t0 + warp; t < t1; t += kGenericWarps) {
+    const int j = t / p.block_size;
+    const int off = t - j * p.block_size;
+    int32_t phys = -1;
+    if (j < p.table_width) phys = table[j];
+    if (phys < 0 || phys >= p.num_blocks) {
+      if (lane == 0) flag_error(p.err, j < p.table_width ? SNAPMIND_DEVERR_BLOCK_ID : SNAPMIND_DEVERR_TABLE);
+      continue;
+    }
+    const int64_t row = (((int64_t)phys * p.n_kv_heads + kvh) * p.block_size + off) * D;
+    float kf[NI], vf[NI];
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int d = lane + 32 * i;
+      kf[i] = d < D ? Conv<T>::to_f(kpool[row + d]) : 0.f;
+      vf[i] = d < D ? Conv<T>::to_f(vpool[row + d]) : 0.f;
+    }
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      if (g >= G) break;
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < NI; ++i) dot = fmaf(qr[g][i], kf[i], dot);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      const float sc = dot * p.scale;
+      const float m_new = fmaxf(m[g], sc);
+      const float corr = expf(m[g] - m_new);
+      const float pe = expf(sc - m_new);
+      l[g] = l[g] * corr + pe;
+#pragma unroll
+      for (int i = 0; i < NI; ++i) acc[g][i] = fmaf(pe, vf[i], acc[g][i] * corr);
+      m[g] = m_new;
+    }
+  }
+
+  // ---- merge the warps of this CTA ------------------------------------------
+  extern __shared__ float sm[];
+  float* sm_m = sm;                                   // [warps][GMAX]
+  float* sm_l = sm + kGenericWarps * GMAX;            // [warps][GMAX]
+  float* sm_acc = sm + 2 * kGenericWarps * GMAX;      // [warps][GMAX][D]
+  __shared__ int s_last;
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      sm_m[warp * GMAX + g] = m[g];
+      sm_l[warp * GMAX + g] = l[g];
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int d = lane + 32 * i;
+      if (g < G && d < D) sm_acc[(warp * GMAX + g) * D + d] = acc[g][i];
+    }
+  }
+  __syncthreads();
+
+  const bool direct = (n_splits == 1);
+  float* part_base = p.partials + ((int64_t)b * p.n_q_heads + kvh * G) * p.max_splits * (D + 2);
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int g = e / D, d = e - g * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kGenericWarps; ++w) M = fmaxf(M, sm_m[w * GMAX + g]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGenericWarps; ++w) {
+      const float mw = sm_m[w * GMAX + g];
+      const float f = (mw == -INFINITY) ? 0.f : expf(mw - M);
+      L += sm_l[w * GMAX + g] * f;
+      A += sm_acc[(w * GMAX + g) * D + d] * f;
+    }
+    if (direct) {
+      T* o = reinterpret_cast<T*>(p.out) + (int64_t)b * p.out_stride_seq +
+             (int64_t)(kvh * G + g) * p.out_stride_head;
+      o[d] = Conv<T>::from_f(A / L);
+    } else {
+      float* part = part_base + ((int64_t)g * p.max_splits + s) * (D + 2);
+      part[2 + d] = A;
+      if (d == 0) {
+        part[0] = M;
+        part[1] = L;
+      }
+    }
+  }
+  if (direct) return;
+
+  // ---- last-ticket merge of the split partials --------------------------------
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int ticket = atomicAdd(&p.counters[b * p.n_kv_heads + kvh], 1);
+    s_last = (ticket == n_splits - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  combine_splits<T>(p, b, kvh, n_splits, sm);
+  if (threadIdx.x == 0) p.counters[b * p.n_kv_heads + kvh] = 0;
+}
+
+template <typename T, int NI>
+static int launch_generic_g(const DecodeParams& p, dim3 grid, cudaStream_t st) {
+  const size_t smem_base = sizeof(float) * 2 * kGenericWarps;
+  auto go = [&](auto kernel, int gmax) -> int {
+    size_t smem = smem_base * gmax + sizeof(float) * kGenericWarps * gmax * p.head_dim;
+    const size_t comb = combine_smem_bytes(p);
+    if (comb > smem) smem = comb;
+    if (smem > 48 * 1024) {
+      cudaError_t e =
+          cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return cuda_status(e, "paged_decode smem attribute");
+    }
+    kernel<<<grid, kGenericWarps * 32, smem, st>>>(p);
+    return cuda_status(cudaGetLastError(), "paged_decode_generic launch");
+  };
+  if (p.group <= 1) return go(paged_decode_generic_kernel<T, NI, 1>, 1);
+  if (p.group <= 2) return go(paged_decode_generic_kernel<T, NI, 2>, 2);
+  if (p.group <= 4) return go(paged_decode_generic_kernel<T, NI, 4>, 4);
+  if (p.group <= 8) return go(paged_decode_generic_kernel<T, NI, 8>, 8);
+  if (NI <= 4 && p.group <= 16) return go(paged_decode_generic_kernel<T, NI, 16>, 16);
+  set_last_error("paged_decode: group size %d with head_dim %d unsupported", p.group, p.head_dim);
+  return SNAPMIND_ERR_UNSUPPORTED;
+}
+
+template <typename T>
+static int launch_generic(const DecodeParams& p, dim3 grid, cudaStream_t st) {
+  if (p.head_dim <= 32) return launch_generic_g<T, 1>(p, grid, st);
+  if (p.head_dim <= 64) return launch_generic_g<T, 2>(p, grid, st);
+  if (p.head_dim <= 128) return launch_generic_g<T, 4>(p, grid, st);
+  return launch_generic_g<T, 8>(p, grid, st);
+}
+
+}  // namespace snapmind
+
+using namespace snapmind;
+
+extern "C" {
+
+int32_t snapmind_paged_gqa_decode_split_tokens(int32_t batch, int32_t n_kv_heads,
+                                               int32_t max_seq_len, int32_t block_size) {
+  return default_split_tokens(batch, n_kv_heads, max_seq_len, block_size);
+}
+
+int64_t snapmind_paged_gqa_decode_workspace_bytes(int32_t batch, int32_t n_q_heads,
+                                                  int32_t n_kv_heads, int32_t head_dim,
+                                                  int32_t max_seq_len, int32_t split_tokens) {
+  if (batch <= 0 || n_q_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || split_tokens <= 0)
+    return 0;
+  const int64_t max_splits = ((int64_t)(max_seq_len > 0 ? max_seq_len : 1) + split_tokens - 1) / split_tokens;
+  return workspace_layout(batch, n_q_heads, n_kv_heads, head_dim, (int)max_splits).total;
+}
+
+int snapmind_paged_gqa_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
+                              const void* k_pool, const void* v_pool, int dtype,
+                              const int32_t* block_tables, int64_t table_stride_seq,
+                              int32_t table_width, const int32_t* seq_lens, void* out,
+                              int64_t out_stride_seq, int64_t out_stride_head, float scale,
+                              int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
+                              int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                              int32_t max_seq_len, int32_t split_tokens, int32_t flags,
+                              void* workspace, int64_t workspace_bytes, int32_t* err_word,
+                              void* stream) {
+  SNAPMIND_CHECK_ARG(dtype_size(dtype) > 0, "paged_decode: unknown dtype");
+  SNAPMIND_CHECK_ARG(batch >= 0 && n_q_heads > 0 && n_kv_heads > 0 && head_dim > 0 &&
+                         head_dim <= 256 && block_size > 0 && num_blocks > 0 && table_width >= 0,
+                     "paged_decode: bad sizes");
+  SNAPMIND_CHECK_ARG(n_q_heads % n_kv_heads == 0,
+                     "paged_decode: n_q_heads (%d) must be a multiple of n_kv_heads (%d)",
+                     n_q_heads, n_kv_heads);
+  if (batch == 0) return SNAPMIND_OK;
+  SNAPMIND_CHECK_ARG(q && k_pool && v_pool && block_tables && seq_lens && out,
+                     "paged_decode: null pointer");
+  if (max_seq_len <= 0) max_seq_len = table_width * block_size;
+  if (split_tokens <= 0)
+    split_tokens = default_split_tokens(batch, n_kv_heads, max_seq_len, block_size);
+  SNAPMIND_CHECK_ARG(split_tokens % block_size == 0,
+                     "paged_decode: split_tokens (%d) must be a multiple of block_size (%d)",
+                     split_tokens, block_size);
+  const int max_splits = (max_seq_len + split_tokens - 1) / split_tokens;
+  const WorkspaceLayout ws =
+      workspace_layout(batch, n_q_heads, n_kv_heads, head_dim, max_splits > 0 ? max_splits : 1);
+  SNAPMIND_CHECK_ARG(workspace != nullptr && workspace_bytes >= ws.total,
+                     "paged_decode: workspace needs %lld bytes, got %lld", (long long)ws.total,
+                     (long long)workspace_bytes);
+
+  DecodeParams p;
+  p.q = q;
+  p.q_stride_seq = q_stride_seq;
+  p.q_stride_head = q_stride_head;
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.tables = block_tables;
+  p.table_stride = table_stride_seq;
+  p.table_width = table_width;
+  p.seq_lens = seq_lens;
+  p.out = out;
+  p.out_stride_seq = out_stride_seq;
+  p.out_stride_head = out_stride_head;
+  p.scale = scale;
+  p.batch = batch;
+  p.n_q_heads = n_q_heads;
+  p.n_kv_heads = n_kv_heads;
+  p.group = n_q_heads / n_kv_heads;
+  p.head_dim = head_dim;
+  p.block_size = block_size;
+  p.num_blocks = num_blocks;
+  p.split_tokens = split_tokens;
+  p.max_splits = max_splits > 0 ? max_splits : 1;
+  p.counters = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + ws.counters_off);
+  p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + ws.partials_off);
+  p.err = err_word;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  if (!(flags & SNAPMIND_DECODE_FORCE_GENERIC)) {
+    int rc = SNAPMIND_ERR_UNSUPPORTED;
+    if (decode_fast_supported(p, dtype)) rc = launch_decode_fast(p, dtype, st);
+    if (rc != SNAPMIND_ERR_UNSUPPORTED) return rc;
+  }
+  dim3 grid(p.max_splits, n_kv_heads, batch);
+  SNAPMIND_CHECK_ARG(grid.y <= 65535 && grid.z <= 65535, "paged_decode: grid too large");
+  switch (dtype) {
+    case SNAPMIND_DTYPE_F32: return launch_generic<float>(p, grid, st);
+    case SNAPMIND_DTYPE_BF16: return launch_generic<__nv_bfloat16>(p, grid, st);
+    default: return launch_generic<__half>(p, grid, st);
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,106 @@
+// Shared declarations of the paged GQA decode kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace snapmind {
+
+struct DecodeParams {
+  const void* q;
+  int64_t q_stride_seq, q_stride_head;  // elements
+  const void* k_pool;
+  const void* v_pool;
+  const int32_t* tables;
+  int64_t table_stride;
+  int32_t table_width;
+  const int32_t* seq_lens;
+  void* out;
+  int64_t out_stride_seq, out_stride_head;  // elements
+  float scale;
+  int32_t batch, n_q_heads, n_kv_heads, group, head_dim, block_size, num_blocks;
+  int32_t split_tokens, max_splits;
+  int32_t* counters;  // [batch][n_kv_heads] tickets, zero between calls
+  float* partials;    // [batch][n_q_heads][max_splits][head_dim + 2]: m, l, acc[head_dim]
+  int32_t* err;
+};
+
+struct WorkspaceLayout {
+  int64_t counters_off, partials_off, total;
+};
+
+inline WorkspaceLayout workspace_layout(int batch, int n_q_heads, int n_kv_heads, int head_dim,
+                                        int max_splits) {
+  WorkspaceLayout w;
+  w.counters_off = 0;
+  const int64_t counters = (int64_t)batch * n_kv_heads * sizeof(int32_t);
+  w.partials_off = (counters + 255) / 256 * 256;
+  w.total = w.partials_off +
+            (int64_t)batch * n_q_heads * max_splits * (head_dim + 2) * (int64_t)sizeof(float);
+  return w;
+}
+
+// Tokens per split: about 16 CTAs per SM over the batch at a mean length of
+// max_seq_len / 2, rounded to whole 64-token tiles (and whole blocks).
+inline int default_split_tokens(int batch, int n_kv_heads, int max_seq_len, int block_size) {
+  if (block_size <= 0) return 0;
+  const int64_t work = (int64_t)(batch > 0 ? batch : 1) * (n_kv_heads > 0 ? n_kv_heads : 1) *
+                       (max_seq_len > 0 ? max_seq_len : 1) / 2;
+  const int64_t target = (int64_t)num_sms() * 16;
+  int64_t split = (work + target - 1) / target;
+  if (split < 256) split = 256;
+  if (split > 8192) split = 8192;
+  int64_t unit = block_size;
+  if (64 % block_size == 0) unit = 64;
+  split = (split + unit - 1) / unit * unit;
+  return (int)split;
+}
+
+inline size_t combine_smem_bytes(const DecodeParams& p) { return sizeof(float) * 2 * p.group; }
+
+// Merge the per-split (m, l, acc) partial states of (b, kv head) into the
+// output: M = max m_s, L = sum l_s e^(m_s - M), out = sum acc_s e^(m_s - M) / L.
+// Partials written by other CTAs are read with L1-bypassing loads.
+template <typename T>
+__device__ void combine_splits(const DecodeParams& p, int b, int kvh, int n_splits, float* sm) {
+  const int G = p.group, D = p.head_dim;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  float* s_M = sm;
+  float* s_L = sm + G;
+  const int64_t pstride = D + 2;
+  const float* base = p.partials + ((int64_t)b * p.n_q_heads + kvh * G) * p.max_splits * pstride;
+  __syncthreads();
+  for (int g = warp; g < G; g += nw) {
+    const float* pg = base + (int64_t)g * p.max_splits * pstride;
+    float M = -INFINITY;
+    for (int s = lane; s < n_splits; s += 32) M = fmaxf(M, __ldcg(pg + s * pstride));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.f;
+    for (int s = lane; s < n_splits; s += 32)
+      L += __ldcg(pg + s * pstride + 1) * expf(__ldcg(pg + s * pstride) - M);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane == 0) {
+      s_M[g] = M;
+      s_L[g] = L;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int g = e / D, d = e - g * D;
+    const float* pg = base + (int64_t)g * p.max_splits * pstride;
+    const float M = s_M[g];
+    float A = 0.f;
+    for (int s = 0; s < n_splits; ++s)
+      A += __ldcg(pg + s * pstride + 2 + d) * expf(__ldcg(pg + s * pstride) - M);
+    T* o = reinterpret_cast<T*>(p.out) + (int64_t)b * p.out_stride_seq +
+           (int64_t)(kvh * G + g) * p.out_stride_head;
+    o[d] = Conv<T>::from_f(A / s_L[g]);
+  }
+}
+
+// Tensor-core path (paged_decode_fast.cu).
+bool decode_fast_supported(const DecodeParams& p, int dtype);
+int launch_decode_fast(const DecodeParams& p, int dtype, cudaStream_t stream);
+
+}  // namespace snapmind

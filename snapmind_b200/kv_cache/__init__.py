@@ -1,0 +1,5 @@
+"""B200 KV-cache plugins; importing this package registers them in ``KV_CACHE``."""
+from snapmind_b200.kv_cache.base import KVCacheABC
+from snapmind_b200.kv_cache.paged import PagedKVCache
+
+__all__ = ["KVCacheABC", "PagedKVCache"]

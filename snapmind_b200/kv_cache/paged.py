@@ -1,0 +1,279 @@
+"""PagedKVCache on the B200: device block pool, host block bookkeeping.
+
+Drop-in for ``snapmind.kv_cache.paged.PagedKVCache`` (snapmind/kv_cache/paged.py:9-145),
+registered under the same key ``"paged"`` in this package's ``KV_CACHE``.
+
+What stays on the host (bookkeeping, exactly as the reference does it, so block
+tables are bit-identical): the free-block ``set`` and its ``pop()`` order, the
+per-layer block-table lists sharing that one set, the per-layer slot counts,
+and the evict plan.  What runs on the GPU (hand-written sm_100a kernels through
+the C ABI): every byte of K/V — the append of ``store``, the tile gather of
+``fetch``/``layer_dicts`` and the compaction copy of ``evict``.
+
+Differences a caller can see: the pool and the tensors ``fetch`` returns live on
+the CUDA device; the pool dtype is ``dtype`` (default float32, the reference's
+default).  Device block tables are mirrored in an int32 tensor updated when a
+table grows.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from snapmind_b200 import _lib
+from snapmind_b200.kv_cache.base import KVCacheABC
+from snapmind_b200.registry import KV_CACHE
+
+_KERNEL_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
+
+
+def _default_device() -> torch.device:
+    if not torch.cuda.is_available():
+        raise RuntimeError("snapmind_b200 PagedKVCache needs a CUDA device")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+@KV_CACHE.register("paged")
+class PagedKVCache(KVCacheABC):
+    def __init__(
+        self,
+        max_seq_len: int,
+        n_layers: int,
+        n_heads: int,
+        head_dim: int,
+        block_size: int = 16,
+        max_blocks: int | None = None,
+        *,
+        dtype: torch.dtype = torch.float32,
+        device: torch.device | str | None = None,
+    ):
+        self.n_layers = n_layers
+        self.n_heads = n_heads
+        self.head_dim = head_dim
+        self.block_size = block_size
+        # snapmind/kv_cache/paged.py:24-25
+        max_blocks = max_blocks or (max_seq_len + block_size - 1) // block_size
+        self.max_blocks = max_blocks
+        self.dtype = dtype
+        self.device = torch.device(device) if device is not None else _default_device()
+        _lib.require_cuda(self.device)
+        _lib.dtype_code(dtype)
+        _lib.load()
+
+        # pool[block][head][slot][dim]: a (block, head) tile is contiguous
+        shape = (max_blocks, n_heads, block_size, head_dim)
+        self._k_buffer = torch.zeros(shape, dtype=dtype, device=self.device)
+        self._v_buffer = torch.zeros(shape, dtype=dtype, device=self.device)
+        self._free_blocks = set(range(max_blocks))
+        self._block_tables: list[list[int]] = [[] for _ in range(n_layers)]
+        self._slot_counts: list[int] = [0] * n_layers
+        self._tables_dev = torch.zeros((n_layers, max_blocks), dtype=torch.int32, device=self.device)
+        self._err = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    # ------------------------------------------------------------------ helpers
+    def _stream(self) -> int:
+        return _lib.stream_handle(self.device)
+
+    def _sync_table(self, layer_idx: int, old_len: int) -> None:
+        bt = self._block_tables[layer_idx]
+        if len(bt) > old_len:
+            new = torch.tensor(bt[old_len:], dtype=torch.int32)
+            self._tables_dev[layer_idx, old_len : len(bt)].copy_(new, non_blocking=False)
+
+    def _as_input(self, t: torch.Tensor) -> torch.Tensor:
+        if t.device != self.device:
+            t = t.to(self.device)
+        if t.dtype not in _KERNEL_DTYPES:
+            t = t.to(self.dtype)
+        if t.stride(-1) != 1:
+            t = t.contiguous()
+        return t
+
+    def check_device_errors(self) -> None:
+        """Synchronise and raise if any kernel of this cache flagged an error."""
+        word = int(self._err.item())
+        if word:
+            self._err.zero_()
+            _lib.raise_device_error(word, "PagedKVCache")
+
+    # --------------------------------------------------------------------- API
+    def store(self, layer_idx: int, key: torch.Tensor, value: torch.Tensor, seq_pos: int) -> None:
+        """Append ``key[0, :, t, :]`` / ``value[0, :, t, :]`` for every t.
+
+        Mirrors snapmind/kv_cache/paged.py:34-54: ``seq_pos`` is ignored, tokens
+        go to the next free slots of the layer, blocks come from ``set.pop()``;
+        on exhaustion the tokens that already had a block are written, the
+        blocks taken so far stay in the table, the slot count is unchanged and
+        ``RuntimeError("PagedKVCache: out of blocks")`` is raised.
+        """
+        num_tokens = key.shape[-2]
+        slot_start = self._slot_counts[layer_idx]
+        bt = self._block_tables[layer_idx]
+        old_len = len(bt)
+        failed = False
+        if num_tokens > 0:
+            last_block = (slot_start + num_tokens - 1) // self.block_size
+            while len(bt) <= last_block:
+                if not self._free_blocks:
+                    failed = True
+                    break
+                bt.append(self._free_blocks.pop())
+        writable = min(num_tokens, max(0, len(bt) * self.block_size - slot_start))
+        self._sync_table(layer_idx, old_len)
+        if writable > 0:
+            if key.shape[1] != self.n_heads or key.shape[-1] != self.head_dim:
+                raise RuntimeError(
+                    f"PagedKVCache.store: expected (1, {self.n_heads}, T, {self.head_dim}) rows, "
+                    f"got {tuple(key.shape)}"
+                )
+            k = self._as_input(key[0])  # (H, T, D)
+            v = self._as_input(value[0])
+            if v.stride() != k.stride() or v.dtype != k.dtype:
+                k, v = k.contiguous(), v.to(k.dtype).contiguous()
+            status = _lib.load().snapmind_kv_append(
+                self._k_buffer.data_ptr(), self._v_buffer.data_ptr(), _lib.dtype_code(self.dtype), 0,
+                k.data_ptr(), v.data_ptr(), _lib.dtype_code(k.dtype),
+                0, 0, k.stride(0), k.stride(1),
+                self._tables_dev[layer_idx].data_ptr(), 0, 0, self.max_blocks,
+                None, slot_start,
+                1, 1, writable, self.n_heads, self.head_dim, self.block_size, self.max_blocks,
+                self._err.data_ptr(), self._stream(),
+            )  # fmt: skip
+            _lib.check(status, "PagedKVCache.store")
+        if failed:
+            raise RuntimeError(_lib.OUT_OF_BLOCKS_MSG)
+        self._slot_counts[layer_idx] = slot_start + num_tokens
+
+    def fetch(self, layer_idx: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Return ``(k, v)`` of shape ``(1, H, T, D)`` (snapmind/kv_cache/paged.py:56-78).
+
+        An empty table returns two ``(0, H, D)`` tensors, as the reference does.
+        """
+        bt = self._block_tables[layer_idx]
+        if not bt:
+            return (
+                torch.empty(0, self.n_heads, self.head_dim, dtype=self.dtype, device=self.device),
+                torch.empty(0, self.n_heads, self.head_dim, dtype=self.dtype, device=self.device),
+            )
+        num_slots = self._slot_counts[layer_idx]
+        if num_slots == 0:
+            # the reference concatenates an empty list here
+            raise RuntimeError("torch.cat(): expected a non-empty list of Tensors")
+        k = torch.empty((1, self.n_heads, num_slots, self.head_dim), dtype=self.dtype, device=self.device)
+        v = torch.empty_like(k)
+        status = _lib.load().snapmind_kv_gather(
+            self._k_buffer.data_ptr(), self._v_buffer.data_ptr(), _lib.dtype_code(self.dtype), 0,
+            k.data_ptr(), v.data_ptr(), 0, k.numel(),
+            self._tables_dev[layer_idx].data_ptr(), 0, 0, self.max_blocks,
+            None, num_slots,
+            1, 1, self.n_heads, self.head_dim, self.block_size, self.max_blocks,
+            self._err.data_ptr(), self._stream(),
+        )  # fmt: skip
+        _lib.check(status, "PagedKVCache.fetch")
+        return k, v
+
+    def _copy_rows(self, rows: list[tuple[int, int, int, int]]) -> None:
+        """Device copy of (src_block, src_row, dst_block, dst_row) rows, in
+        ascending chunks of at most 64 rows, each chunk read before written."""
+        lib = _lib.load()
+        arr = ctypes.c_int32 * 64
+        for c in range(0, len(rows), 64):
+            chunk = rows[c : c + 64]
+            sb, sr, db, dr = (arr(*[r[i] for r in chunk]) for i in range(4))
+            status = lib.snapmind_kv_copy_slots(
+                self._k_buffer.data_ptr(), self._v_buffer.data_ptr(), _lib.dtype_code(self.dtype),
+                sb, sr, db, dr, len(chunk), self.n_heads, self.head_dim, self.block_size,
+                self.max_blocks, self._err.data_ptr(), self._stream(),
+            )  # fmt: skip
+            _lib.check(status, "PagedKVCache.evict")
+
+    def evict(self, tokens_to_keep: int) -> None:
+        """Keep the newest ``tokens_to_keep`` tokens per layer.
+
+        Mirrors snapmind/kv_cache/paged.py:80-116 step by step, including its
+        limits: when the start is not block aligned the kept tokens are packed
+        into the first kept block, which the reference can only do when they fit
+        in it — otherwise its slice assignment raises ``RuntimeError`` after the
+        freed blocks were returned and the earlier packing steps were written;
+        this implementation reproduces that state and raises the same type.
+        """
+        bs = self.block_size
+        for layer_idx in range(self.n_layers):
+            total = self._slot_counts[layer_idx]
+            if total <= tokens_to_keep:
+                continue
+            start_slot = total - tokens_to_keep
+            start_block = start_slot // bs
+            offset_in_block = start_slot % bs
+            bt = self._block_tables[layer_idx]
+            blocks_needed = (offset_in_block + tokens_to_keep + bs - 1) // bs
+            kept_blocks = bt[start_block : start_block + blocks_needed]
+            freed_blocks = bt[:start_block] + bt[start_block + blocks_needed :]
+            for b in freed_blocks:
+                self._free_blocks.add(b)
+
+            if offset_in_block > 0 and kept_blocks:
+                first = kept_blocks[0]
+                remaining = tokens_to_keep
+                src_off = offset_in_block
+                dst_off = 0
+                rows: list[tuple[int, int, int, int]] = []
+                error: str | None = None
+                for b in kept_blocks:
+                    take = min(bs - src_off, remaining)
+                    dst_len = max(0, min(bs, dst_off + take) - min(bs, dst_off))
+                    if dst_len != take:
+                        error = (
+                            f"The expanded size of the tensor ({dst_len}) must match the existing "
+                            f"size ({take}) at non-singleton dimension 0."
+                        )
+                        break
+                    rows.extend((b, src_off + i, first, dst_off + i) for i in range(take))
+                    dst_off += take
+                    remaining -= take
+                    src_off = 0
+                self._copy_rows(rows)
+                if error is not None:
+                    raise RuntimeError(error)
+                needed = (dst_off + bs - 1) // bs
+                for b in kept_blocks[needed:]:
+                    self._free_blocks.add(b)
+                kept_blocks = kept_blocks[:needed]
+
+            self._block_tables[layer_idx] = kept_blocks
+            if kept_blocks:
+                self._tables_dev[layer_idx, : len(kept_blocks)].copy_(
+                    torch.tensor(kept_blocks, dtype=torch.int32)
+                )
+            self._slot_counts[layer_idx] = tokens_to_keep
+
+    def reset(self) -> None:
+        self._k_buffer.zero_()
+        self._v_buffer.zero_()
+        self._free_blocks = set(range(self.max_blocks))
+        self._block_tables = [[] for _ in range(self.n_layers)]
+        self._slot_counts = [0] * self.n_layers
+        self._tables_dev.zero_()
+
+    def memory_usage(self) -> dict:
+        total_bytes = self._k_buffer.numel() * self._k_buffer.element_size()
+        total_bytes += self._v_buffer.numel() * self._v_buffer.element_size()
+        return {
+            "num_tokens": sum(self._slot_counts),
+            "total_bytes": total_bytes,
+            "used_blocks": sum(len(bt) for bt in self._block_tables),
+            "max_blocks": self.max_blocks,
+        }
+
+    def layer_dicts(self) -> dict[int, dict[str, torch.Tensor | None]]:
+        result: dict[int, dict[str, torch.Tensor | None]] = {}
+        for i in range(self.n_layers):
+            k, v = self.fetch(i)
+            result[i] = {"k": None, "v": None} if k.numel() == 0 else {"k": k, "v": v}
+        return result
+
+    # ------------------------------------------------------- introspection
+    def block_tables(self) -> list[list[int]]:
+        """Copy of the per-layer block tables (host lists)."""
+        return [list(bt) for bt in self._block_tables]

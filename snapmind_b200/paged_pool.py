@@ -1,0 +1,255 @@
+"""Many sequences on one paged KV pool — the batched form of PagedKVCache.
+
+The reference cache holds one sequence per instance (snapmind/kv_cache/paged.py:51-52
+reads ``key[0]`` only).  Serving many sequences needs the same slot arithmetic
+over one shared pool; this class is that extension, with all state on the GPU:
+
+* ``k``, ``v``: ``[layer][block][head][slot][dim]``; a block id is valid in every
+  layer, so one block table row per sequence serves all layers;
+* ``block_tables`` int32 ``[max_seqs][max_blocks_per_seq]``, ``seq_lens`` int32;
+* a device free stack (``free_stack``, ``free_top``) from which
+  ``snapmind_kv_reserve`` grows tables deterministically (ascending sequence
+  order, blocks from the top of the stack).
+
+Host mirrors of the lengths and the free count let the pool raise
+``RuntimeError("PagedKVCache: out of blocks")`` before launching, as the
+reference does, and size gather outputs without a device sync.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from snapmind_b200 import _lib
+
+
+class PagedKVPool:
+    def __init__(
+        self,
+        n_layers: int,
+        n_kv_heads: int,
+        head_dim: int,
+        num_blocks: int,
+        max_seqs: int,
+        max_blocks_per_seq: int,
+        block_size: int = 16,
+        dtype: torch.dtype = torch.bfloat16,
+        device: torch.device | str | None = None,
+    ):
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        _lib.require_cuda(self.device)
+        _lib.load()
+        self.n_layers, self.n_kv_heads, self.head_dim = n_layers, n_kv_heads, head_dim
+        self.num_blocks, self.max_seqs, self.block_size = num_blocks, max_seqs, block_size
+        self.max_blocks_per_seq = max_blocks_per_seq
+        self.dtype = dtype
+        self._dcode = _lib.dtype_code(dtype)
+        shape = (n_layers, num_blocks, n_kv_heads, block_size, head_dim)
+        self.k = torch.empty(shape, dtype=dtype, device=self.device)
+        self.v = torch.empty(shape, dtype=dtype, device=self.device)
+        self.layer_stride = num_blocks * n_kv_heads * block_size * head_dim
+        self.block_tables = torch.zeros((max_seqs, max_blocks_per_seq), dtype=torch.int32, device=self.device)
+        self.seq_lens = torch.zeros(max_seqs, dtype=torch.int32, device=self.device)
+        # free_stack[top-1] is popped first; initially block 0, then 1, ...
+        self.free_stack = torch.arange(num_blocks - 1, -1, -1, dtype=torch.int32, device=self.device)
+        self.free_top = torch.tensor([num_blocks], dtype=torch.int32, device=self.device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._host_lens = np.zeros(max_seqs, dtype=np.int64)
+        self._host_free = num_blocks
+        self._workspace: torch.Tensor | None = None
+        self._ws_key: tuple | None = None
+
+    # ------------------------------------------------------------------ state
+    def _stream(self) -> int:
+        return _lib.stream_handle(self.device)
+
+    def set_state(self, tables: np.ndarray, lens: np.ndarray, free_stack: np.ndarray) -> None:
+        """Install block tables, lengths and the free stack (e.g. a shuffled pool)."""
+        tables = np.asarray(tables)
+        b, w = tables.shape
+        if b > self.max_seqs or w > self.max_blocks_per_seq:
+            raise ValueError("tables larger than the pool's table capacity")
+        if tables.size and (tables.min() < 0 or tables.max() >= self.num_blocks):
+            raise ValueError("block id outside the pool")
+        full = np.zeros((self.max_seqs, self.max_blocks_per_seq), dtype=np.int32)
+        full[:b, :w] = tables
+        self.block_tables.copy_(torch.from_numpy(full))
+        lens_full = np.zeros(self.max_seqs, dtype=np.int32)
+        lens_full[: len(lens)] = lens
+        self.seq_lens.copy_(torch.from_numpy(lens_full))
+        self._host_lens = lens_full.astype(np.int64)
+        fs = np.zeros(self.num_blocks, dtype=np.int32)
+        fs[: len(free_stack)] = free_stack
+        self.free_stack.copy_(torch.from_numpy(fs))
+        self.free_top.fill_(len(free_stack))
+        self._host_free = len(free_stack)
+
+    @property
+    def host_lens(self) -> np.ndarray:
+        return self._host_lens
+
+    def check(self) -> None:
+        """Synchronise and raise if a kernel flagged an error on this pool."""
+        word = int(self.err.item())
+        if word:
+            self.err.zero_()
+            _lib.raise_device_error(word, "PagedKVPool")
+
+    # -------------------------------------------------------------- mutation
+    def reserve(self, n_new: int = 1, batch: int | None = None) -> None:
+        """Grow the first ``batch`` sequences by ``n_new`` tokens (tables + lengths)."""
+        batch = self.max_seqs if batch is None else batch
+        bs = self.block_size
+        lens = self._host_lens[:batch]
+        need = int(((lens + n_new + bs - 1) // bs - (lens + bs - 1) // bs).sum())
+        if need > self._host_free:
+            raise RuntimeError(_lib.OUT_OF_BLOCKS_MSG)
+        if batch and int(((lens + n_new + bs - 1) // bs).max()) > self.max_blocks_per_seq:
+            raise ValueError("sequence would outgrow its block table row")
+        status = _lib.load().snapmind_kv_reserve(
+            self.block_tables.data_ptr(), self.max_blocks_per_seq, self.max_blocks_per_seq,
+            self.seq_lens.data_ptr(), batch, n_new, bs,
+            self.free_stack.data_ptr(), self.free_top.data_ptr(), self.num_blocks,
+            self.err.data_ptr(), self._stream(),
+        )  # fmt: skip
+        _lib.check(status, "PagedKVPool.reserve")
+        self._host_lens[:batch] += n_new
+        self._host_free -= need
+
+    def release(self, seq_ids: list[int]) -> None:
+        """Return the blocks of finished sequences to the free stack."""
+        if not seq_ids:
+            return
+        if min(seq_ids) < 0 or max(seq_ids) >= self.max_seqs or len(set(seq_ids)) != len(seq_ids):
+            raise ValueError("release: sequence ids must be distinct and inside the pool")
+        ids = torch.tensor(seq_ids, dtype=torch.int32, device=self.device)
+        freed = int(sum((self._host_lens[s] + self.block_size - 1) // self.block_size for s in seq_ids))
+        status = _lib.load().snapmind_kv_release(
+            self.block_tables.data_ptr(), self.max_blocks_per_seq, self.max_blocks_per_seq,
+            self.seq_lens.data_ptr(), ids.data_ptr(), len(seq_ids), self.block_size,
+            self.free_stack.data_ptr(), self.free_top.data_ptr(), self.num_blocks,
+            self.err.data_ptr(), self._stream(),
+        )  # fmt: skip
+        _lib.check(status, "PagedKVPool.release")
+        for s in seq_ids:
+            self._host_lens[s] = 0
+        self._host_free += freed
+
+    def append(self, layer: int | None, k_new: torch.Tensor, v_new: torch.Tensor, slot_starts=None,
+               slot_start0: int | None = None) -> None:
+        """Write new tokens' K/V rows.
+
+        ``k_new``: ``[B, H, D]`` (one token, layer ``layer``), ``[B, H, T, D]``,
+        or ``[L, B, H, T, D]`` with ``layer=None`` (all layers at once).  By
+        default token t of sequence b goes to slot ``seq_lens[b] - T + t`` — the
+        slots that the last ``reserve(T)`` added.
+        """
+        if k_new.dim() == 3:
+            k_new, v_new = k_new.unsqueeze(2), v_new.unsqueeze(2)
+        if k_new.dim() == 4:
+            if layer is None:
+                raise ValueError("layer is required for [B, H, T, D] inputs")
+            k_new, v_new = k_new.unsqueeze(0), v_new.unsqueeze(0)
+            n_layers, base = 1, layer
+        else:
+            n_layers, base = k_new.shape[0], (0 if layer is None else layer)
+        if k_new.stride() != v_new.stride():
+            k_new, v_new = k_new.contiguous(), v_new.contiguous()
+        _, batch, n_heads, n_tokens, head_dim = k_new.shape
+        if n_heads != self.n_kv_heads or head_dim != self.head_dim:
+            raise ValueError(f"expected {self.n_kv_heads} heads of {self.head_dim}, got {tuple(k_new.shape)}")
+        if slot_starts is None:
+            starts_ptr, start0 = self.seq_lens.data_ptr(), -n_tokens
+        else:
+            starts_ptr = None if isinstance(slot_starts, int) else slot_starts.data_ptr()
+            start0 = slot_starts if isinstance(slot_starts, int) else 0
+        if slot_start0 is not None:
+            start0 = slot_start0
+        st = k_new.stride()
+        status = _lib.load().snapmind_kv_append(
+            self.k[base].data_ptr(), self.v[base].data_ptr(), self._dcode, self.layer_stride,
+            k_new.data_ptr(), v_new.data_ptr(), _lib.dtype_code(k_new.dtype),
+            st[0], st[1], st[2], st[3],
+            self.block_tables.data_ptr(), self.max_blocks_per_seq, 0, self.max_blocks_per_seq,
+            starts_ptr, start0,
+            n_layers, batch, n_tokens, n_heads, head_dim, self.block_size, self.num_blocks,
+            self.err.data_ptr(), self._stream(),
+        )  # fmt: skip
+        _lib.check(status, "PagedKVPool.append")
+
+    # ----------------------------------------------------------------- reads
+    def gather(self, batch: int | None = None, layers: range | None = None, out=None):
+        """Packed K/V of the first ``batch`` sequences.
+
+        Returns ``(k, v)`` of shape ``[n_layers, total_tokens * H * D]`` where the
+        row of each layer is the concatenation over b of ``(H, len_b, D)`` — for
+        one sequence the tensor ``PagedKVCache.fetch`` returns.
+        """
+        batch = self.max_seqs if batch is None else batch
+        layers = range(self.n_layers) if layers is None else layers
+        total = int(self._host_lens[:batch].sum())
+        per_layer = total * self.n_kv_heads * self.head_dim
+        if out is None:
+            k_out = torch.empty((len(layers), per_layer), dtype=self.dtype, device=self.device)
+            v_out = torch.empty_like(k_out)
+        else:
+            k_out, v_out = out
+            for t in (k_out, v_out):
+                if t.dtype != self.dtype or t.shape[0] < len(layers) or t[0].numel() < per_layer or not t.is_contiguous():
+                    raise ValueError("gather output too small or not contiguous")
+        if per_layer == 0 or len(layers) == 0:
+            return k_out, v_out
+        status = _lib.load().snapmind_kv_gather(
+            self.k[layers.start].data_ptr(), self.v[layers.start].data_ptr(), self._dcode, self.layer_stride,
+            k_out.data_ptr(), v_out.data_ptr(), per_layer, per_layer,
+            self.block_tables.data_ptr(), self.max_blocks_per_seq, 0, self.max_blocks_per_seq,
+            self.seq_lens.data_ptr(), 0,
+            len(layers), batch, self.n_kv_heads, self.head_dim, self.block_size, self.num_blocks,
+            self.err.data_ptr(), self._stream(),
+        )  # fmt: skip
+        _lib.check(status, "PagedKVPool.gather")
+        return k_out, v_out
+
+    def _decode_workspace(self, batch, n_q_heads, max_len, split):
+        lib = _lib.load()
+        need = lib.snapmind_paged_gqa_decode_workspace_bytes(
+            batch, n_q_heads, self.n_kv_heads, self.head_dim, max_len, split
+        )
+        if self._workspace is None or self._workspace.numel() < need:
+            # zero-filled once; the kernel leaves its tickets at zero
+            self._workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+        return self._workspace
+
+    def decode(self, layer: int, q: torch.Tensor, out: torch.Tensor | None = None, scale: float | None = None,
+               batch: int | None = None, split_tokens: int = 0, force_generic: bool = False,
+               max_seq_len: int | None = None) -> torch.Tensor:
+        """Paged GQA decode attention of ``q`` ``[B, Hq, D]`` against layer ``layer``."""
+        batch = q.shape[0] if batch is None else batch
+        n_q = q.shape[1]
+        if q.dtype != self.dtype:
+            raise TypeError(f"q dtype {q.dtype} != pool dtype {self.dtype}")
+        if q.stride(-1) != 1:
+            q = q.contiguous()
+        if out is None:
+            out = torch.empty((batch, n_q, self.head_dim), dtype=self.dtype, device=self.device)
+        scale = self.head_dim ** -0.5 if scale is None else scale
+        if max_seq_len is None:
+            max_seq_len = max(1, int(self._host_lens[:batch].max())) if batch else 1
+        max_len = max_seq_len
+        lib = _lib.load()
+        split = split_tokens or lib.snapmind_paged_gqa_decode_split_tokens(
+            batch, self.n_kv_heads, max_len, self.block_size
+        )
+        ws = self._decode_workspace(batch, n_q, max_len, split)
+        status = lib.snapmind_paged_gqa_decode(
+            q.data_ptr(), q.stride(0), q.stride(1),
+            self.k[layer].data_ptr(), self.v[layer].data_ptr(), self._dcode,
+            self.block_tables.data_ptr(), self.max_blocks_per_seq, self.max_blocks_per_seq,
+            self.seq_lens.data_ptr(),
+            out.data_ptr(), out.stride(0), out.stride(1),
+            float(scale), batch, n_q, self.n_kv_heads, self.head_dim, self.block_size, self.num_blocks,
+            max_len, split, _lib.DECODE_FORCE_GENERIC if force_generic else 0,
+            ws.data_ptr(), ws.numel(), self.err.data_ptr(), self._stream(),
+        )  # fmt: skip
+        _lib.check(status, "PagedKVPool.decode")
+        return out

@@ -1,0 +1,308 @@
+"""Generate golden vectors by running the reference snapmind code itself.
+
+Usage (in a checkout where the reference is importable):
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --reference /path/to/snapmind
+
+Writes, next to this script:
+  * paged_ops.json      — scripted store/fetch/evict/reset/memory_usage/layer_dicts
+                          sequences on the reference ``PagedKVCache``: block
+                          tables, slot counts, free sets, errors and sha256 of
+                          every fetched tensor after each step;
+  * paged_batched.json  — many sequences on one shuffled shared pool: each
+                          (sequence, layer) is a reference ``PagedKVCache`` with
+                          the given block table, prefilled then appended one
+                          token; sha256 of the fetched K/V;
+  * gqa_decode.npz / gqa_decode.json — the reference ``GroupedQueryAttention``
+                          forward for one decode token over a ``PagedKVCache``
+                          (q/k/v projections saved, out_proj set to identity so
+                          the output is the attention result itself).
+
+Inputs are regenerated from seeds with ``inputs.randn`` (frozen RandomState
+stream), so the fixtures hold seeds, small tensors and digests only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+from inputs import digest, randn  # noqa: E402
+
+
+def _bf16_bits(t):
+    import torch
+
+    return t.to(torch.bfloat16).contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _fetch_record(k, v):
+    import torch
+
+    rec = {"shape": list(k.shape), "dtype": str(k.dtype).replace("torch.", "")}
+    rec["k_sha_f32"] = digest(k.to(torch.float32).numpy())
+    rec["v_sha_f32"] = digest(v.to(torch.float32).numpy())
+    rec["k_sha_bf16"] = digest(_bf16_bits(k))
+    rec["v_sha_bf16"] = digest(_bf16_bits(v))
+    return rec
+
+
+def run_paged_scenario(cfg, ops):
+    import torch
+    from snapmind.kv_cache.paged import PagedKVCache
+
+    cache = PagedKVCache(**cfg)
+    H, D = cfg["n_heads"], cfg["head_dim"]
+    records = []
+    for op in ops:
+        rec: dict = {}
+        try:
+            kind = op["op"]
+            if kind == "store":
+                k = torch.from_numpy(randn(op["seed"], (1, H, op["T"], D)))
+                v = torch.from_numpy(randn(op["seed"] + 1000, (1, H, op["T"], D)))
+                if op.get("dtype") == "bf16":
+                    k, v = k.to(torch.bfloat16), v.to(torch.bfloat16)
+                cache.store(op["layer"], k, v, op.get("seq_pos", 0))
+            elif kind == "fetch":
+                k, v = cache.fetch(op["layer"])
+                rec["fetch"] = _fetch_record(k, v)
+            elif kind == "evict":
+                cache.evict(op["keep"])
+            elif kind == "reset":
+                cache.reset()
+            elif kind == "memory_usage":
+                rec["usage"] = cache.memory_usage()
+            elif kind == "layer_dicts":
+                d = cache.layer_dicts()
+                rec["layers"] = {
+                    str(i): (None if e["k"] is None else _fetch_record(e["k"], e["v"])) for i, e in d.items()
+                }
+            else:
+                raise ValueError(kind)
+            rec["error"] = None
+        except Exception as e:  # the reference's own error behaviour is part of the fixture
+            rec["error"] = [type(e).__name__, str(e)]
+        rec["tables"] = [list(map(int, bt)) for bt in cache._block_tables]
+        rec["slot_counts"] = list(map(int, cache._slot_counts))
+        rec["free"] = sorted(map(int, cache._free_blocks))
+        records.append({"op": op, "expect": rec})
+    return records
+
+
+PAGED_SCENARIOS = [
+    {
+        # the fixture of snapmind/tests/kv_cache/test_paged.py:5-9, scripted
+        "name": "test_paged_fixture",
+        "config": {"max_seq_len": 128, "n_layers": 2, "n_heads": 4, "head_dim": 64, "block_size": 16},
+        "ops": [
+            {"op": "fetch", "layer": 0},
+            {"op": "store", "layer": 0, "T": 10, "seed": 1},
+            {"op": "store", "layer": 1, "T": 7, "seed": 2},
+            {"op": "fetch", "layer": 0},
+            {"op": "fetch", "layer": 1},
+            {"op": "store", "layer": 0, "T": 20, "seed": 3, "seq_pos": 10},
+            {"op": "fetch", "layer": 0},
+            {"op": "memory_usage"},
+            {"op": "evict", "keep": 5},
+            {"op": "fetch", "layer": 0},
+            {"op": "fetch", "layer": 1},
+            {"op": "store", "layer": 1, "T": 40, "seed": 4},
+            {"op": "fetch", "layer": 1},
+            {"op": "memory_usage"},
+            # multi-block non-aligned compaction: the reference raises mid-way
+            {"op": "evict", "keep": 20},
+            {"op": "fetch", "layer": 1},
+            # reuses a block that evict returned while layer 1 still lists it
+            {"op": "store", "layer": 0, "T": 60, "seed": 5},
+            {"op": "fetch", "layer": 0},
+            {"op": "fetch", "layer": 1},
+            {"op": "store", "layer": 0, "T": 100, "seed": 6},  # out of blocks
+            {"op": "fetch", "layer": 0},
+            {"op": "layer_dicts"},
+            {"op": "evict", "keep": 16},  # block-aligned start
+            {"op": "layer_dicts"},
+            {"op": "evict", "keep": 0},
+            {"op": "layer_dicts"},
+            {"op": "memory_usage"},
+            {"op": "reset"},
+            {"op": "fetch", "layer": 1},
+            {"op": "store", "layer": 1, "T": 33, "seed": 7},
+            {"op": "fetch", "layer": 1},
+            {"op": "evict", "keep": 3},
+            {"op": "fetch", "layer": 1},
+        ],
+    },
+    {
+        # Llama-3-8B KV head shape, bf16 inputs into the fp32 reference pool
+        "name": "llama3_kv_bf16_inputs",
+        "config": {"max_seq_len": 512, "n_layers": 3, "n_heads": 8, "head_dim": 128, "block_size": 16},
+        "ops": [
+            {"op": "store", "layer": 0, "T": 37, "seed": 11, "dtype": "bf16"},
+            {"op": "store", "layer": 1, "T": 16, "seed": 12, "dtype": "bf16"},
+            {"op": "store", "layer": 2, "T": 1, "seed": 13, "dtype": "bf16"},
+            {"op": "store", "layer": 0, "T": 1, "seed": 14, "dtype": "bf16"},
+            {"op": "store", "layer": 1, "T": 1, "seed": 15, "dtype": "bf16"},
+            {"op": "layer_dicts"},
+            {"op": "store", "layer": 2, "T": 200, "seed": 16, "dtype": "bf16"},
+            {"op": "evict", "keep": 9},
+            {"op": "layer_dicts"},
+            {"op": "memory_usage"},
+        ],
+    },
+    {
+        # block_size 8, odd head_dim, many small stores
+        "name": "small_blocks",
+        "config": {"max_seq_len": 64, "n_layers": 2, "n_heads": 2, "head_dim": 24, "block_size": 8,
+                   "max_blocks": 6},
+        "ops": [
+            {"op": "store", "layer": 0, "T": 3, "seed": 21},
+            {"op": "store", "layer": 0, "T": 3, "seed": 22},
+            {"op": "store", "layer": 1, "T": 9, "seed": 23},
+            {"op": "store", "layer": 0, "T": 3, "seed": 24},
+            {"op": "layer_dicts"},
+            {"op": "evict", "keep": 4},
+            {"op": "layer_dicts"},
+            {"op": "store", "layer": 1, "T": 30, "seed": 25},
+            {"op": "layer_dicts"},
+            {"op": "memory_usage"},
+        ],
+    },
+]
+
+
+def make_paged_ops(out: Path):
+    data = []
+    for sc in PAGED_SCENARIOS:
+        data.append({"name": sc["name"], "config": sc["config"], "steps": run_paged_scenario(sc["config"], sc["ops"])})
+    out.write_text(json.dumps(data, indent=1))
+
+
+def make_paged_batched(out: Path):
+    import torch
+    from snapmind.kv_cache.paged import PagedKVCache
+
+    L, H, D, bs = 2, 8, 128, 16
+    lens = [0, 1, 16, 17, 33, 100, 32, 48]
+    need_after = [(n + 1 + bs - 1) // bs for n in lens]
+    pool = int(np.ceil(1.1 * sum(need_after)))
+    perm = np.random.RandomState(99).permutation(pool).astype(np.int64)
+    width = max(need_after) + 2
+    tables = np.zeros((len(lens), width), dtype=np.int64)
+    off = 0
+    for b, n in enumerate(lens):
+        nb = (n + bs - 1) // bs
+        tables[b, :nb] = perm[off:off + nb]
+        off += nb
+    free_stack = perm[off:].copy()
+    top = len(free_stack)
+    # expected growth: ascending sequence order, from the top of the stack
+    tables_after = tables.copy()
+    taken = 0
+    for b, n in enumerate(lens):
+        have = (n + bs - 1) // bs
+        for k in range(need_after[b] - have):
+            tables_after[b, have + k] = free_stack[top - 1 - taken]
+            taken += 1
+    records = []
+    for b, n in enumerate(lens):
+        for layer in range(L):
+            ref = PagedKVCache(max_seq_len=pool * bs, n_layers=1, n_heads=H, head_dim=D, block_size=bs,
+                               max_blocks=pool)
+            ref._block_tables[0] = [int(x) for x in tables_after[b, :need_after[b]]]
+            ref._free_blocks = set()
+            seed = 1000 + 10 * b + layer
+            if n:
+                kp = torch.from_numpy(randn(seed, (1, H, n, D))).to(torch.bfloat16)
+                vp = torch.from_numpy(randn(seed + 500, (1, H, n, D))).to(torch.bfloat16)
+                ref.store(0, kp, vp, 0)
+            ka = torch.from_numpy(randn(seed + 2000, (1, H, 1, D))).to(torch.bfloat16)
+            va = torch.from_numpy(randn(seed + 2500, (1, H, 1, D))).to(torch.bfloat16)
+            ref.store(0, ka, va, n)
+            k, v = ref.fetch(0)
+            records.append({"seq": b, "layer": layer, "seed": seed, **_fetch_record(k, v)})
+    data = {
+        "config": {"n_layers": L, "n_heads": H, "head_dim": D, "block_size": bs, "num_blocks": pool},
+        "lens": lens,
+        "tables": tables.tolist(),
+        "free_stack": free_stack.tolist(),
+        "tables_after": tables_after.tolist(),
+        "free_top_after": top - taken,
+        "seeds": "prefill k=randn(seed,(1,H,n,D)) v=randn(seed+500); append k=randn(seed+2000,(1,H,1,D)) v=randn(seed+2500); all rounded to bf16",
+        "fetch": records,
+    }
+    out.write_text(json.dumps(data, indent=1))
+
+
+GQA_CASES = [
+    # name, Hq, H, D, T_cached, dtype, seed
+    ("tiny_test_shape", 4, 2, 8, 20, "f32", 31),
+    ("tinyllama_kv", 32, 4, 64, 100, "f32", 32),
+    ("llama3_kv_f32", 32, 8, 128, 300, "f32", 33),
+    ("llama3_kv_bf16", 32, 8, 128, 300, "bf16", 34),
+    ("mha_block_edge", 4, 4, 32, 16, "f32", 35),
+]
+
+
+def make_gqa(out_npz: Path, out_json: Path):
+    import torch
+    from snapmind.kv_cache.paged import PagedKVCache
+    from snapmind.layers.attention.gqa import GroupedQueryAttention
+
+    arrays = {}
+    meta = []
+    for name, hq, h, d, t, dt, seed in GQA_CASES:
+        torch.manual_seed(seed)
+        gqa = GroupedQueryAttention(d_model=hq * d, n_heads=hq, n_kv_heads=h, pe=None)
+        with torch.no_grad():
+            gqa.out_proj.weight.copy_(torch.eye(hq * d))
+        cache = PagedKVCache(max_seq_len=t + 1, n_layers=1, n_heads=h, head_dim=d, block_size=16)
+        kc = torch.from_numpy(randn(seed + 1, (1, h, t, d)))
+        vc = torch.from_numpy(randn(seed + 2, (1, h, t, d)))
+        x = torch.from_numpy(randn(seed + 3, (1, 1, hq * d)))
+        if dt == "bf16":
+            kc, vc, x = kc.to(torch.bfloat16), vc.to(torch.bfloat16), x.to(torch.bfloat16)
+            gqa = gqa.to(torch.bfloat16)
+        cache.store(0, kc, vc, 0)
+        kv = cache.layer_dicts()[0]
+        if dt == "bf16":
+            kv = {"k": kv["k"].to(torch.bfloat16), "v": kv["v"].to(torch.bfloat16)}
+        with torch.no_grad():
+            q = gqa.q_proj(x).view(hq, d)
+            k_new = gqa.k_proj(x).view(h, d)
+            v_new = gqa.v_proj(x).view(h, d)
+            out, _ = gqa(x, kv_cache=kv)
+        out = out.view(hq, d)
+        assert kv["k"].shape[-2] == t + 1
+        enc = (lambda a: _bf16_bits(a)) if dt == "bf16" else (lambda a: a.float().numpy())
+        for key, val in (("q", q), ("k_new", k_new), ("v_new", v_new), ("out", out)):
+            arrays[f"{name}__{key}"] = enc(val)
+        meta.append({"name": name, "n_q_heads": hq, "n_kv_heads": h, "head_dim": d, "cached_tokens": t,
+                     "dtype": dt, "seed": seed, "scale": d ** -0.5,
+                     "cached_k": "randn(seed+1,(1,H,T,D))", "cached_v": "randn(seed+2,(1,H,T,D))"})
+    np.savez_compressed(out_npz, **arrays)
+    out_json.write_text(json.dumps(meta, indent=1))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("SNAPMIND_REFERENCE", "/root/reference"))
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    import torch
+
+    torch.set_num_threads(4)
+    make_paged_ops(HERE / "paged_ops.json")
+    make_paged_batched(HERE / "paged_batched.json")
+    make_gqa(HERE / "gqa_decode.npz", HERE / "gqa_decode.json")
+    print("golden vectors written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,117 @@
+"""The oracle against golden vectors produced by running the reference itself."""
+import json
+
+import numpy as np
+import pytest
+
+from inputs import digest, randn
+from oracle import bf16, gqa, paged
+from replay import GOLDEN, load_paged_batched, load_paged_ops, replay
+
+
+def _np_input(a, dtype):
+    return bf16.round_to_bf16(a) if dtype == "bf16" else a
+
+
+@pytest.mark.parametrize("scenario", load_paged_ops(), ids=lambda s: s["name"])
+def test_oracle_replays_reference_paged_ops(scenario):
+    replay(
+        scenario,
+        make_cache=lambda cfg: paged.PagedKVCacheOracle(**cfg),
+        to_input=_np_input,
+        to_numpy=lambda a: np.ascontiguousarray(a, dtype=np.float32),
+        digest_key="f32",
+    )
+
+
+@pytest.mark.parametrize("scenario", load_paged_ops(), ids=lambda s: s["name"])
+def test_oracle_replays_reference_paged_ops_bf16_digest(scenario):
+    replay(
+        scenario,
+        make_cache=lambda cfg: paged.PagedKVCacheOracle(**cfg),
+        to_input=_np_input,
+        to_numpy=lambda a: bf16.f32_to_bf16(np.asarray(a, dtype=np.float32)),
+        digest_key="bf16",
+    )
+
+
+def batched_oracle_run(g):
+    cfg = g["config"]
+    L, H, D, bs, nb = cfg["n_layers"], cfg["n_heads"], cfg["head_dim"], cfg["block_size"], cfg["num_blocks"]
+    lens = np.array(g["lens"])
+    tables = np.array(g["tables"])
+    k_pool = np.zeros((L, nb, H, bs, D), np.float32)
+    v_pool = np.zeros_like(k_pool)
+    recs = {(r["seq"], r["layer"]): r for r in g["fetch"]}
+    # prefill each sequence with its own tokens
+    for b, n in enumerate(lens):
+        if n == 0:
+            continue
+        kn = np.stack([bf16.round_to_bf16(randn(recs[(b, l)]["seed"], (1, H, n, D)))[0] for l in range(L)])
+        vn = np.stack([bf16.round_to_bf16(randn(recs[(b, l)]["seed"] + 500, (1, H, n, D)))[0] for l in range(L)])
+        paged.append(k_pool, v_pool, tables[b:b + 1], [0], kn[:, None], vn[:, None], bs)
+    free = np.array(g["free_stack"])
+    tables2, lens2, top2, err = paged.reserve(tables, lens, free, len(free), 1, bs)
+    assert err is None
+    ka = np.stack([np.stack([bf16.round_to_bf16(randn(recs[(b, l)]["seed"] + 2000, (H, 1, D))) for b in range(len(lens))]) for l in range(L)])
+    va = np.stack([np.stack([bf16.round_to_bf16(randn(recs[(b, l)]["seed"] + 2500, (H, 1, D))) for b in range(len(lens))]) for l in range(L)])
+    paged.append(k_pool, v_pool, tables2, lens2 - 1, ka, va, bs)
+    kg, vg = paged.gather(k_pool, v_pool, tables2, lens2, bs)
+    return tables2, lens2, top2, kg, vg
+
+
+def test_oracle_batched_matches_reference_fetch():
+    g = load_paged_batched()
+    H, D = g["config"]["n_heads"], g["config"]["head_dim"]
+    tables2, lens2, top2, kg, vg = batched_oracle_run(g)
+    assert tables2.tolist() == g["tables_after"]
+    assert top2 == g["free_top_after"]
+    offs = np.concatenate([[0], np.cumsum(lens2)]) * H * D
+    for r in g["fetch"]:
+        b, l = r["seq"], r["layer"]
+        k = kg[l, offs[b]:offs[b + 1]].reshape(1, H, lens2[b], D)
+        v = vg[l, offs[b]:offs[b + 1]].reshape(1, H, lens2[b], D)
+        assert digest(k) == r["k_sha_f32"]
+        assert digest(v) == r["v_sha_f32"]
+        assert digest(bf16.f32_to_bf16(k)) == r["k_sha_bf16"]
+
+
+def load_gqa():
+    meta = json.loads((GOLDEN / "gqa_decode.json").read_text())
+    arrays = np.load(GOLDEN / "gqa_decode.npz")
+    return meta, arrays
+
+
+def gqa_case_inputs(m, arrays):
+    """(q (Hq,D), K (H,T+1,D), V, expected out (Hq,D)) as float32, bf16 values exact."""
+    name, h, d, t = m["name"], m["n_kv_heads"], m["head_dim"], m["cached_tokens"]
+    dec = (lambda a: bf16.bf16_to_f32(a)) if m["dtype"] == "bf16" else (lambda a: a.astype(np.float32))
+    q, kn, vn, out = (dec(arrays[f"{name}__{k}"]) for k in ("q", "k_new", "v_new", "out"))
+    kc = randn(m["seed"] + 1, (1, h, t, d))[0]
+    vc = randn(m["seed"] + 2, (1, h, t, d))[0]
+    if m["dtype"] == "bf16":
+        kc, vc = bf16.round_to_bf16(kc), bf16.round_to_bf16(vc)
+    k = np.concatenate([kc, kn[:, None, :]], axis=1)
+    v = np.concatenate([vc, vn[:, None, :]], axis=1)
+    return q, k, v, out
+
+
+def tolerance(dtype):
+    return (1e-5, 1e-5) if dtype == "f32" else (2e-2, 2e-2)
+
+
+@pytest.mark.parametrize("case", json.loads((GOLDEN / "gqa_decode.json").read_text()), ids=lambda m: m["name"])
+def test_oracle_gqa_matches_reference_forward(case):
+    meta, arrays = load_gqa()
+    q, k, v, out = gqa_case_inputs(case, arrays)
+    got = gqa.gqa_attention(q[None, :, None, :], k[None], v[None], case["scale"])[0, :, 0, :]
+    rtol, atol = tolerance(case["dtype"])
+    np.testing.assert_allclose(got, out, rtol=rtol, atol=atol)
+
+
+def test_bf16_rounding_is_round_to_nearest_even():
+    x = np.array([1.0, 1.00390625, 1.01171875, -2.5, 3.0e38, np.inf, 1e-40], np.float32)
+    import torch
+
+    want = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert (bf16.f32_to_bf16(x) == want).all()
