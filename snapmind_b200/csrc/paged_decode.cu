@@ -204,7 +204,12 @@ static int launch_generic_g(const DecodeParams& p, dim3 grid, cudaStream_t st) {
   if (p.group <= 2) return go(paged_decode_generic_kernel<T, NI, 2>, 2);
   if (p.group <= 4) return go(paged_decode_generic_kernel<T, NI, 4>, 4);
   if (p.group <= 8) return go(paged_decode_generic_kernel<T, NI, 8>, 8);
-  if (NI <= 4 && p.group <= 16) return go(paged_decode_generic_kernel<T, NI, 16>, 16);
+  if constexpr (NI <= 4) {
+    if (p.group <= 16) return go(paged_decode_generic_kernel<T, NI, 16>, 16);
+  }
+  if constexpr (NI <= 2) {
+    if (p.group <= 32) return go(paged_decode_generic_kernel<T, NI, 32>, 32);
+  }
   set_last_error("paged_decode: group size %d with head_dim %d unsupported", p.group, p.head_dim);
   return SNAPMIND_ERR_UNSUPPORTED;
 }

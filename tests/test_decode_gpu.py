@@ -86,6 +86,39 @@ def test_decode_random_matches_oracle(cuda_device, hq, h, d, dt, force_generic):
         np.testing.assert_allclose(got.float().cpu().numpy(), want, rtol=rtol, atol=atol)
 
 
+@pytest.mark.parametrize("bs", [16, 32, 64, 8])
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_decode_block_sizes_tensor_core_vs_oracle(cuda_device, bs, dt):
+    """Block sizes 16/32/64 take the TMA + tensor-core kernel; 8 falls back to CUDA cores."""
+    hq, h, d = 32, 8, 128
+    lens = [1, 63, 64, 65, 200, 511, 1000]
+    rnd = bf16.round_to_bf16 if dt == "bf16" else (lambda a: a.astype(np.float16).astype(np.float32))
+    ks = [rnd(randn(600 + i, (h, n, d))) for i, n in enumerate(lens)]
+    vs = [rnd(randn(700 + i, (h, n, d))) for i, n in enumerate(lens)]
+    pool, kp, vp, tables, lens_a = build_pool(ks, vs, TORCH_DT[dt], bs=bs, seed=bs)
+    q = rnd(randn(8, (len(lens), hq, d)))
+    want = gqa.paged_gqa_decode(q, kp, vp, tables, lens_a, d ** -0.5, bs)
+    for split in (64, 128, 0):
+        got = pool.decode(0, torch.from_numpy(q).cuda().to(TORCH_DT[dt]), split_tokens=max(split, bs) if split else 0)
+        pool.check()
+        np.testing.assert_allclose(got.float().cpu().numpy(), want, rtol=2e-2, atol=2e-2)
+
+
+def test_decode_tensor_core_matches_cuda_core(cuda_device):
+    """The two kernels agree closely on a config-3-like batch (bf16)."""
+    rng = np.random.RandomState(11)
+    lens = list(rng.randint(1, 3000, size=24))
+    h, hq, d = 8, 32, 128
+    ks = [bf16.round_to_bf16(randn(800 + i, (h, n, d))) for i, n in enumerate(lens)]
+    vs = [bf16.round_to_bf16(randn(900 + i, (h, n, d))) for i, n in enumerate(lens)]
+    pool, *_ = build_pool(ks, vs, torch.bfloat16, seed=2)
+    q = torch.from_numpy(bf16.round_to_bf16(randn(5, (len(lens), hq, d)))).cuda().to(torch.bfloat16)
+    fast = pool.decode(0, q, split_tokens=256)
+    slow = pool.decode(0, q, split_tokens=256, force_generic=True)
+    pool.check()
+    torch.testing.assert_close(fast.float(), slow.float(), rtol=1e-2, atol=1e-2)
+
+
 def test_decode_long_context_many_splits_and_repeat(cuda_device):
     """Contexts up to 8192 (config-3 range), tickets reset between calls."""
     rng = np.random.RandomState(5)
