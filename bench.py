@@ -74,27 +74,43 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.lines: list[str] = []
+        self._first = None
+        self._thread = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            if ln.strip():
+                self.lines.append(ln)
+                self._first.set()
 
     def __enter__(self):
+        import threading
+
+        self._first = threading.Event()
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"],
+                 "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+        self._first.wait(timeout=5.0)  # sampling is live before the timed region starts
+        self.lines.clear()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            if self._thread is not None:
+                self._thread.join(timeout=5)
 
     def summary(self) -> dict | None:
         rows = []
@@ -143,6 +159,12 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
     torch.cuda.set_device(dev)
     steps, warmup = args.steps, args.warmup
     seed = 1234 + 7919 * rank
+    if args.only == "append_gather":
+        ag = run_append_gather(args, dev, seed, dist, world)
+        return {"metric": METRIC, "value": ag["value"], "unit": ag["unit"], "n_gpus": world, "steps": steps,
+                "warmup": warmup, "ms_per_step": ag["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": {"workload": ag["workload"]},
+                "roofline": ag["roofline"], "gpu_launches": ag["gpu_launches"], "kv_append_gather": ag}
 
     # ---------------- decode workload ----------------
     lens = seeded_lengths(seed, DECODE_BATCH, *DECODE_CTX)
@@ -241,7 +263,7 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
     torch.cuda.empty_cache()
 
     # ---------------- append + gather workload ----------------
-    ag = run_append_gather(args, dev, seed, dist, world)
+    ag = run_append_gather(args, dev, seed, dist, world) if args.only == "all" else None
 
     line = {
         "metric": METRIC,
@@ -257,7 +279,7 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) K/V/q, seeded context lengths and shuffled block tables)",
         "config": {
-            "workload": "paged GQA decode step, Llama-3-8B KV shape: 32 layers x (append 1 token/seq + "
+            "workload": f"paged GQA decode step, Llama-3-8B KV shape: {L} layers x (append 1 token/seq + "
                         "paged decode attention); 32 q / 8 kv heads, head_dim 128, bf16, block 16, "
                         "ctx U[1024,8192], shuffled block tables",
             "batch_per_gpu": DECODE_BATCH,
@@ -505,14 +527,16 @@ def cpu_reference_timing(n_seqs: int, steps: int, warmup: int, seed: int = 99) -
 def run_reference_arm(args, rank: int, world: int) -> dict | None:
     if rank != 0:
         return None
-    res = cpu_reference_timing(n_seqs=args.cpu_sample, steps=args.steps, warmup=min(args.warmup, 1))
+    # each step is seconds of CPU work: time at most 5 of them so the run stays within minutes
+    timed = max(1, min(args.steps, 5))
+    res = cpu_reference_timing(n_seqs=args.cpu_sample, steps=timed, warmup=min(args.warmup, 1))
     return {
         "impl": "reference",
         "metric": METRIC,
         "value": res["value"],
         "unit": "tok/s",
         "n_gpus": world,
-        "steps": args.steps,
+        "steps": timed,
         "warmup": args.warmup,
         "ms_per_step": round(res["step_s"] * 1e3, 2),
         "higher_is_better": True,
@@ -532,13 +556,20 @@ def run_reference_arm(args, rank: int, world: int) -> dict | None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=min(128, max(8, os.cpu_count() or 8)))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # smaller cases of the same kernels (profiling captures); defaults are the benchmark config
+    ap.add_argument("--batch", type=int, default=DECODE_BATCH, help="decode sequences per GPU")
+    ap.add_argument("--ag-batch", type=int, default=AG_BATCH, help="append/gather sequences per GPU")
+    ap.add_argument("--layers", type=int, default=L)
+    ap.add_argument("--only", choices=["all", "decode", "append_gather"], default="all")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup
+    global DECODE_BATCH, AG_BATCH, L
+    DECODE_BATCH, AG_BATCH, L = args.batch, args.ag_batch, args.layers
 
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
