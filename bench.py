@@ -553,6 +553,11 @@ def run_reference_arm(args, rank: int, world: int) -> dict | None:
 
 
 # ----------------------------------------------------------------------------- main
+def _set_workload(batch: int, ag_batch: int, layers: int) -> None:
+    global DECODE_BATCH, AG_BATCH, L
+    DECODE_BATCH, AG_BATCH, L = batch, ag_batch, layers
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -568,8 +573,7 @@ def main():
     ap.add_argument("--only", choices=["all", "decode", "append_gather"], default="all")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup
-    global DECODE_BATCH, AG_BATCH, L
-    DECODE_BATCH, AG_BATCH, L = args.batch, args.ag_batch, args.layers
+    _set_workload(args.batch, args.ag_batch, args.layers)
 
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
