@@ -173,6 +173,34 @@ SNAPMIND_API int snapmind_paged_gqa_decode(const void *q, int64_t q_stride_seq, 
                               void *workspace, int64_t workspace_bytes, int32_t *err_word,
                               void *stream);
 
+/*
+ * The same paged GQA decode for callers that cannot allocate device memory:
+ * a host bound through this C ABI with no CUDA allocator of its own (or whose
+ * device memory belongs to another allocator it cannot reach), or a serving
+ * loop that must not call cudaMalloc between steps because it can synchronise
+ * the device.  No counterpart exists in the reference (snapmind has no GPU
+ * path); it takes the arguments of snapmind_paged_gqa_decode minus the
+ * workspace and allocates nothing.
+ *
+ * Its scratch is a static device array of SNAPMIND_NOALLOC_DECODE_SCRATCH_BYTES
+ * that every GPU loading the library holds until exit; a call that would need
+ * more is rejected (SNAPMIND_ERR_BAD_ARGUMENT, with the sizes in the message).
+ * The first call on a device looks up the array's address — make it before
+ * any stream capture.  All calls on a device share the array: each clears the
+ * ticket counters it needs on its stream, and calls that overlap on the GPU
+ * race on the shared scratch and must not be issued.
+ */
+#define SNAPMIND_NOALLOC_DECODE_SCRATCH_BYTES (16u << 20)
+SNAPMIND_API int snapmind_paged_gqa_decode_noalloc(const void *q, int64_t q_stride_seq, int64_t q_stride_head,
+                                      const void *k_pool, const void *v_pool, int dtype,
+                                      const int32_t *block_tables, int64_t table_stride_seq,
+                                      int32_t table_width, const int32_t *seq_lens,
+                                      void *out, int64_t out_stride_seq, int64_t out_stride_head,
+                                      float scale, int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
+                                      int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                                      int32_t max_seq_len, int32_t split_tokens, int32_t flags,
+                                      int32_t *err_word, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
