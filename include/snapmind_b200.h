@@ -142,6 +142,31 @@ SNAPMIND_API int snapmind_kv_release(int32_t *block_tables, int64_t table_stride
                         int32_t num_blocks, int32_t *err_word, void *stream);
 
 /*
+ * One segment of a token-dimension concatenation: `rows` rows (the leading
+ * dims of a (..., T, D) tensor, flattened) of n_tokens x head_dim elements,
+ * row r starting row_stride tokens (row_stride*head_dim elements) after row
+ * r-1 at k (likewise v).
+ */
+typedef struct snapmind_segment {
+  const void *k;
+  const void *v;
+  int64_t row_stride;
+  int32_t n_tokens;
+  int32_t pad_;
+} snapmind_segment;
+
+/*
+ * Concatenate segments along the token dimension into (rows, sum n, D)
+ * outputs — the torch.cat(k_parts, dim=-2) of the tiered cache's live view
+ * (snapmind/kv_cache/tiered.py:156-182) in one launch per 256 segments.
+ * `segs` is a HOST array of n_segs descriptors.  Output row r starts
+ * out_row_stride tokens after row r-1 (out_row_stride >= sum n).
+ */
+SNAPMIND_API int snapmind_kv_concat(const snapmind_segment *segs, int32_t n_segs, int32_t rows,
+                       int32_t head_dim, int dtype, void *k_out, void *v_out,
+                       int64_t out_row_stride, void *stream);
+
+/*
  * Paged GQA decode attention: one query token per sequence against the
  * seq_lens[b] cached tokens reached through the block table.  Computes
  * softmax(q k^T * scale) v per query head, query head h reading kv head

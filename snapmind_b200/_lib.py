@@ -67,6 +67,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _int,
         [_p, _i64, _i32, _p, _p, _i32, _i32, _p, _p, _i32, _p, _p],
     ),
+    "snapmind_kv_concat": (_int, [_p, _i32, _i32, _i32, _int, _p, _p, _i64, _p]),
     "snapmind_paged_gqa_decode_split_tokens": (_i32, [_i32, _i32, _i32, _i32]),
     "snapmind_paged_gqa_decode_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "snapmind_paged_gqa_decode": (

@@ -290,6 +290,174 @@ def make_gqa(out_npz: Path, out_json: Path):
     out_json.write_text(json.dumps(meta, indent=1))
 
 
+TIERED_SCENARIOS = [
+    {
+        "name": "decode_token_major_evicting",
+        "config": {"max_seq_len": 512, "n_layers": 2, "n_heads": 2, "head_dim": 16, "pool_tokens": 24,
+                   "chunk_size": 8},
+        "ops": [
+            {"op": "decode", "start": 0, "count": 45, "seed": 1},
+            {"op": "layer_dicts"},
+            {"op": "memory_usage"},
+            {"op": "score_and_repage", "scores": {"0": 0.9, "1": 0.2, "2": 0.7, "3": 0.5, "4": 0.49}},
+            {"op": "fetch", "layer": 0},
+            {"op": "fetch", "layer": 1},
+            {"op": "decode", "start": 45, "count": 20, "seed": 2},
+            {"op": "fetch", "layer": 0},
+            {"op": "layer_dicts"},
+            {"op": "score_and_repage", "scores": {"1": 0.8, "5": 0.9, "6": 0.1}, "tensor": True, "threshold": 0.6},
+            {"op": "memory_usage"},
+            {"op": "evict", "keep": 10},
+            {"op": "score_and_repage", "scores": {}},
+            {"op": "reset"},
+            {"op": "fetch", "layer": 0},
+            {"op": "layer_dicts"},
+            {"op": "decode", "start": 0, "count": 9, "seed": 3},
+            {"op": "layer_dicts"},
+        ],
+    },
+    {
+        # layer-major prefill: one active chunk is shared by all layers (loses data)
+        "name": "layer_major_prefill",
+        "config": {"max_seq_len": 512, "n_layers": 3, "n_heads": 2, "head_dim": 8, "pool_tokens": 16,
+                   "chunk_size": 8},
+        "ops": [
+            {"op": "store", "layer": 0, "T": 30, "pos": 0, "seed": 11},
+            {"op": "store", "layer": 1, "T": 30, "pos": 0, "seed": 12},
+            {"op": "store", "layer": 2, "T": 10, "pos": 0, "seed": 13},
+            {"op": "layer_dicts"},
+            {"op": "memory_usage"},
+            {"op": "decode", "start": 30, "count": 5, "seed": 14},
+            {"op": "layer_dicts"},
+            {"op": "score_and_repage", "scores": {"1": 0.7, "2": 0.7}},
+            {"op": "memory_usage"},
+        ],
+    },
+    {
+        # chunk-crossing multi-token stores, repeated positions, position jumps
+        "name": "multi_token_duplicates_jumps",
+        "config": {"max_seq_len": 512, "n_layers": 2, "n_heads": 2, "head_dim": 16, "pool_tokens": 32,
+                   "chunk_size": 8},
+        "ops": [
+            {"op": "store", "layer": 0, "T": 13, "pos": 5, "seed": 21},
+            {"op": "store", "layer": 1, "T": 13, "pos": 5, "seed": 22},
+            {"op": "store", "layer": 0, "T": 1, "pos": 17, "seed": 23},
+            {"op": "store", "layer": 1, "T": 3, "pos": 16, "seed": 24},
+            {"op": "layer_dicts"},
+            {"op": "store", "layer": 0, "T": 20, "pos": 100, "seed": 25},
+            {"op": "layer_dicts"},
+            {"op": "store", "layer": 0, "T": 8, "pos": 200, "seed": 26},
+            {"op": "store", "layer": 0, "T": 8, "pos": 200, "seed": 27},
+            {"op": "store", "layer": 1, "T": 1, "pos": 300, "seed": 28},
+            {"op": "layer_dicts"},
+            {"op": "memory_usage"},
+            {"op": "score_and_repage", "scores": {"2": 0.6, "12": 0.9}},
+            {"op": "fetch", "layer": 1},
+        ],
+    },
+    {
+        "name": "batch2_bf16",
+        "config": {"max_seq_len": 512, "n_layers": 2, "n_heads": 2, "head_dim": 32, "pool_tokens": 48,
+                   "chunk_size": 16},
+        "ops": [
+            {"op": "decode", "start": 0, "count": 70, "seed": 31, "batch": 2, "dtype": "bf16"},
+            {"op": "layer_dicts"},
+            {"op": "score_and_repage", "scores": {"0": 0.1, "1": 0.9, "2": 0.4}},
+            {"op": "memory_usage"},
+            {"op": "fetch", "layer": 1},
+        ],
+    },
+    {
+        "name": "reference_defaults",
+        "config": {"max_seq_len": 4096, "n_layers": 2, "n_heads": 8, "head_dim": 64},
+        "ops": [
+            {"op": "decode", "start": 0, "count": 150, "seed": 41},
+            {"op": "layer_dicts"},
+            {"op": "score_and_repage", "scores": {"0": 0.1, "1": 0.1}},
+            {"op": "memory_usage"},
+        ],
+    },
+]
+
+
+def tiered_inputs(op, n_layers, n_heads, head_dim):
+    """The (layer, key, value, seq_pos) stores an op performs, as float32 numpy."""
+    b = op.get("batch", 1)
+    if op["op"] == "store":
+        k = randn(op["seed"], (b, n_heads, op["T"], head_dim))
+        v = randn(op["seed"] + 1000, (b, n_heads, op["T"], head_dim))
+        return [(op["layer"], k, v, op["pos"])]
+    out = []
+    for t in range(op["count"]):
+        for layer in range(n_layers):
+            s = op["seed"] * 100000 + t * n_layers + layer
+            out.append((layer, randn(s, (b, n_heads, 1, head_dim)), randn(s + 50000, (b, n_heads, 1, head_dim)),
+                        op["start"] + t))
+    return out
+
+
+def _tiered_state(cache):
+    import torch
+
+    layout, chunk_bytes, data = {}, {}, {}
+    for cid, layers in cache._chunks.items():
+        layout[str(cid)] = [None if e["k"] is None else int(e["k"].shape[-2]) for e in layers]
+        chunk_bytes[str(cid)] = sum(2 * e["k"].numel() * e["k"].element_size() for e in layers if e["k"] is not None)
+        data[str(cid)] = [None if e["k"] is None else [digest(e["k"].to(torch.float32).numpy()),
+                                                        digest(e["v"].to(torch.float32).numpy())] for e in layers]
+    return {"hot": sorted(cache._hot_set), "chunks": sorted(cache._chunks), "layout": layout,
+            "chunk_bytes": chunk_bytes, "chunk_data": data, "total_tokens": cache._total_tokens}
+
+
+def _live_record(k, v):
+    import torch
+
+    if k is None:
+        return None
+    return {"shape": list(k.shape), "k": digest(k.to(torch.float32).numpy()), "v": digest(v.to(torch.float32).numpy())}
+
+
+def make_tiered(out: Path):
+    import torch
+    from snapmind.kv_cache.tiered import TieredPagedKVCache
+
+    data = []
+    for sc in TIERED_SCENARIOS:
+        cfg = sc["config"]
+        cache = TieredPagedKVCache(**cfg, device="cpu")
+        steps = []
+        for op in sc["ops"]:
+            rec: dict = {}
+            kind = op["op"]
+            if kind in ("store", "decode"):
+                for layer, k, v, pos in tiered_inputs(op, cfg["n_layers"], cfg["n_heads"], cfg["head_dim"]):
+                    kt, vt = torch.from_numpy(k), torch.from_numpy(v)
+                    if op.get("dtype") == "bf16":
+                        kt, vt = kt.to(torch.bfloat16), vt.to(torch.bfloat16)
+                    cache.store(layer, kt, vt, pos)
+            elif kind == "layer_dicts":
+                d = cache.layer_dicts()
+                rec["live"] = {str(i): _live_record(e["k"], e["v"]) for i, e in d.items()}
+            elif kind == "fetch":
+                k, v = cache.fetch(op["layer"])
+                rec["fetch"] = None if k.numel() == 0 else _live_record(k, v)
+            elif kind == "score_and_repage":
+                scores = {int(c): (torch.tensor(s) if op.get("tensor") else s) for c, s in op["scores"].items()}
+                cache.score_and_repage(scores, threshold=op.get("threshold", 0.5))
+                if cache._live_dicts is not None:
+                    rec["live"] = {str(i): _live_record(e["k"], e["v"]) for i, e in cache._live_dicts.items()}
+            elif kind == "memory_usage":
+                rec["usage_reported_cpu_device"] = cache.memory_usage()
+            elif kind == "evict":
+                cache.evict(op["keep"])
+            elif kind == "reset":
+                cache.reset()
+            rec["state"] = _tiered_state(cache)
+            steps.append({"op": op, "expect": rec})
+        data.append({"name": sc["name"], "config": cfg, "steps": steps})
+    out.write_text(json.dumps(data, indent=1))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SNAPMIND_REFERENCE", "/root/reference"))
@@ -301,6 +469,7 @@ def main():
     make_paged_ops(HERE / "paged_ops.json")
     make_paged_batched(HERE / "paged_batched.json")
     make_gqa(HERE / "gqa_decode.npz", HERE / "gqa_decode.json")
+    make_tiered(HERE / "tiered_ops.json")
     print("golden vectors written to", HERE)
 
 

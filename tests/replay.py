@@ -87,3 +87,100 @@ def _check_fetch(kv, rec, to_numpy, digest_key, where):
     ka, va = to_numpy(k), to_numpy(v)
     assert digest(ka) == rec[f"k_sha_{digest_key}"], f"{where}: K bytes differ"
     assert digest(va) == rec[f"v_sha_{digest_key}"], f"{where}: V bytes differ"
+
+
+# ---------------------------------------------------------------------------
+# tiered cache (tests/golden/tiered_ops.json)
+# ---------------------------------------------------------------------------
+def load_tiered_ops():
+    return json.loads((GOLDEN / "tiered_ops.json").read_text())
+
+
+def tiered_inputs(op, n_layers, n_heads, head_dim):
+    """Same stores as tests/golden/make_golden.py::tiered_inputs."""
+    b = op.get("batch", 1)
+    if op["op"] == "store":
+        k = randn(op["seed"], (b, n_heads, op["T"], head_dim))
+        v = randn(op["seed"] + 1000, (b, n_heads, op["T"], head_dim))
+        return [(op["layer"], k, v, op["pos"])]
+    out = []
+    for t in range(op["count"]):
+        for layer in range(n_layers):
+            s = op["seed"] * 100000 + t * n_layers + layer
+            out.append((layer, randn(s, (b, n_heads, 1, head_dim)), randn(s + 50000, (b, n_heads, 1, head_dim)),
+                        op["start"] + t))
+    return out
+
+
+def replay_tiered(scenario, cache, to_input, to_numpy, make_score, state_of, entry_arrays):
+    """Drive ``cache`` through the recorded ops and compare every recorded fact.
+
+    to_input(array, dtype_tag) -> cache input; to_numpy(tensor) -> float32 array;
+    make_score(float, as_tensor) -> score value; state_of(cache) -> (hot, chunks,
+    layout, total_tokens); entry_arrays(cache, cid, layer) -> (k, v) float32 or None.
+    """
+    cfg = scenario["config"]
+    for i, step in enumerate(scenario["steps"]):
+        op, exp = step["op"], step["expect"]
+        where = f"{scenario['name']} step {i} {op['op']}"
+        kind = op["op"]
+        got = {}
+        if kind in ("store", "decode"):
+            for layer, k, v, pos in tiered_inputs(op, cfg["n_layers"], cfg["n_heads"], cfg["head_dim"]):
+                cache.store(layer, to_input(k, op.get("dtype")), to_input(v, op.get("dtype")), pos)
+        elif kind == "layer_dicts":
+            got["live"] = cache.layer_dicts()
+        elif kind == "fetch":
+            got["fetch"] = cache.fetch(op["layer"])
+        elif kind == "score_and_repage":
+            scores = {int(c): make_score(s, op.get("tensor", False)) for c, s in op["scores"].items()}
+            cache.score_and_repage(scores, threshold=op.get("threshold", 0.5))
+            got["live"] = getattr(cache, "_live_dicts", None) or getattr(cache, "live_dicts", None)
+        elif kind == "memory_usage":
+            got["usage"] = cache.memory_usage()
+        elif kind == "evict":
+            cache.evict(op["keep"])
+        elif kind == "reset":
+            cache.reset()
+        st = exp["state"]
+        hot, chunks, layout, total = state_of(cache)
+        assert sorted(hot) == st["hot"], where
+        assert sorted(chunks) == st["chunks"], where
+        assert {str(c): n for c, n in layout.items()} == st["layout"], where
+        assert total == st["total_tokens"], where
+        for cid, per_layer in st["chunk_data"].items():
+            for layer, rec in enumerate(per_layer):
+                arr = entry_arrays(cache, int(cid), layer)
+                if rec is None:
+                    assert arr is None, f"{where}: chunk {cid} layer {layer}"
+                else:
+                    assert digest(arr[0]) == rec[0] and digest(arr[1]) == rec[1], f"{where}: chunk {cid} layer {layer}"
+        if "live" in exp:
+            for li, rec in exp["live"].items():
+                d = got["live"][int(li)]
+                _check_live(d["k"], d["v"], rec, to_numpy, f"{where} live {li}")
+        if "fetch" in exp:
+            k, v = got["fetch"]
+            if exp["fetch"] is None:
+                assert k.numel() == 0 if hasattr(k, "numel") else k.size == 0
+            else:
+                _check_live(k, v, exp["fetch"], to_numpy, f"{where} fetch")
+        if "usage_reported_cpu_device" in exp:
+            ref = exp["usage_reported_cpu_device"]
+            gpu = sum(b for c, b in st["chunk_bytes"].items() if int(c) in st["hot"])
+            cpu = sum(b for c, b in st["chunk_bytes"].items() if int(c) not in st["hot"])
+            assert gpu + cpu == ref["cpu_bytes"] + ref["gpu_bytes"], where
+            u = got["usage"]
+            assert (u["gpu_bytes"], u["cpu_bytes"]) == (gpu, cpu), f"{where}: {u}"
+            for key in ("hot_chunks", "cold_chunks", "total_tokens", "pool_slots"):
+                assert u[key] == ref[key], f"{where}: {key}"
+
+
+def _check_live(k, v, rec, to_numpy, where):
+    if rec is None:
+        assert k is None and v is None, where
+        return
+    assert k is not None, where
+    assert list(k.shape) == rec["shape"], f"{where}: {tuple(k.shape)} vs {rec['shape']}"
+    assert digest(to_numpy(k)) == rec["k"], f"{where}: K differs"
+    assert digest(to_numpy(v)) == rec["v"], f"{where}: V differs"

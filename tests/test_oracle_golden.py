@@ -115,3 +115,34 @@ def test_bf16_rounding_is_round_to_nearest_even():
 
     want = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     assert (bf16.f32_to_bf16(x) == want).all()
+
+
+# ---------------------------------------------------------------------------
+# tiered cache oracle against the reference's recorded behaviour
+# ---------------------------------------------------------------------------
+from oracle import tiered as otiered  # noqa: E402
+from replay import load_tiered_ops, replay_tiered  # noqa: E402
+
+
+@pytest.mark.parametrize("scenario", load_tiered_ops(), ids=lambda s: s["name"])
+def test_tiered_oracle_replays_reference(scenario):
+    cfg = scenario["config"]
+    cache = otiered.TieredPagedKVCacheOracle(**cfg)
+    bf16_ops = any(st["op"].get("dtype") == "bf16" for st in scenario["steps"])
+    elem = 2 if bf16_ops else 4
+    cache_usage = cache.memory_usage
+    cache.memory_usage = lambda: cache_usage(elem_size=elem)
+
+    def entry_arrays(c, cid, layer):
+        e = c.chunks[cid][layer]
+        return None if e["k"] is None else (np.asarray(e["k"], np.float32), np.asarray(e["v"], np.float32))
+
+    replay_tiered(
+        scenario,
+        cache,
+        to_input=lambda a, tag: bf16.round_to_bf16(a) if tag == "bf16" else a,
+        to_numpy=lambda a: np.asarray(a, np.float32),
+        make_score=lambda s, as_tensor: s,
+        state_of=lambda c: (c.hot_set, c.chunks.keys(), c.chunk_layout(), c.total_tokens),
+        entry_arrays=entry_arrays,
+    )
