@@ -73,6 +73,7 @@ SNAPMIND_API const char *snapmind_last_error(void);
  *       + t*in_stride_tok + d.
  * Input and pool dtypes may differ (values are converted, round to nearest even).
  * Table entries must already exist (the host or snapmind_kv_reserve grows them).
+ * v_pool and v_new may both be NULL: a single-pool cache (the MLA latent rows).
  */
 SNAPMIND_API int snapmind_kv_append(void *k_pool, void *v_pool, int pool_dtype, int64_t pool_layer_stride,
                        const void *k_new, const void *v_new, int in_dtype,
@@ -93,7 +94,8 @@ SNAPMIND_API int snapmind_kv_append(void *k_pool, void *v_pool, int pool_dtype, 
  * seq_len(b) = seq_lens[b] when seq_lens != NULL, else seq_len0.
  * Output layer l starts at k_out + l*out_layer_stride and holds
  * out_layer_capacity elements; when the lengths need more, nothing is written
- * and SNAPMIND_DEVERR_TABLE is set.  batch <= 8192.
+ * and SNAPMIND_DEVERR_TABLE is set.  batch <= 8192.  v_pool and v_out may both
+ * be NULL (single-pool cache).
  */
 SNAPMIND_API int snapmind_kv_gather(const void *k_pool, const void *v_pool, int dtype, int64_t pool_layer_stride,
                        void *k_out, void *v_out, int64_t out_layer_stride,
@@ -165,6 +167,74 @@ typedef struct snapmind_segment {
 SNAPMIND_API int snapmind_kv_concat(const snapmind_segment *segs, int32_t n_segs, int32_t rows,
                        int32_t head_dim, int dtype, void *k_out, void *v_out,
                        int64_t out_row_stride, void *stream);
+
+/*
+ * Frozen chunk keys of the lookahead indexer: for chunks
+ * [chunk_begin, chunk_begin + chunk_count) of every sequence, the mean of the
+ * chunk's rows (the first `width` columns of each pool row of row_width
+ * elements) — LookaheadSparseIndexer.build_frozen_keys
+ * (snapmind/layers/indexer/lookahead.py:40-50), with chunk c = block c of the
+ * sequence's table (block_size = chunk size).  When `proj` is not NULL the mean
+ * is also projected: out = proj . mean, proj row-major [out_dim][width] of
+ * proj_dtype.  out is fp32 [batch][max_chunks][out_dim or width]; chunks past
+ * a sequence's length are written as zeros.  seq_lens may be NULL: every
+ * chunk then holds block_size rows.
+ */
+SNAPMIND_API int snapmind_indexer_pool_chunks(const void *pool, int dtype, int64_t row_width, int32_t width,
+                                 const int32_t *block_tables, int64_t table_stride, int32_t table_width,
+                                 const int32_t *seq_lens, int32_t batch, int32_t block_size,
+                                 int32_t num_blocks, int32_t chunk_begin, int32_t chunk_count,
+                                 int32_t max_chunks, const void *proj, int proj_dtype, int32_t out_dim,
+                                 float *out, int32_t *err_word, void *stream);
+
+/*
+ * The reference chunk score for every chunk at once (lookahead.py:82-106):
+ * scores[c] = mean_n sigmoid(sum_h relu(q[n,h,:] . keys[c,:]) * w[n,h]);
+ * q fp32 [n_rows][n_heads][dim], w fp32 [n_rows][n_heads], keys fp32
+ * [n_chunks][dim].
+ */
+SNAPMIND_API int snapmind_indexer_score_ref(const float *q, const float *w, int32_t n_rows, int32_t n_heads,
+                               const float *keys, int32_t n_chunks, int32_t dim, float *scores,
+                               void *stream);
+
+/*
+ * Sigmoid-gated chunk scores sigmoid(q . k * scale + bias) and the k best
+ * chunks per sequence (no reference counterpart: IndexerConfig.score_k exists
+ * but is never read, snapmind/core/config.py:92).  Order: score descending,
+ * then chunk id ascending (a stable descending sort).  q [batch][dim], keys
+ * [batch][max_chunks][dim] (dtype), n_chunks[b] (device, or n_chunks0 for all)
+ * chunks valid per sequence; out_idx int32 [batch][k] (-1 past the valid
+ * chunks), optional out_score [batch][k] and all_scores [batch][max_chunks].
+ * max_chunks <= 16384.
+ */
+SNAPMIND_API int snapmind_indexer_topk(const void *q, const void *keys, int dtype, const int32_t *n_chunks,
+                          int32_t n_chunks0, int32_t batch, int32_t max_chunks, int32_t dim, float scale,
+                          float bias, int32_t k, int32_t *out_idx, float *out_score, float *all_scores,
+                          void *stream);
+
+/*
+ * Sparse MLA decode attention over the positions of an attention sink
+ * (< sink), a recent window (>= len - window) and the selected chunks
+ * (selected [batch][k] chunk ids, -1 = unused), read from the paged latent
+ * pools (latent [blocks][block_size][kv_lora_rank], rope
+ * [blocks][block_size][rope_dim]) through the block tables.  Computes, per
+ * head, softmax(scale * (q_lat . c_t + q_pe . k_pe_t)) over those positions
+ * and the latent output sum_t p_t c_t into out [batch][n_heads][kv_lora_rank]
+ * — the attention of MultiHeadLatentAttention.forward
+ * (snapmind/layers/attention/mla.py:217-245) with the query absorbed into the
+ * latent space (q_lat = W_uk^T q_nope) and restricted to the selection.
+ * n_heads is a multiple of 16; splits > 1 need a zero-filled workspace of
+ * snapmind_sparse_mla_workspace_bytes(...) bytes.
+ */
+SNAPMIND_API int64_t snapmind_sparse_mla_workspace_bytes(int32_t batch, int32_t n_heads, int32_t kv_lora_rank,
+                                                         int32_t n_splits);
+SNAPMIND_API int snapmind_sparse_mla_decode(const void *q_lat, const void *q_pe, int dtype, const void *latent_pool,
+                               const void *rope_pool, const int32_t *block_tables, int64_t table_stride,
+                               int32_t table_width, const int32_t *seq_lens, const int32_t *selected,
+                               int32_t k, int32_t sink, int32_t window, float scale, int32_t batch,
+                               int32_t n_heads, int32_t kv_lora_rank, int32_t rope_dim, int32_t block_size,
+                               int32_t num_blocks, int32_t n_splits, void *out, void *workspace,
+                               int64_t workspace_bytes, int32_t *err_word, void *stream);
 
 /*
  * Paged GQA decode attention: one query token per sequence against the

@@ -4,9 +4,12 @@ Importing the package registers the B200 plugins in this package's registries
 (``snapmind_b200.registry.KV_CACHE`` …) under the reference's keys.  The CUDA
 library is loaded on first use; there is no CPU fallback.
 """
-from snapmind_b200 import kv_cache  # noqa: F401  (registers "paged")
+from snapmind_b200 import kv_cache  # noqa: F401  (registers "paged", "tiered")
+from snapmind_b200 import indexer  # noqa: F401  (registers "lookahead_sparse")
+from snapmind_b200.mla import MLALatentPool, PagedLatentDict
 from snapmind_b200.paged_pool import PagedKVPool
 from snapmind_b200.registry import ATTENTION, INDEXER, KV_CACHE, Registry, RegistryError
 
-__all__ = ["KV_CACHE", "ATTENTION", "INDEXER", "Registry", "RegistryError", "PagedKVPool"]
+__all__ = ["KV_CACHE", "ATTENTION", "INDEXER", "Registry", "RegistryError", "PagedKVPool", "MLALatentPool",
+           "PagedLatentDict"]
 __version__ = "0.1.0"

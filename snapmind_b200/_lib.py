@@ -68,6 +68,22 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _i64, _i32, _p, _p, _i32, _i32, _p, _p, _i32, _p, _p],
     ),
     "snapmind_kv_concat": (_int, [_p, _i32, _i32, _i32, _int, _p, _p, _i64, _p]),
+    "snapmind_indexer_pool_chunks": (
+        _int,
+        [_p, _int, _i64, _i32, _p, _i64, _i32, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p, _int, _i32,
+         _p, _p, _p],
+    ),
+    "snapmind_indexer_score_ref": (_int, [_p, _p, _i32, _i32, _p, _i32, _i32, _p, _p]),
+    "snapmind_indexer_topk": (
+        _int,
+        [_p, _p, _int, _p, _i32, _i32, _i32, _i32, _f32, _f32, _i32, _p, _p, _p, _p],
+    ),
+    "snapmind_sparse_mla_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32]),
+    "snapmind_sparse_mla_decode": (
+        _int,
+        [_p, _p, _int, _p, _p, _p, _i64, _i32, _p, _p, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _i32,
+         _i32, _i32, _i32, _p, _p, _i64, _p, _p],
+    ),
     "snapmind_paged_gqa_decode_split_tokens": (_i32, [_i32, _i32, _i32, _i32]),
     "snapmind_paged_gqa_decode_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "snapmind_paged_gqa_decode": (

@@ -39,6 +39,7 @@ struct AppendParams {
   int32_t n_layers, batch, n_tokens, n_heads, block_size, num_blocks;
   int32_t row_bytes_in, row_bytes_out;  // head_dim * element size
   int32_t head_dim;
+  int32_t nkv;  // 2 for K and V pools, 1 for a single pool (v pointers NULL)
   int32_t* err;
 };
 
@@ -67,7 +68,7 @@ template <int W>
 __global__ void __launch_bounds__(256) kv_append_copy_kernel(AppendParams p) {
   using V = typename VecT<W>::type;
   const int vpr = p.row_bytes_out / W;  // vectors per row
-  const int64_t rows = (int64_t)p.n_layers * p.batch * p.n_tokens * 2 * p.n_heads;
+  const int64_t rows = (int64_t)p.n_layers * p.batch * p.n_tokens * p.nkv * p.n_heads;
   const int64_t total = rows * vpr;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
@@ -75,7 +76,7 @@ __global__ void __launch_bounds__(256) kv_append_copy_kernel(AppendParams p) {
     const int v = (int)(idx - r * vpr);
     int64_t q = r;
     const int h = (int)(q % p.n_heads); q /= p.n_heads;
-    const int kv = (int)(q & 1); q >>= 1;
+    const int kv = (int)(q % p.nkv); q /= p.nkv;
     const int t = (int)(q % p.n_tokens); q /= p.n_tokens;
     const int b = (int)(q % p.batch);
     const int layer = (int)(q / p.batch);
@@ -92,7 +93,7 @@ __global__ void __launch_bounds__(256) kv_append_copy_kernel(AppendParams p) {
 template <typename Tin, typename Tout>
 __global__ void __launch_bounds__(256) kv_append_convert_kernel(AppendParams p) {
   const int D = p.head_dim;
-  const int64_t rows = (int64_t)p.n_layers * p.batch * p.n_tokens * 2 * p.n_heads;
+  const int64_t rows = (int64_t)p.n_layers * p.batch * p.n_tokens * p.nkv * p.n_heads;
   const int64_t total = rows * D;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
@@ -100,7 +101,7 @@ __global__ void __launch_bounds__(256) kv_append_convert_kernel(AppendParams p) 
     const int d = (int)(idx - r * D);
     int64_t q = r;
     const int h = (int)(q % p.n_heads); q /= p.n_heads;
-    const int kv = (int)(q & 1); q >>= 1;
+    const int kv = (int)(q % p.nkv); q /= p.nkv;
     const int t = (int)(q % p.n_tokens); q /= p.n_tokens;
     const int b = (int)(q % p.batch);
     const int layer = (int)(q / p.batch);
@@ -141,6 +142,7 @@ struct GatherParams {
   int32_t seq_len0;
   int32_t n_layers, batch, n_heads, block_size, num_blocks;
   int32_t row_bytes;
+  int32_t nkv;  // 2 for K and V pools, 1 for a single pool
   int32_t* err;
 };
 
@@ -216,13 +218,13 @@ __global__ void __launch_bounds__(kGatherThreads) kv_gather_kernel(GatherParams 
     if (blockIdx.x == 0 && threadIdx.x == 0) flag_error(p.err, SNAPMIND_DEVERR_TABLE);
     return;
   }
-  const int64_t items = (int64_t)p.n_layers * 2 * total_blocks;
+  const int64_t items = (int64_t)p.n_layers * p.nkv * total_blocks;
   const int vrow = p.row_bytes / W;  // vectors per token row
   for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
     const int gb = (int)(it % total_blocks);
     const int rest = (int)(it / total_blocks);
-    const int kv = rest & 1;
-    const int layer = rest >> 1;
+    const int kv = rest % p.nkv;
+    const int layer = rest / p.nkv;
     const int b = upper_bound_i32(cu_blocks, p.batch + 1, gb) - 1;
     const int j = gb - cu_blocks[b];
     const int len = cu_tok[b + 1] - cu_tok[b];
@@ -482,10 +484,11 @@ int snapmind_kv_append(void* k_pool, void* v_pool, int pool_dtype, int64_t pool_
   SNAPMIND_CHECK_ARG(n_layers >= 0 && batch >= 0 && n_tokens >= 0 && n_heads > 0 && head_dim > 0 &&
                          block_size > 0 && num_blocks > 0 && table_width >= 0,
                      "kv_append: bad sizes");
-  const int64_t rows = (int64_t)n_layers * batch * n_tokens * 2 * n_heads;
+  const int nkv = v_pool ? 2 : 1;
+  const int64_t rows = (int64_t)n_layers * batch * n_tokens * nkv * n_heads;
   if (rows == 0) return SNAPMIND_OK;
-  SNAPMIND_CHECK_ARG(k_pool && v_pool && k_new && v_new && block_tables,
-                     "kv_append: null pointer");
+  SNAPMIND_CHECK_ARG(k_pool && k_new && block_tables && ((v_pool == nullptr) == (v_new == nullptr)),
+                     "kv_append: null pointer (v_pool and v_new are both set or both NULL)");
   AppendParams p;
   p.pool[0] = static_cast<char*>(k_pool);
   p.pool[1] = static_cast<char*>(v_pool);
@@ -511,6 +514,7 @@ int snapmind_kv_append(void* k_pool, void* v_pool, int pool_dtype, int64_t pool_
   p.row_bytes_in = head_dim * esz_in;
   p.row_bytes_out = head_dim * esz_out;
   p.head_dim = head_dim;
+  p.nkv = nkv;
   p.err = err_word;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int max_grid = num_sms() * 8;
@@ -557,7 +561,8 @@ int snapmind_kv_gather(const void* k_pool, const void* v_pool, int dtype, int64_
                          block_size > 0 && num_blocks > 0,
                      "kv_gather: bad sizes");
   if (n_layers == 0 || batch == 0) return SNAPMIND_OK;
-  SNAPMIND_CHECK_ARG(k_pool && v_pool && k_out && v_out && block_tables, "kv_gather: null pointer");
+  SNAPMIND_CHECK_ARG(k_pool && k_out && block_tables && ((v_pool == nullptr) == (v_out == nullptr)),
+                     "kv_gather: null pointer (v_pool and v_out are both set or both NULL)");
   GatherParams p;
   p.pool[0] = static_cast<const char*>(k_pool);
   p.pool[1] = static_cast<const char*>(v_pool);
@@ -578,6 +583,7 @@ int snapmind_kv_gather(const void* k_pool, const void* v_pool, int dtype, int64_
   p.block_size = block_size;
   p.num_blocks = num_blocks;
   p.row_bytes = head_dim * esz;
+  p.nkv = v_pool ? 2 : 1;
   p.err = err_word;
   const int vw = vec_width(p.row_bytes, reinterpret_cast<uintptr_t>(k_pool),
                            reinterpret_cast<uintptr_t>(v_pool), reinterpret_cast<uintptr_t>(k_out),

@@ -11,19 +11,18 @@ over one shared pool; this class is that extension, with all state on the GPU:
   ``snapmind_kv_reserve`` grows tables deterministically (ascending sequence
   order, blocks from the top of the stack).
 
-Host mirrors of the lengths and the free count let the pool raise
-``RuntimeError("PagedKVCache: out of blocks")`` before launching, as the
-reference does, and size gather outputs without a device sync.
+Block bookkeeping (tables, lengths, free stack, reserve/release) is in
+:class:`snapmind_b200.block_pool.BlockPool`.
 """
 from __future__ import annotations
 
-import numpy as np
 import torch
 
 from snapmind_b200 import _lib
+from snapmind_b200.block_pool import BlockPool
 
 
-class PagedKVPool:
+class PagedKVPool(BlockPool):
     def __init__(
         self,
         n_layers: int,
@@ -36,104 +35,15 @@ class PagedKVPool:
         dtype: torch.dtype = torch.bfloat16,
         device: torch.device | str | None = None,
     ):
-        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-        _lib.require_cuda(self.device)
-        _lib.load()
+        super().__init__(num_blocks, max_seqs, max_blocks_per_seq, block_size, device)
         self.n_layers, self.n_kv_heads, self.head_dim = n_layers, n_kv_heads, head_dim
-        self.num_blocks, self.max_seqs, self.block_size = num_blocks, max_seqs, block_size
-        self.max_blocks_per_seq = max_blocks_per_seq
         self.dtype = dtype
         self._dcode = _lib.dtype_code(dtype)
         shape = (n_layers, num_blocks, n_kv_heads, block_size, head_dim)
         self.k = torch.empty(shape, dtype=dtype, device=self.device)
         self.v = torch.empty(shape, dtype=dtype, device=self.device)
         self.layer_stride = num_blocks * n_kv_heads * block_size * head_dim
-        self.block_tables = torch.zeros((max_seqs, max_blocks_per_seq), dtype=torch.int32, device=self.device)
-        self.seq_lens = torch.zeros(max_seqs, dtype=torch.int32, device=self.device)
-        # free_stack[top-1] is popped first; initially block 0, then 1, ...
-        self.free_stack = torch.arange(num_blocks - 1, -1, -1, dtype=torch.int32, device=self.device)
-        self.free_top = torch.tensor([num_blocks], dtype=torch.int32, device=self.device)
-        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self._host_lens = np.zeros(max_seqs, dtype=np.int64)
-        self._host_free = num_blocks
         self._workspace: torch.Tensor | None = None
-        self._ws_key: tuple | None = None
-
-    # ------------------------------------------------------------------ state
-    def _stream(self) -> int:
-        return _lib.stream_handle(self.device)
-
-    def set_state(self, tables: np.ndarray, lens: np.ndarray, free_stack: np.ndarray) -> None:
-        """Install block tables, lengths and the free stack (e.g. a shuffled pool)."""
-        tables = np.asarray(tables)
-        b, w = tables.shape
-        if b > self.max_seqs or w > self.max_blocks_per_seq:
-            raise ValueError("tables larger than the pool's table capacity")
-        if tables.size and (tables.min() < 0 or tables.max() >= self.num_blocks):
-            raise ValueError("block id outside the pool")
-        full = np.zeros((self.max_seqs, self.max_blocks_per_seq), dtype=np.int32)
-        full[:b, :w] = tables
-        self.block_tables.copy_(torch.from_numpy(full))
-        lens_full = np.zeros(self.max_seqs, dtype=np.int32)
-        lens_full[: len(lens)] = lens
-        self.seq_lens.copy_(torch.from_numpy(lens_full))
-        self._host_lens = lens_full.astype(np.int64)
-        fs = np.zeros(self.num_blocks, dtype=np.int32)
-        fs[: len(free_stack)] = free_stack
-        self.free_stack.copy_(torch.from_numpy(fs))
-        self.free_top.fill_(len(free_stack))
-        self._host_free = len(free_stack)
-
-    @property
-    def host_lens(self) -> np.ndarray:
-        return self._host_lens
-
-    def check(self) -> None:
-        """Synchronise and raise if a kernel flagged an error on this pool."""
-        word = int(self.err.item())
-        if word:
-            self.err.zero_()
-            _lib.raise_device_error(word, "PagedKVPool")
-
-    # -------------------------------------------------------------- mutation
-    def reserve(self, n_new: int = 1, batch: int | None = None) -> None:
-        """Grow the first ``batch`` sequences by ``n_new`` tokens (tables + lengths)."""
-        batch = self.max_seqs if batch is None else batch
-        bs = self.block_size
-        lens = self._host_lens[:batch]
-        need = int(((lens + n_new + bs - 1) // bs - (lens + bs - 1) // bs).sum())
-        if need > self._host_free:
-            raise RuntimeError(_lib.OUT_OF_BLOCKS_MSG)
-        if batch and int(((lens + n_new + bs - 1) // bs).max()) > self.max_blocks_per_seq:
-            raise ValueError("sequence would outgrow its block table row")
-        status = _lib.load().snapmind_kv_reserve(
-            self.block_tables.data_ptr(), self.max_blocks_per_seq, self.max_blocks_per_seq,
-            self.seq_lens.data_ptr(), batch, n_new, bs,
-            self.free_stack.data_ptr(), self.free_top.data_ptr(), self.num_blocks,
-            self.err.data_ptr(), self._stream(),
-        )  # fmt: skip
-        _lib.check(status, "PagedKVPool.reserve")
-        self._host_lens[:batch] += n_new
-        self._host_free -= need
-
-    def release(self, seq_ids: list[int]) -> None:
-        """Return the blocks of finished sequences to the free stack."""
-        if not seq_ids:
-            return
-        if min(seq_ids) < 0 or max(seq_ids) >= self.max_seqs or len(set(seq_ids)) != len(seq_ids):
-            raise ValueError("release: sequence ids must be distinct and inside the pool")
-        ids = torch.tensor(seq_ids, dtype=torch.int32, device=self.device)
-        freed = int(sum((self._host_lens[s] + self.block_size - 1) // self.block_size for s in seq_ids))
-        status = _lib.load().snapmind_kv_release(
-            self.block_tables.data_ptr(), self.max_blocks_per_seq, self.max_blocks_per_seq,
-            self.seq_lens.data_ptr(), ids.data_ptr(), len(seq_ids), self.block_size,
-            self.free_stack.data_ptr(), self.free_top.data_ptr(), self.num_blocks,
-            self.err.data_ptr(), self._stream(),
-        )  # fmt: skip
-        _lib.check(status, "PagedKVPool.release")
-        for s in seq_ids:
-            self._host_lens[s] = 0
-        self._host_free += freed
 
     def append(self, layer: int | None, k_new: torch.Tensor, v_new: torch.Tensor, slot_starts=None,
                slot_start0: int | None = None) -> None:
@@ -158,13 +68,7 @@ class PagedKVPool:
         _, batch, n_heads, n_tokens, head_dim = k_new.shape
         if n_heads != self.n_kv_heads or head_dim != self.head_dim:
             raise ValueError(f"expected {self.n_kv_heads} heads of {self.head_dim}, got {tuple(k_new.shape)}")
-        if slot_starts is None:
-            starts_ptr, start0 = self.seq_lens.data_ptr(), -n_tokens
-        else:
-            starts_ptr = None if isinstance(slot_starts, int) else slot_starts.data_ptr()
-            start0 = slot_starts if isinstance(slot_starts, int) else 0
-        if slot_start0 is not None:
-            start0 = slot_start0
+        starts_ptr, start0 = self._slot_args(n_tokens, slot_starts, slot_start0)
         st = k_new.stride()
         status = _lib.load().snapmind_kv_append(
             self.k[base].data_ptr(), self.v[base].data_ptr(), self._dcode, self.layer_stride,

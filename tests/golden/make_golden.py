@@ -458,6 +458,115 @@ def make_tiered(out: Path):
     out.write_text(json.dumps(data, indent=1))
 
 
+MLA_CASES = [
+    # name, d_model, heads, kv_lora_rank, nope, rope, v_head, dtype, seed, store_weights
+    ("mla_tiny_f32", 16, 4, 8, 4, 4, 4, "f32", 51, True),
+    ("mla_small_f32", 64, 4, 32, 16, 8, 16, "f32", 52, True),
+    ("mla_deepseek_rank_bf16", 1024, 8, 512, 128, 64, 128, "bf16", 53, False),
+]
+MLA_STEPS = [(20, None), (1, 20), (1, 21), (3, None)]  # (new tokens, decode position or None)
+
+
+def make_mla(out_npz: Path, out_json: Path):
+    """Reference MLA forward with a dict kv_cache: per step the kv_proj rows it
+    appended, the cache contents after the step, and (small shapes) the weights
+    and outputs that pin the oracle's MLA attention math."""
+    import torch
+    from snapmind.layers.attention.mla import MultiHeadLatentAttention
+
+    arrays, meta = {}, []
+    for name, d_model, heads, rank, nope, rope, vdim, dt, seed, store_w in MLA_CASES:
+        torch.manual_seed(seed)
+        mla = MultiHeadLatentAttention(d_model=d_model, n_heads=heads, kv_lora_rank=rank, qk_nope_head_dim=nope,
+                                       qk_rope_head_dim=rope, v_head_dim=vdim, max_seq_len=256)
+        assert heads * vdim == d_model
+        with torch.no_grad():
+            mla.out_proj.weight.copy_(torch.eye(d_model))
+        if dt == "bf16":
+            mla = mla.to(torch.bfloat16)
+        enc = (lambda a: _bf16_bits(a)) if dt == "bf16" else (lambda a: a.detach().float().numpy())
+        if store_w:
+            for wname in ("kv_proj", "k_up_proj", "v_up_proj", "q_proj"):
+                arrays[f"{name}__w_{wname}"] = enc(getattr(mla, wname).weight)
+        cache: dict = {}
+        steps = []
+        for si, (n_new, pos) in enumerate(MLA_STEPS):
+            x = torch.from_numpy(randn(seed * 10 + si, (2, n_new, d_model)))
+            if dt == "bf16":
+                x = x.to(torch.bfloat16)
+            with torch.no_grad():
+                kv = mla.kv_proj(x)
+                pid = None if pos is None else torch.tensor([pos])
+                out, _ = mla(x, kv_cache=cache, position_ids=pid)
+            arrays[f"{name}__s{si}_x"] = enc(x)
+            arrays[f"{name}__s{si}_latent_new"] = enc(kv[..., :rank])
+            arrays[f"{name}__s{si}_rope_new"] = enc(kv[..., rank:])
+            arrays[f"{name}__s{si}_out"] = enc(out)
+            steps.append({"n_new": n_new, "position": pos,
+                          "k_shape": list(cache["k"].shape), "k_rope_shape": list(cache["k_rope"].shape),
+                          "k_bits": digest(_bf16_bits(cache["k"])) if dt == "bf16" else digest(cache["k"].numpy()),
+                          "k_rope_bits": digest(_bf16_bits(cache["k_rope"])) if dt == "bf16"
+                          else digest(cache["k_rope"].numpy())})
+        meta.append({"name": name, "d_model": d_model, "n_heads": heads, "kv_lora_rank": rank,
+                     "qk_nope_head_dim": nope, "qk_rope_head_dim": rope, "v_head_dim": vdim, "dtype": dt,
+                     "seed": seed, "rope_theta": 10000.0, "max_seq_len": 256, "weights_stored": store_w,
+                     "steps": steps})
+    np.savez_compressed(out_npz, **arrays)
+    out_json.write_text(json.dumps(meta, indent=1))
+
+
+INDEXER_CASES = [
+    # name, d_model, kv_lora_rank, n_heads, n_chunks, chunk, dtype, seed, store_weights
+    ("indexer_small_f32", 64, 32, 4, 12, 16, "f32", 61, True),
+    ("indexer_default_f32", 2048, 512, 4, 40, 64, "f32", 62, False),
+    ("indexer_default_bf16", 2048, 512, 4, 24, 64, "bf16", 63, False),
+]
+
+
+def make_indexer(out_npz: Path, out_json: Path):
+    """Reference LookaheadSparseIndexer: frozen keys and scores.  Weights come from
+    torch.manual_seed(seed) then the module constructor (stored for small cases)."""
+    import torch
+    from snapmind.layers.indexer.lookahead import LookaheadSparseIndexer
+
+    arrays, meta = {}, []
+    for name, d_model, rank, heads, n_chunks, chunk, dt, seed, store_w in INDEXER_CASES:
+        torch.manual_seed(seed)
+        idx = LookaheadSparseIndexer(d_model=d_model, n_layers=24, kv_lora_rank=rank, n_indexer_heads=heads)
+        tdt = torch.bfloat16 if dt == "bf16" else torch.float32
+        idx = idx.to(tdt)
+        enc = (lambda a: _bf16_bits(a)) if dt == "bf16" else (lambda a: a.detach().float().numpy())
+        if store_w:
+            for wname in ("q_down_proj", "q_up_proj", "w_proj"):
+                arrays[f"{name}__w_{wname}"] = enc(getattr(idx, wname).weight)
+        # chunk keys: (chunk tokens, rank + 64) like MLA latent+rope rows; chunk 3 absent
+        key_states = {}
+        for c in range(n_chunks):
+            if c == 3:
+                continue
+            t = chunk if c < n_chunks - 1 else chunk // 2 + 1  # a partial last chunk
+            key_states[c] = torch.from_numpy(randn(seed * 1000 + c, (t, rank + 64))).to(tdt)
+        hidden = {lid: torch.from_numpy(randn(seed * 1000 + 500 + lid, (1, d_model))).to(tdt) for lid in (10, 12, 20, 5)}
+        with torch.no_grad():
+            uninit = idx.score(hidden, [0, 1])
+            idx.build_frozen_keys(key_states, list(range(n_chunks)))
+            ids = list(range(n_chunks)) + [n_chunks + 5]
+            scores = idx.score(hidden, ids)
+            fallback = idx.score({5: hidden[5]}, ids)  # no indexer layer present: min layer used
+        for c in sorted(idx._frozen_keys):
+            arrays[f"{name}__frozen_{c}"] = enc(idx._frozen_keys[c])
+        meta.append({
+            "name": name, "d_model": d_model, "kv_lora_rank": rank, "n_indexer_heads": heads, "n_chunks": n_chunks,
+            "chunk": chunk, "dtype": dt, "seed": seed, "weights_stored": store_w,
+            "key_states": {str(c): list(v.shape) for c, v in key_states.items()},
+            "uninitialized": {str(c): float(v) for c, v in uninit.items()},
+            "scores": {str(c): float(v.float()) for c, v in scores.items()},
+            "fallback_scores": {str(c): float(v.float()) for c, v in fallback.items()},
+        })
+    np.savez_compressed(out_npz, **arrays)
+    out_json.write_text(json.dumps(meta, indent=1))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SNAPMIND_REFERENCE", "/root/reference"))
@@ -470,6 +579,8 @@ def main():
     make_paged_batched(HERE / "paged_batched.json")
     make_gqa(HERE / "gqa_decode.npz", HERE / "gqa_decode.json")
     make_tiered(HERE / "tiered_ops.json")
+    make_mla(HERE / "mla.npz", HERE / "mla.json")
+    make_indexer(HERE / "indexer.npz", HERE / "indexer.json")
     print("golden vectors written to", HERE)
 
 

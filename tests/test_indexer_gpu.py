@@ -1,0 +1,166 @@
+"""Indexer, chunk selection and sparse MLA decode on the B200 against the
+reference indexer (golden) and the oracle."""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from inputs import randn
+from oracle import bf16
+from oracle import indexer as oidx
+from oracle import mla as omla
+from oracle import paged
+from replay import GOLDEN
+from test_oracle_golden import indexer_key_states
+
+pytestmark = pytest.mark.gpu
+
+
+def _cases():
+    return json.loads((GOLDEN / "indexer.json").read_text())
+
+
+@pytest.mark.parametrize("case", _cases(), ids=lambda m: m["name"])
+def test_lookahead_indexer_matches_reference(cuda_device, case):
+    from snapmind_b200.indexer import LookaheadSparseIndexer
+
+    arrays = np.load(GOLDEN / "indexer.npz")
+    dt = torch.bfloat16 if case["dtype"] == "bf16" else torch.float32
+    torch.manual_seed(case["seed"])  # same construction as the reference -> same weights
+    idx = LookaheadSparseIndexer(d_model=case["d_model"], n_layers=24, kv_lora_rank=case["kv_lora_rank"],
+                                 n_indexer_heads=case["n_indexer_heads"]).to("cuda", dt)
+    if case["weights_stored"]:
+        for wname in ("q_down_proj", "q_up_proj", "w_proj"):
+            np.testing.assert_array_equal(getattr(idx, wname).weight.detach().float().cpu().numpy(),
+                                          arrays[f"{case['name']}__w_{wname}"])
+    ks, hidden = indexer_key_states(case)
+    ks_t = {c: torch.from_numpy(k).cuda().to(dt) for c, k in ks.items()}
+    hid_t = {lid: torch.from_numpy(h).cuda().to(dt) for lid, h in hidden.items()}
+    assert {c: float(v) for c, v in idx.score(hid_t, [0, 1]).items()} == {0: 0.5, 1: 0.5}
+    idx.build_frozen_keys(ks_t, list(range(case["n_chunks"])))
+    tol = 1e-6 if case["dtype"] == "f32" else 8e-3
+    for c in ks:
+        ref = arrays[f"{case['name']}__frozen_{c}"]
+        ref = bf16.bf16_to_f32(ref) if case["dtype"] == "bf16" else ref
+        np.testing.assert_allclose(idx._frozen_keys[c].cpu().numpy(), ref, rtol=tol, atol=tol)
+    ids = [int(c) for c in case["scores"]]
+    stol = 1e-5 if case["dtype"] == "f32" else 2e-2
+    got = idx.score(hid_t, ids)
+    for c in ids:
+        assert float(got[c]) == pytest.approx(case["scores"][str(c)], abs=stol), c
+    fb = idx.score({5: hid_t[5]}, ids)
+    for c in ids:
+        assert float(fb[c]) == pytest.approx(case["fallback_scores"][str(c)], abs=stol), c
+
+
+def _latent_pool(B, lens, bs=64, R=512, P=64, seed=0, dtype=torch.bfloat16):
+    """An MLALatentPool with seeded rows on shuffled blocks, plus the oracle copy."""
+    from snapmind_b200.mla import MLALatentPool
+
+    lens = np.asarray(lens)
+    nbs = (lens + bs - 1) // bs
+    nb = int(nbs.sum()) + 3
+    perm = np.random.RandomState(seed).permutation(nb).astype(np.int32)
+    W = int(nbs.max())
+    tables = np.zeros((B, W), np.int32)
+    off = 0
+    for b in range(B):
+        tables[b, : nbs[b]] = perm[off : off + nbs[b]]
+        off += nbs[b]
+    lat = bf16.round_to_bf16(randn(seed + 1, (nb, bs, R)))
+    rope = bf16.round_to_bf16(randn(seed + 2, (nb, bs, P)))
+    pool = MLALatentPool(1, nb, B, W, block_size=bs, kv_lora_rank=R, rope_dim=P, dtype=dtype)
+    pool.latent[0, :, 0].copy_(torch.from_numpy(lat).to(dtype))
+    pool.rope[0, :, 0].copy_(torch.from_numpy(rope).to(dtype))
+    pool.set_state(tables, lens, perm[off:])
+    return pool, lat, rope, tables
+
+
+def _seq_rows(arr, tables, b, n, bs):
+    blocks = [int(x) for x in tables[b][: (n + bs - 1) // bs]]
+    return np.concatenate([arr[p] for p in blocks], axis=0)[:n] if n else arr[:0].reshape(0, arr.shape[-1])
+
+
+def test_chunk_selector_keys_and_stable_topk(cuda_device):
+    from snapmind_b200.indexer import ChunkSelector
+
+    B, bs = 3, 64
+    lens = [64 * 40 + 17, 64 * 3, 64 * 50]
+    pool, lat, rope, tables = _latent_pool(B, lens, bs=bs, seed=5)
+    sel = ChunkSelector(pool, d_model=256, index_dim=128, seed=1)
+    n_chunks = [(n + bs - 1) // bs for n in lens]
+    sel.update_keys(0, 0, max(n_chunks), batch=B)
+    wk = sel.w_k.float().cpu().numpy().astype(np.float64)
+    for b in range(B):
+        rows = _seq_rows(lat, tables, b, lens[b], bs)
+        for c in range(n_chunks[b]):
+            want = wk @ rows[c * bs:(c + 1) * bs].astype(np.float64).mean(axis=0)
+            np.testing.assert_allclose(sel.keys[b, c].cpu().numpy(), want, rtol=1e-4, atol=1e-4)
+    hidden = torch.from_numpy(randn(9, (B, 256))).cuda()
+    q = sel.query(hidden)
+    nct = torch.tensor(n_chunks, dtype=torch.int32, device="cuda")
+    idx, sc, full = sel.select(q, nct, k=32, all_scores=True)
+    torch.cuda.synchronize()
+    for b in range(B):
+        s_all = full[b, : n_chunks[b]].cpu().numpy()
+        # bit-exact: the stable descending order of the scores the kernel reports
+        assert idx[b].cpu().numpy().tolist() == oidx.stable_topk(s_all, 32).tolist()
+        want = oidx.sigmoid_scores(q[b].cpu().numpy(), sel.keys[b, : n_chunks[b]].cpu().numpy(),
+                                   128 ** -0.5, sel.bias)
+        np.testing.assert_allclose(s_all, want, rtol=1e-5, atol=1e-6)
+        valid = idx[b][idx[b] >= 0].cpu().numpy()
+        np.testing.assert_allclose(sc[b, : len(valid)].cpu().numpy(), s_all[valid], rtol=0, atol=0)
+
+
+def test_topk_tie_break_on_equal_scores(cuda_device):
+    from snapmind_b200 import _lib
+
+    B, C, D, k = 2, 100, 8, 10
+    keys = torch.zeros((B, C, D), device="cuda")
+    keys[:, ::7, 0] = 1.0  # chunks 0, 7, 14, ... tie at the top score, the rest tie below
+    q = torch.ones((B, D), device="cuda")
+    idx = torch.empty((B, k), dtype=torch.int32, device="cuda")
+    rc = _lib.load().snapmind_indexer_topk(q.data_ptr(), keys.data_ptr(), 0, None, C, B, C, D, 1.0, 0.0, k,
+                                           idx.data_ptr(), None, None, _lib.stream_handle())
+    _lib.check(rc, "topk")
+    want = [0, 7, 14, 21, 28, 35, 42, 49, 56, 63]
+    assert idx.cpu().tolist() == [want, want]
+
+
+@pytest.mark.parametrize("sink,window,n_splits", [(4, 1024, 4), (0, 0, 1), (4, 200, 3), (70, 5000, 2)])
+def test_sparse_mla_decode_matches_oracle(cuda_device, sink, window, n_splits):
+    B, H, R, P, bs, k = 4, 32, 512, 64, 64, 8
+    lens = [64 * 30 + 5, 700, 64 * 20, 1]
+    pool, lat, rope, tables = _latent_pool(B, lens, bs=bs, seed=11)
+    rng = np.random.RandomState(3)
+    selected = np.full((B, k), -1, np.int32)
+    for b in range(B):
+        nc = (lens[b] + bs - 1) // bs
+        picks = rng.randint(0, nc + 2, size=k - 2)  # some past the end, some repeated
+        selected[b, : k - 2] = picks
+    q_lat = bf16.round_to_bf16(randn(21, (B, H, R)) * 0.05)
+    q_pe = bf16.round_to_bf16(randn(22, (B, H, P)) * 0.05)
+    scale = (128 + 64) ** -0.5
+    out = pool.sparse_decode(0, torch.from_numpy(q_lat).cuda().to(torch.bfloat16),
+                             torch.from_numpy(q_pe).cuda().to(torch.bfloat16),
+                             torch.from_numpy(selected).cuda(), sink=sink, window=window, scale=scale,
+                             n_splits=n_splits)
+    pool.check()
+    got = out.float().cpu().numpy()
+    for b in range(B):
+        rows_c = _seq_rows(lat, tables, b, lens[b], bs)
+        rows_p = _seq_rows(rope, tables, b, lens[b], bs)
+        sel_b = [int(c) for c in selected[b] if 0 <= c < (lens[b] + bs - 1) // bs]
+        pos = omla.sparse_positions(lens[b], sel_b, bs, sink, window)
+        if len(pos) == 0:
+            np.testing.assert_array_equal(got[b], 0)
+            continue
+        want = omla.sparse_mla_decode(q_lat[b], q_pe[b], rows_c, rows_p, pos, scale)
+        np.testing.assert_allclose(got[b], want, rtol=2e-2, atol=2e-2)
+    # the same call again reuses the workspace tickets
+    out2 = pool.sparse_decode(0, torch.from_numpy(q_lat).cuda().to(torch.bfloat16),
+                              torch.from_numpy(q_pe).cuda().to(torch.bfloat16),
+                              torch.from_numpy(selected).cuda(), sink=sink, window=window, scale=scale,
+                              n_splits=n_splits)
+    assert torch.equal(out, out2)

@@ -146,3 +146,133 @@ def test_tiered_oracle_replays_reference(scenario):
         state_of=lambda c: (c.hot_set, c.chunks.keys(), c.chunk_layout(), c.total_tokens),
         entry_arrays=entry_arrays,
     )
+
+
+# ---------------------------------------------------------------------------
+# MLA: oracle attention math and latent cache semantics against the reference
+# ---------------------------------------------------------------------------
+from oracle import mla as omla  # noqa: E402
+
+
+def load_mla():
+    return json.loads((GOLDEN / "mla.json").read_text()), np.load(GOLDEN / "mla.npz")
+
+
+def mla_array(arrays, m, key):
+    a = arrays[f"{m['name']}__{key}"]
+    return bf16.bf16_to_f32(a) if m["dtype"] == "bf16" else a.astype(np.float32)
+
+
+@pytest.mark.parametrize("case", json.loads((GOLDEN / "mla.json").read_text()), ids=lambda m: m["name"])
+def test_mla_cache_is_concatenation_of_appended_rows(case):
+    meta, arrays = load_mla()
+    lat, rope = [], []
+    for si, st in enumerate(case["steps"]):
+        lat.append(mla_array(arrays, case, f"s{si}_latent_new"))
+        rope.append(mla_array(arrays, case, f"s{si}_rope_new"))
+        k = np.concatenate(lat, axis=1)
+        kr = np.concatenate(rope, axis=1)
+        assert list(k.shape) == st["k_shape"] and list(kr.shape) == st["k_rope_shape"]
+        if case["dtype"] == "bf16":
+            assert digest(bf16.f32_to_bf16(k)) == st["k_bits"]
+            assert digest(bf16.f32_to_bf16(kr)) == st["k_rope_bits"]
+        else:
+            assert digest(k) == st["k_bits"] and digest(kr) == st["k_rope_bits"]
+
+
+@pytest.mark.parametrize("case", [m for m in json.loads((GOLDEN / "mla.json").read_text()) if m["weights_stored"]],
+                         ids=lambda m: m["name"])
+def test_oracle_mla_forward_matches_reference(case):
+    meta, arrays = load_mla()
+    w = {k: mla_array(arrays, case, f"w_{k}") for k in ("kv_proj", "k_up_proj", "v_up_proj", "q_proj")}
+    w["out_proj"] = np.eye(case["d_model"])
+    cache: dict = {}
+    for si, st in enumerate(case["steps"]):
+        x = mla_array(arrays, case, f"s{si}_x")
+        pid = None if st["position"] is None else [st["position"]]
+        out = omla.mla_forward(x, w, case, cache, pid)
+        np.testing.assert_allclose(out, mla_array(arrays, case, f"s{si}_out"), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("case", [m for m in json.loads((GOLDEN / "mla.json").read_text()) if m["weights_stored"]],
+                         ids=lambda m: m["name"])
+def test_absorbed_unrotated_decode_equals_reference_decode_math(case):
+    """The B200 decode form (absorbed q, raw rope) equals the reference decode math."""
+    meta, arrays = load_mla()
+    H, R, dn, dr, dv = (case[k] for k in ("n_heads", "kv_lora_rank", "qk_nope_head_dim", "qk_rope_head_dim", "v_head_dim"))
+    w = {k: mla_array(arrays, case, f"w_{k}").astype(np.float64) for k in ("kv_proj", "k_up_proj", "v_up_proj", "q_proj")}
+    w["out_proj"] = np.eye(case["d_model"])
+    cache: dict = {}
+    for si, st in enumerate(case["steps"]):
+        x = mla_array(arrays, case, f"s{si}_x").astype(np.float64)
+        pid = None if st["position"] is None else [st["position"]]
+        ref = omla.mla_forward(x, w, case, cache, pid)
+        if pid is None:
+            continue
+        q = x @ w["q_proj"].T  # (B, 1, H*(dn+dr))
+        qn = q[:, 0, : H * dn].reshape(-1, H, dn)
+        qp = q[:, 0, H * dn:].reshape(-1, H, dr)
+        q_lat = omla.absorb_query(qn, w["k_up_proj"], H, dn)
+        T = cache["k"].shape[1]
+        for b in range(x.shape[0]):
+            o_lat = omla.sparse_mla_decode(q_lat[b], qp[b], cache["k"][b], cache["k_rope"][b], np.arange(T),
+                                           (dn + dr) ** -0.5)
+            out = np.einsum("hr,hvr->hv", o_lat, w["v_up_proj"].reshape(H, dv, R)).reshape(-1)
+            # equal up to the float32 rounding of the rotation tables
+            np.testing.assert_allclose(out, ref[b, 0], rtol=1e-6, atol=1e-9)
+
+
+# ---------------------------------------------------------------------------
+# indexer oracle against the reference LookaheadSparseIndexer
+# ---------------------------------------------------------------------------
+from oracle import indexer as oidx  # noqa: E402
+
+
+def load_indexer():
+    return json.loads((GOLDEN / "indexer.json").read_text()), np.load(GOLDEN / "indexer.npz")
+
+
+def indexer_key_states(m):
+    """The chunk key states of tests/golden/make_golden.py::make_indexer (float32, bf16-rounded if bf16)."""
+    ks = {}
+    for c, shape in m["key_states"].items():
+        a = randn(m["seed"] * 1000 + int(c), tuple(shape))
+        ks[int(c)] = bf16.round_to_bf16(a) if m["dtype"] == "bf16" else a
+    hidden = {lid: randn(m["seed"] * 1000 + 500 + lid, (1, m["d_model"])) for lid in (10, 12, 20, 5)}
+    if m["dtype"] == "bf16":
+        hidden = {k: bf16.round_to_bf16(v) for k, v in hidden.items()}
+    return ks, hidden
+
+
+@pytest.mark.parametrize("case", json.loads((GOLDEN / "indexer.json").read_text()), ids=lambda m: m["name"])
+def test_oracle_frozen_keys_match_reference(case):
+    meta, arrays = load_indexer()
+    ks, _ = indexer_key_states(case)
+    tol = 1e-6 if case["dtype"] == "f32" else 8e-3
+    for c, k in ks.items():
+        ref = arrays[f"{case['name']}__frozen_{c}"]
+        ref = bf16.bf16_to_f32(ref) if case["dtype"] == "bf16" else ref
+        np.testing.assert_allclose(oidx.frozen_key(k, case["kv_lora_rank"]), ref, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("case", [m for m in json.loads((GOLDEN / "indexer.json").read_text()) if m["weights_stored"]],
+                         ids=lambda m: m["name"])
+def test_oracle_scores_match_reference(case):
+    meta, arrays = load_indexer()
+    ks, hidden = indexer_key_states(case)
+    w = {k: arrays[f"{case['name']}__w_{k}"].astype(np.float64) for k in ("q_down_proj", "q_up_proj", "w_proj")}
+    frozen = {c: oidx.frozen_key(k, case["kv_lora_rank"]) for c, k in ks.items()}
+    ids = [int(c) for c in case["scores"]]
+    assert oidx.score(hidden, [0, 1], frozen, w, initialized=False) == {0: 0.5, 1: 0.5}
+    got = oidx.score(hidden, ids, frozen, w)
+    for c in ids:
+        assert got[c] == pytest.approx(case["scores"][str(c)], abs=1e-6)
+    fb = oidx.score({5: hidden[5]}, ids, frozen, w)
+    for c in ids:
+        assert fb[c] == pytest.approx(case["fallback_scores"][str(c)], abs=1e-6)
+
+
+def test_stable_topk_breaks_ties_by_lower_chunk_id():
+    s = np.array([0.5, 0.7, 0.7, 0.1, 0.7, 0.5])
+    assert oidx.stable_topk(s, 4).tolist() == [1, 2, 4, 0]
+    assert oidx.stable_topk(s[:2], 4).tolist() == [1, 0, -1, -1]
