@@ -169,6 +169,48 @@ SNAPMIND_API int snapmind_kv_concat(const snapmind_segment *segs, int32_t n_segs
                        int64_t out_row_stride, void *stream);
 
 /*
+ * Batched tiered pool, placement step (the device-side form of the tiered
+ * cache's residency policy, snapmind/kv_cache/tiered.py:95-154, with the
+ * LRU + sink/window pinning of the many-sequence pool).  One CTA: every
+ * sequence grows by n_new tokens (a new chunk gets a slot; the chunk just
+ * completed is copied to outbound staging slot stage_out_base + b), then each
+ * request (req_seq[i], req_chunk[i]) that is not resident is admitted from
+ * inbound staging slot stage_in_base + i.  Slots come free ones first (by id),
+ * then least recently used by (slot_last, slot id) among unpinned chunks;
+ * chunk 0, chunks overlapping the last `window` tokens and the active chunk
+ * are pinned.  Rebuilds tables [batch][max_chunks] (resident slots in chunk
+ * order) and table_lens, and writes the copy plan [max_plan][2] (src, dst
+ * slot) and its length.  req_* are HOST arrays of n_req <= 64 entries;
+ * n_slots <= 8192.  Pool exhaustion sets SNAPMIND_DEVERR_OUT_OF_BLOCKS.
+ */
+SNAPMIND_API int snapmind_tiered_plan(int32_t *slot_owner, int32_t *slot_last, int32_t *chunk_slot,
+                         int32_t *seq_lens, int32_t *tables, int32_t *table_lens, int32_t *plan,
+                         int32_t *plan_count, int32_t batch, int32_t max_chunks, int32_t n_slots,
+                         int32_t chunk, int32_t sink, int32_t window, int32_t step, int32_t n_new,
+                         int32_t stage_in_base, int32_t stage_out_base, int32_t max_plan,
+                         const int32_t *req_seq, const int32_t *req_chunk, int32_t n_req,
+                         int32_t *err_word, void *stream);
+
+/*
+ * Execute a tiered plan: copy slot src -> dst for every plan entry, every
+ * layer, K and V (slot_bytes bytes per slot and layer, layer_stride_bytes
+ * between layers).
+ */
+SNAPMIND_API int snapmind_tiered_move(void *k_pool, void *v_pool, int64_t layer_stride_bytes, int64_t slot_bytes,
+                         int32_t n_layers, const int32_t *plan, const int32_t *plan_count,
+                         int32_t max_plan, void *stream);
+
+/*
+ * Strided copy between host-pinned backing and device slots (height rows of
+ * width bytes; direction inferred from the pointers), issued with
+ * cudaMemcpy2DAsync on `stream` — one call moves a chunk's K (or V) rows of
+ * every layer.  Replaces the chunk `.to(device)` / `.to("cpu")` moves of the
+ * tiered cache (snapmind/kv_cache/tiered.py:108-118, 142-151).
+ */
+SNAPMIND_API int snapmind_copy_2d(void *dst, int64_t dst_pitch, const void *src, int64_t src_pitch, int64_t width,
+                     int64_t height, void *stream);
+
+/*
  * Frozen chunk keys of the lookahead indexer: for chunks
  * [chunk_begin, chunk_begin + chunk_count) of every sequence, the mean of the
  * chunk's rows (the first `width` columns of each pool row of row_width

@@ -68,6 +68,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _i64, _i32, _p, _p, _i32, _i32, _p, _p, _i32, _p, _p],
     ),
     "snapmind_kv_concat": (_int, [_p, _i32, _i32, _i32, _int, _p, _p, _i64, _p]),
+    "snapmind_tiered_plan": (
+        _int,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+         _p, _p, _i32, _p, _p],
+    ),
+    "snapmind_tiered_move": (_int, [_p, _p, _i64, _i64, _i32, _p, _p, _i32, _p]),
+    "snapmind_copy_2d": (_int, [_p, _i64, _p, _i64, _i64, _i64, _p]),
     "snapmind_indexer_pool_chunks": (
         _int,
         [_p, _int, _i64, _i32, _p, _i64, _i32, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p, _int, _i32,
