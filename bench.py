@@ -159,6 +159,13 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
     torch.cuda.set_device(dev)
     steps, warmup = args.steps, args.warmup
     seed = 1234 + 7919 * rank
+    if args.only in ("tiered", "mla"):
+        fn = run_tiered if args.only == "tiered" else run_mla_sparse
+        r = fn(args, dev, seed, dist, world)
+        return {"metric": METRIC, "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": steps,
+                "warmup": warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": {"workload": r["workload"]},
+                args.only: r}
     if args.only == "append_gather":
         ag = run_append_gather(args, dev, seed, dist, world)
         return {"metric": METRIC, "value": ag["value"], "unit": ag["unit"], "n_gpus": world, "steps": steps,
@@ -307,10 +314,219 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
             "d2h_bytes_per_step": int(d2h),
         },
         "kv_append_gather": ag,
+        "tiered": run_tiered(args, dev, seed, dist, world) if args.only == "all" else None,
+        "mla_sparse": run_mla_sparse(args, dev, seed, dist, world) if args.only == "all" else None,
         "gpu_launches": launches_per_step * steps,
         "clocks": clocks.summary(),
     }
     return line
+
+
+# ----------------------------------------------------------------------------- tiered (config 4)
+TIER_L, TIER_B, TIER_CTX, TIER_POOL, TIER_CHUNK, TIER_SINK, TIER_WINDOW, TIER_REQ = 32, 16, 32768, 1024, 64, 4, 1024, 8
+
+
+def run_tiered(args, dev, seed, dist, world) -> dict:
+    """Tiered KV pool at the Mistral-7B KV shape: 32 layers, 8 kv heads, head_dim 128, bf16;
+    sequences of 32768 tokens with all chunks in host-pinned backing; a device pool of
+    1024 chunks of 64 tokens (= 4096 blocks of 16 per layer); sink chunk + 1024-token
+    window pinned; LRU eviction; 8 seeded-random cold chunks re-fetched per step
+    (H2D one step ahead on a copy stream).  Reports decode tok/s with and without the
+    re-fetch and the overlap 1 - exposed copy time / copy time."""
+    import torch
+
+    from snapmind_b200.tiered_pool import TieredKVPool
+
+    B = args.tiered_batch
+    steps = min(args.steps, 100)
+    warmup = args.warmup
+    max_tokens = TIER_CTX + 2 * (steps + warmup) + 2 * TIER_CHUNK
+    pool = TieredKVPool(TIER_L, H, D, B, max_tokens, TIER_POOL, chunk=TIER_CHUNK, sink=TIER_SINK,
+                        window=TIER_WINDOW, n_requests=TIER_REQ, dtype=torch.bfloat16, device=dev)
+    # backing: one sequence's worth of seeded data replicated to every sequence
+    g = torch.Generator(device=dev).manual_seed(seed + 40)
+    n_chunks = TIER_CTX // TIER_CHUNK
+    per = pool.backing[0, 0].numel()
+    src = torch.randn((n_chunks, per), generator=g, device=dev).to(torch.bfloat16)
+    for b in range(B):
+        pool.backing[b, :n_chunks].view(n_chunks, per).copy_(src)
+    del src
+    rng = np.random.RandomState(seed + 41)
+    lens = np.full(B, TIER_CTX, np.int64)
+    pinned_per_seq = 1 + TIER_WINDOW // TIER_CHUNK
+    extra = (TIER_POOL - B * (pinned_per_seq + 1)) // B  # leave room for the first new chunks
+    resident = []
+    for b in range(B):
+        win = list(range(n_chunks - TIER_WINDOW // TIER_CHUNK, n_chunks))
+        old = sorted(rng.choice(np.arange(1, n_chunks - len(win)), size=extra, replace=False).tolist())
+        resident.append([0] + old + win)
+    pool.install(lens, resident)
+    q = torch.randn((TIER_L, B, HQ, D), generator=g, device=dev).to(torch.bfloat16)
+    kn = torch.randn((TIER_L, B, H, D), generator=g, device=dev).to(torch.bfloat16)
+    vn = torch.randn((TIER_L, B, H, D), generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty((TIER_L, B, HQ, D), dtype=torch.bfloat16, device=dev)
+
+    def run(n_steps: int, refetch: bool) -> float:
+        recent: list = []
+        nxt = pool.pick_requests(rng, TIER_REQ) if refetch else []
+        if nxt:
+            pool.prefetch(nxt)
+        barrier(dist)
+        torch.cuda.synchronize(dev)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(n_steps):
+            req = nxt
+            recent = (recent + req)[-4 * TIER_REQ:]
+            nxt = pool.pick_requests(rng, TIER_REQ, exclude=set(recent)) if refetch else []
+            pool.step(q, kn, vn, out, req, nxt)
+        t1.record()
+        torch.cuda.synchronize(dev)
+        barrier(dist)
+        return t0.elapsed_time(t1)
+
+    run(warmup, True)
+    ms_with = reduce_max(dist, run(steps, True), dev)
+    h2d0 = pool.h2d_bytes
+    ms_without = reduce_max(dist, run(steps, False), dev)
+    pool.check()
+    # copy time alone: the same 8-chunk prefetch, nothing else running
+    reqs = pool.pick_requests(rng, TIER_REQ)
+    torch.cuda.synchronize(dev)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(pool.copy_stream)
+    for _ in range(10):
+        pool.prefetch(reqs)
+    c1.record(pool.copy_stream)
+    torch.cuda.synchronize(dev)
+    copy_ms = c0.elapsed_time(c1) / 10
+    chunk_bytes = pool.chunk_host_bytes
+    exposed = max(0.0, (ms_with - ms_without) / steps)
+    res = {
+        "value": round(B * world * steps / (ms_with * 1e-3), 1),
+        "unit": "tok/s",
+        "workload": f"tiered pool, Mistral-7B KV shape: {TIER_L} layers, 8 kv / 32 q heads, head_dim 128, bf16; "
+                    f"{B} seqs x {TIER_CTX} tokens in host-pinned backing; device pool {TIER_POOL} chunks x "
+                    f"{TIER_CHUNK} tokens; sink chunk + {TIER_WINDOW}-token window pinned; LRU; "
+                    f"{TIER_REQ} seeded-random cold chunks re-fetched per step",
+        "batch_per_gpu": B,
+        "ms_per_step": round(ms_with / steps, 4),
+        "ms_per_step_without_refetch": round(ms_without / steps, 4),
+        "tok_s_without_refetch": round(B * world * steps / (ms_without * 1e-3), 1),
+        "h2d_bytes_per_step": int(TIER_REQ * chunk_bytes),
+        "h2d_gbs_copy_alone": round(TIER_REQ * chunk_bytes / (copy_ms * 1e-3) / 1e9, 1),
+        "copy_ms_per_step_alone": round(copy_ms, 4),
+        "overlap": round(1.0 - min(1.0, exposed / copy_ms), 4) if copy_ms > 0 else None,
+        "resident_tokens_per_seq": int(pool.table_lens.float().mean().item()),
+        "h2d_bytes_measured": int(h2d0),
+        "gpu_launches_per_step": 3 + TIER_L,
+    }
+    del pool
+    torch.cuda.empty_cache()
+    return res
+
+
+# ----------------------------------------------------------------------------- MLA + indexer (config 5)
+MLA_B, MLA_CTX, MLA_HEADS, MLA_RANK, MLA_ROPE, MLA_CHUNK, MLA_TOPK, MLA_DMODEL = 8, 131072, 128, 512, 64, 64, 32, 7168
+
+
+def run_mla_sparse(args, dev, seed, dist, world) -> dict:
+    """One MLA layer at DeepSeek shape (128 heads, kv_lora_rank 512, rope 64, bf16), 8 seqs
+    of 131072 tokens in the paged latent pool (block = 64-token chunk).  A step: reserve and
+    append one latent row per sequence, add the key of a chunk that just completed, score
+    all chunks (sigmoid(q.k/sqrt(128)+b) over 128-d projections) with a stable top-32, then
+    sparse MLA decode over the selected chunks + 4-token sink + 1024-token window.  Also the
+    full latent gather and the all-chunk key pooling in GB/s."""
+    import torch
+
+    from snapmind_b200.indexer import ChunkSelector
+    from snapmind_b200.mla import MLALatentPool
+
+    B = MLA_B
+    steps = min(args.steps, 100)
+    warmup = args.warmup
+    ctx_chunks = MLA_CTX // MLA_CHUNK
+    width = ctx_chunks + (steps + warmup) // MLA_CHUNK + 2
+    nb = B * width
+    pool = MLALatentPool(1, nb, B, width, block_size=MLA_CHUNK, kv_lora_rank=MLA_RANK, rope_dim=MLA_ROPE,
+                         dtype=torch.bfloat16, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed + 50)
+    pool.latent.normal_(generator=g)
+    pool.rope.normal_(generator=g)
+    perm = np.random.RandomState(seed + 51).permutation(nb).astype(np.int32)
+    tables = perm[: B * ctx_chunks].reshape(B, ctx_chunks)
+    pool.set_state(tables, np.full(B, MLA_CTX), perm[B * ctx_chunks:])
+    sel = ChunkSelector(pool, d_model=MLA_DMODEL, index_dim=128, seed=seed + 52)
+    sel.update_keys(0, 0, ctx_chunks, batch=B)
+    hidden = torch.randn((B, MLA_DMODEL), generator=g, device=dev).to(torch.bfloat16)
+    q_lat = (torch.randn((B, MLA_HEADS, MLA_RANK), generator=g, device=dev) * 0.05).to(torch.bfloat16)
+    q_pe = (torch.randn((B, MLA_HEADS, MLA_ROPE), generator=g, device=dev) * 0.05).to(torch.bfloat16)
+    lat_new = torch.randn((B, 1, MLA_RANK), generator=g, device=dev).to(torch.bfloat16)
+    rope_new = torch.randn((B, 1, MLA_ROPE), generator=g, device=dev).to(torch.bfloat16)
+    scale = (128 + 64) ** -0.5
+    launches = [0]
+
+    def step():
+        pool.reserve(1, batch=B)
+        pool.append(0, lat_new, rope_new)
+        length = int(pool.host_lens[0])  # every sequence has the same length here
+        launches[0] += 3
+        if length % MLA_CHUNK == 0:  # a chunk just completed: its key joins the index
+            sel.update_keys(0, length // MLA_CHUNK - 1, 1, batch=B)
+            launches[0] += 1
+        idx, _ = sel.select(sel.query(hidden), length // MLA_CHUNK, k=MLA_TOPK)
+        pool.sparse_decode(0, q_lat, q_pe, idx, sink=4, window=1024, scale=scale, n_splits=4)
+        launches[0] += 2
+
+    for _ in range(warmup):
+        step()
+    pool.check()
+    launches[0] = 0
+    barrier(dist)
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize(dev)
+    barrier(dist)
+    pool.check()
+    ms = reduce_max(dist, t0.elapsed_time(t1), dev)
+    # full latent gather and all-chunk key pooling (HBM-bound)
+    length = int(pool.host_lens[0])
+    lo = torch.empty((B, length, MLA_RANK), dtype=torch.bfloat16, device=dev)
+    ro = torch.empty((B, length, MLA_ROPE), dtype=torch.bfloat16, device=dev)
+    pool.gather(0, B, length, out=(lo, ro))  # warm
+    torch.cuda.synchronize(dev)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    e[0].record()
+    pool.gather(0, B, length, out=(lo, ro))
+    e[1].record()
+    sel.update_keys(0, 0, length // MLA_CHUNK, batch=B)
+    e[2].record()
+    torch.cuda.synchronize(dev)
+    gather_ms = e[0].elapsed_time(e[1])
+    pool_ms = e[1].elapsed_time(e[2])
+    gather_bytes = 2 * B * length * (MLA_RANK + MLA_ROPE) * 2  # read pool + write output
+    pool_bytes = B * (length // MLA_CHUNK) * MLA_CHUNK * MLA_RANK * 2
+    pk = peaks()
+    res = {
+        "value": round(B * world * steps / (ms * 1e-3), 1),
+        "unit": "tok/s (one MLA layer)",
+        "workload": f"MLA latent cache + indexer + sparse attention, one layer: {MLA_HEADS} heads, kv_lora_rank "
+                    f"{MLA_RANK}, rope {MLA_ROPE}, bf16, {B} seqs x {MLA_CTX} tokens, chunk {MLA_CHUNK}, "
+                    f"top-{MLA_TOPK} + 4-token sink + 1024-token window",
+        "ms_per_step": round(ms / steps, 4),
+        "latent_gather_gbs": round(gather_bytes / (gather_ms * 1e-3) / 1e9, 1),
+        "latent_gather_frac": round(gather_bytes / (gather_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+        "chunk_pool_gbs": round(pool_bytes / (pool_ms * 1e-3) / 1e9, 1),
+        "chunk_pool_frac": round(pool_bytes / (pool_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+        "gpu_launches": launches[0],
+    }
+    del pool, lo, ro
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_append_gather(args, dev, seed, dist, world) -> dict:
@@ -570,7 +786,8 @@ def main():
     ap.add_argument("--batch", type=int, default=DECODE_BATCH, help="decode sequences per GPU")
     ap.add_argument("--ag-batch", type=int, default=AG_BATCH, help="append/gather sequences per GPU")
     ap.add_argument("--layers", type=int, default=L)
-    ap.add_argument("--only", choices=["all", "decode", "append_gather"], default="all")
+    ap.add_argument("--only", choices=["all", "decode", "append_gather", "tiered", "mla"], default="all")
+    ap.add_argument("--tiered-batch", type=int, default=TIER_B)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup
     _set_workload(args.batch, args.ag_batch, args.layers)

@@ -38,48 +38,115 @@ struct PoolParams {
   int32_t* err;
 };
 
+constexpr int kPoolThreads = 512;
+constexpr int kPoolUnroll = 8;
+
+// Persistent: each CTA loops over (sequence, chunk) items.  The projection
+// matrix is staged once per CTA in shared memory (when it fits), the rows of a
+// chunk are summed by row groups with 16-byte loads (kPoolUnroll rows in
+// flight per thread), and the group partials are reduced in shared memory.
+// smem: [proj cache (optional)][mean: width][partials: groups x width]
 template <typename T, typename TP>
-__global__ void __launch_bounds__(256) indexer_pool_kernel(PoolParams p) {
-  extern __shared__ float mean[];  // [width]
-  const int c = p.chunk_begin + blockIdx.x;
-  const int b = blockIdx.y;
-  const int out_w = p.proj ? p.out_dim : p.width;
-  float* out = p.out + ((int64_t)b * p.max_chunks + c) * out_w;
-  // without lengths every chunk is full
-  const int n = p.seq_lens ? min(p.block_size, p.seq_lens[b] - c * p.block_size) : p.block_size;
-  if (c >= p.max_chunks) return;
-  if (n <= 0 || c >= p.table_width) {
-    for (int i = threadIdx.x; i < out_w; i += blockDim.x) out[i] = 0.f;
-    return;
+__global__ void __launch_bounds__(kPoolThreads) indexer_pool_kernel(PoolParams p, int cache_proj, int vec_ok) {
+  extern __shared__ __align__(16) unsigned char pool_smem[];
+  const int W = p.width;
+  const int64_t proj_elems = cache_proj ? (int64_t)p.out_dim * W : 0;
+  TP* wcache = reinterpret_cast<TP*>(pool_smem);
+  float* mean = reinterpret_cast<float*>(pool_smem + ((proj_elems * (int64_t)sizeof(TP) + 15) / 16) * 16);
+  float* part = mean + W;
+  const int tid = threadIdx.x;
+  if (cache_proj) {
+    const TP* P = reinterpret_cast<const TP*>(p.proj);
+    for (int64_t i = tid; i < proj_elems; i += kPoolThreads) wcache[i] = P[i];
   }
-  const int32_t phys = p.tables[(int64_t)b * p.table_stride + c];
-  if (phys < 0 || phys >= p.num_blocks) {
-    if (threadIdx.x == 0) flag_error(p.err, SNAPMIND_DEVERR_BLOCK_ID);
-    for (int i = threadIdx.x; i < out_w; i += blockDim.x) out[i] = 0.f;
-    return;
-  }
-  const T* rows = reinterpret_cast<const T*>(p.pool) + (int64_t)phys * p.block_size * p.row_width;
-  const float inv = 1.f / (float)n;
-  for (int d = threadIdx.x; d < p.width; d += blockDim.x) {
-    float s = 0.f;
-    for (int r = 0; r < n; ++r) s += Conv<T>::to_f(rows[(int64_t)r * p.row_width + d]);
-    mean[d] = s * inv;
-  }
-  __syncthreads();
-  if (!p.proj) {
-    for (int d = threadIdx.x; d < p.width; d += blockDim.x) out[d] = mean[d];
-    return;
-  }
-  // projection: one warp per output, lanes over the width
-  const TP* P = reinterpret_cast<const TP*>(p.proj);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int o = warp; o < p.out_dim; o += nw) {
-    const TP* prow = P + (int64_t)o * p.width;
-    float acc = 0.f;
-    for (int d = lane; d < p.width; d += 32) acc = fmaf(Conv<TP>::to_f(prow[d]), mean[d], acc);
+  constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte vector
+  const int n_vec = W / EPV;
+  const int groups = vec_ok ? kPoolThreads / n_vec : 1;
+  const int out_w = p.proj ? p.out_dim : W;
+  const int64_t items = (int64_t)p.batch * p.chunk_count;
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+    const int b = (int)(it / p.chunk_count);
+    const int c = p.chunk_begin + (int)(it - (int64_t)b * p.chunk_count);
+    float* out = p.out + ((int64_t)b * p.max_chunks + c) * out_w;
+    // without lengths every chunk is full
+    const int n = p.seq_lens ? min(p.block_size, p.seq_lens[b] - c * p.block_size) : p.block_size;
+    int32_t phys = -1;
+    if (n > 0 && c < p.table_width) phys = p.tables[(int64_t)b * p.table_stride + c];
+    if (n > 0 && c < p.table_width && (phys < 0 || phys >= p.num_blocks)) {
+      if (tid == 0) flag_error(p.err, SNAPMIND_DEVERR_BLOCK_ID);
+      phys = -1;
+    }
+    __syncthreads();  // previous item's mean/part reads are done (and the cache is loaded)
+    if (phys < 0) {
+      for (int i = tid; i < out_w; i += kPoolThreads) out[i] = 0.f;
+      continue;
+    }
+    const T* rows = reinterpret_cast<const T*>(p.pool) + (int64_t)phys * p.block_size * p.row_width;
+    const float inv = 1.f / (float)n;
+    if (vec_ok) {
+      const int j = tid % n_vec, g = tid / n_vec;
+      float acc[EPV];
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) out[o] = acc;
+      for (int e = 0; e < EPV; ++e) acc[e] = 0.f;
+      if (g < groups) {
+        for (int r0 = g; r0 < n; r0 += groups * kPoolUnroll) {
+          uint4 v[kPoolUnroll];
+#pragma unroll
+          for (int u = 0; u < kPoolUnroll; ++u) {
+            const int r = r0 + u * groups;
+            v[u] = r < n ? *reinterpret_cast<const uint4*>(rows + (int64_t)r * p.row_width + j * EPV)
+                         : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int u = 0; u < kPoolUnroll; ++u) {
+            const T* x = reinterpret_cast<const T*>(&v[u]);
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) acc[e] += Conv<T>::to_f(x[e]);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) part[g * W + j * EPV + e] = acc[e];
+      }
+      __syncthreads();
+      for (int d = tid; d < W; d += kPoolThreads) {
+        float s = 0.f;
+        for (int gg = 0; gg < groups; ++gg) s += part[gg * W + d];
+        mean[d] = s * inv;
+      }
+    } else {
+      for (int d = tid; d < W; d += kPoolThreads) {
+        float s = 0.f;
+        for (int r = 0; r < n; ++r) s += Conv<T>::to_f(rows[(int64_t)r * p.row_width + d]);
+        mean[d] = s * inv;
+      }
+    }
+    __syncthreads();
+    if (!p.proj) {
+      for (int d = tid; d < W; d += kPoolThreads) out[d] = mean[d];
+      continue;
+    }
+    // projection: 4 consecutive threads per output, each over a quarter of the
+    // width, reading at a per-thread rotation so that a warp spreads its loads
+    // over the banks
+    const TP* P = cache_proj ? wcache : reinterpret_cast<const TP*>(p.proj);
+    const int qw = (W + 3) / 4;
+    for (int base = 0; base < p.out_dim * 4; base += kPoolThreads) {  // uniform trip count (shuffles)
+      const int task = base + tid;
+      const bool active = task < p.out_dim * 4;
+      const int o = task >> 2, qd = task & 3;
+      const int d_lo = qd * qw, d_hi = min(W, d_lo + qw), n_d = active ? max(0, d_hi - d_lo) : 0;
+      const TP* prow = P + (int64_t)o * W + d_lo;
+      const float* mrow = mean + d_lo;
+      float a = 0.f;
+      int i = n_d > 0 ? o % n_d : 0;
+      for (int it2 = 0; it2 < n_d; ++it2) {
+        a = fmaf(Conv<TP>::to_f(prow[i]), mrow[i], a);
+        if (++i == n_d) i = 0;
+      }
+      a += __shfl_xor_sync(0xffffffffu, a, 1);
+      a += __shfl_xor_sync(0xffffffffu, a, 2);
+      if (active && qd == 0) out[o] = a;
+    }
   }
 }
 
@@ -130,19 +197,39 @@ __global__ void __launch_bounds__(kTopkThreads) indexer_topk_kernel(
   const T* qb = q + (int64_t)b * dim;
   const T* kb = keys + (int64_t)b * max_chunks * dim;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  // scores: one warp per chunk
-  for (int c = warp; c < sort_n; c += nw) {
-    unsigned long long key = 0ull;  // below every real key
-    if (c < nc) {
-      float dot = 0.f;
-      for (int d = lane; d < dim; d += 32) dot = fmaf(Conv<T>::to_f(qb[d]), Conv<T>::to_f(kb[(int64_t)c * dim + d]), dot);
+  // scores: each warp takes 8 chunks per pass so that 8 independent key rows are in flight
+  constexpr int kU = 8;
+  for (int c0 = warp * kU; c0 < sort_n; c0 += nw * kU) {
+    float dot[kU];
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-      const float s = 1.f / (1.f + expf(-(dot * scale + bias)));
-      if (lane == 0 && all_scores) all_scores[(int64_t)b * max_chunks + c] = s;
-      key = ((unsigned long long)ordered_bits(s) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)c);
+    for (int u = 0; u < kU; ++u) dot[u] = 0.f;
+    for (int d = lane; d < dim; d += 32) {
+      const float qd = Conv<T>::to_f(qb[d]);
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int c = c0 + u;
+        if (c < nc) dot[u] = fmaf(qd, Conv<T>::to_f(kb[(int64_t)c * dim + d]), dot[u]);
+      }
     }
-    if (lane == 0) skeys[c] = key;
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], off);
+    }
+    if (lane < kU) {
+      float mine = dot[0];
+#pragma unroll
+      for (int u = 1; u < kU; ++u)
+        if (lane == u) mine = dot[u];
+      const int c = c0 + lane;
+      unsigned long long key = 0ull;  // below every real key
+      if (c < nc) {
+        const float s = 1.f / (1.f + expf(-(mine * scale + bias)));
+        if (all_scores) all_scores[(int64_t)b * max_chunks + c] = s;
+        key = ((unsigned long long)ordered_bits(s) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)c);
+      }
+      if (c < sort_n) skeys[c] = key;
+    }
   }
   __syncthreads();
   // bitonic sort, descending
@@ -197,18 +284,29 @@ int snapmind_indexer_pool_chunks(const void* pool, int dtype, int64_t row_width,
   PoolParams p{static_cast<const char*>(pool), row_width, width, block_tables, table_stride, table_width,
                seq_lens, batch, block_size, num_blocks, chunk_begin, chunk_count, max_chunks,
                static_cast<const char*>(proj), out_dim, out, err_word};
-  dim3 grid(chunk_count, batch);
-  const size_t smem = sizeof(float) * width;
+  const int esz = dtype_size(dtype);
+  const int epv = 16 / esz;
+  const int n_vec = width / epv;
+  const int vec_ok = (width % epv == 0) && n_vec <= kPoolThreads && ((row_width * esz) % 16 == 0) &&
+                     ((reinterpret_cast<uintptr_t>(pool) & 15) == 0);
+  const int groups = vec_ok ? kPoolThreads / n_vec : 1;
+  const int pd = proj ? proj_dtype : SNAPMIND_DTYPE_F32;
+  const int64_t proj_bytes = proj ? (int64_t)out_dim * width * dtype_size(pd) : 0;
+  const int cache_proj = proj && proj_bytes <= 160 * 1024;
+  const size_t smem = (size_t)(cache_proj ? (proj_bytes + 15) / 16 * 16 : 0) + sizeof(float) * width * (1 + groups);
+  SNAPMIND_CHECK_ARG(smem <= 220 * 1024, "indexer_pool_chunks: width too large for shared memory");
+  const int64_t items = (int64_t)batch * chunk_count;
+  const int per_sm = smem > 110 * 1024 ? 1 : 2;
+  const int grid = (int)(items < (int64_t)num_sms() * per_sm ? items : (int64_t)num_sms() * per_sm);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto go = [&](auto kernel) -> int {
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return cuda_status(e, "indexer_pool smem attribute");
     }
-    kernel<<<grid, 256, smem, st>>>(p);
+    kernel<<<grid, kPoolThreads, smem, st>>>(p, cache_proj, vec_ok);
     return cuda_status(cudaGetLastError(), "indexer_pool launch");
   };
-  const int pd = proj ? proj_dtype : SNAPMIND_DTYPE_F32;
 #define SNAPMIND_POOL_CASE(TT, TPP) return go(indexer_pool_kernel<TT, TPP>)
   if (dtype == SNAPMIND_DTYPE_F32) {
     if (pd == SNAPMIND_DTYPE_F32) SNAPMIND_POOL_CASE(float, float);

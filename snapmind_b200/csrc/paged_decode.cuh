@@ -40,14 +40,16 @@ inline WorkspaceLayout workspace_layout(int batch, int n_q_heads, int n_kv_heads
 }
 
 // Tokens per split: about 16 CTAs per SM over the batch at a mean length of
-// max_seq_len / 2, rounded to whole 64-token tiles (and whole blocks).
+// max_seq_len / 2, at least 512 tokens (8 pipeline tiles, so the fill and the
+// per-CTA merge stay small next to the streaming), rounded to whole 64-token
+// tiles (and whole blocks).
 inline int default_split_tokens(int batch, int n_kv_heads, int max_seq_len, int block_size) {
   if (block_size <= 0) return 0;
   const int64_t work = (int64_t)(batch > 0 ? batch : 1) * (n_kv_heads > 0 ? n_kv_heads : 1) *
                        (max_seq_len > 0 ? max_seq_len : 1) / 2;
   const int64_t target = (int64_t)num_sms() * 16;
   int64_t split = (work + target - 1) / target;
-  if (split < 256) split = 256;
+  if (split < 512) split = 512;
   if (split > 8192) split = 8192;
   int64_t unit = block_size;
   if (64 % block_size == 0) unit = 64;

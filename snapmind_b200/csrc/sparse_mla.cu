@@ -20,6 +20,7 @@
 
 #include "common.cuh"
 #include "paged_decode.cuh"
+#include "sparse_mla.cuh"
 
 namespace snapmind {
 namespace {
@@ -27,22 +28,6 @@ namespace {
 constexpr int kHeadsPerCta = 16;
 constexpr int kThreads = 256;
 constexpr int kMaxChunkBits = 8192;  // chunks per sequence covered by the bitmaps
-
-struct SparseParams {
-  const void* q_lat;   // [B][H][R]
-  const void* q_pe;    // [B][H][P]
-  const void* latent;  // layer base: [blocks][bs][R]
-  const void* rope;    // layer base: [blocks][bs][P]
-  const int32_t* tables;
-  int64_t table_stride;
-  int32_t table_width;
-  const int32_t* seq_lens;
-  const int32_t* selected;  // [B][k] chunk ids, -1 = empty
-  int32_t k, sink, window;
-  float scale;
-  int32_t batch, n_heads, R, P, bs, num_blocks, n_splits;
-  DecodeParams dp;  // output, partials and tickets in the paged-decode layout (group = 16 heads)
-};
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) sparse_mla_kernel(SparseParams p) {
@@ -345,8 +330,9 @@ int snapmind_sparse_mla_decode(const void* q_lat, const void* q_pe, int dtype, c
                       sizeof(uint32_t) * 2 * (kMaxChunkBits / 32) + sizeof(int32_t) * kMaxChunkBits +
                       (size_t)block_size * (kv_lora_rank + rope_dim) * esz + 16;
   SNAPMIND_CHECK_ARG(smem <= 227 * 1024, "sparse_mla_decode: shared memory %zu exceeds the limit", smem);
-  dim3 grid(n_splits, groups, batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (sparse_mla_tc_supported(p, dtype)) return launch_sparse_mla_tc(p, dtype, st);
+  dim3 grid(n_splits, groups, batch);
   auto go = [&](auto kernel) -> int {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_status(e, "sparse_mla smem attribute");

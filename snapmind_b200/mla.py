@@ -86,29 +86,34 @@ class MLALatentPool(BlockPool):
         self._append_one(self.latent, latent_new, base, n_layers, starts_ptr, start0)
         self._append_one(self.rope, rope_new, base, n_layers, starts_ptr, start0)
 
-    def gather(self, layer: int, batch: int, seq_len: int | None = None):
+    def gather(self, layer: int, batch: int, seq_len: int | None = None, out=None):
         """Latent ``(B, T, R)`` and rope ``(B, T, P)`` of the first ``batch`` sequences
         of one layer; ``seq_len`` (all sequences) defaults to the pool lengths,
-        which must then be equal."""
+        which must then be equal.  ``out`` may pass preallocated (latent, rope)."""
         if seq_len is None:
             lens = self._host_lens[:batch]
             if batch and (lens != lens[0]).any():
                 raise ValueError("gather of a dense (B, T, R) view needs equal lengths")
             seq_len = int(lens[0]) if batch else 0
         outs = []
-        for pool, width in ((self.latent, self.kv_lora_rank), (self.rope, self.rope_dim)):
-            out = torch.empty((batch, seq_len, width), dtype=self.dtype, device=self.device)
+        for i, (pool, width) in enumerate(((self.latent, self.kv_lora_rank), (self.rope, self.rope_dim))):
+            if out is None:
+                o = torch.empty((batch, seq_len, width), dtype=self.dtype, device=self.device)
+            else:
+                o = out[i]
+                if o.shape != (batch, seq_len, width) or o.dtype != self.dtype or not o.is_contiguous():
+                    raise ValueError("gather output has the wrong shape, dtype or layout")
             if batch and seq_len:
                 status = _lib.load().snapmind_kv_gather(
                     pool[layer].data_ptr(), None, self._dcode, 0,
-                    out.data_ptr(), None, 0, out.numel(),
+                    o.data_ptr(), None, 0, o.numel(),
                     self.block_tables.data_ptr(), self.max_blocks_per_seq, 0, self.max_blocks_per_seq,
                     None, seq_len,
                     1, batch, 1, width, self.block_size, self.num_blocks,
                     self.err.data_ptr(), self._stream(),
                 )  # fmt: skip
                 _lib.check(status, "MLALatentPool.gather")
-            outs.append(out)
+            outs.append(o)
         return outs[0], outs[1]
 
 

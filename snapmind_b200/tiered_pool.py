@@ -219,8 +219,9 @@ class TieredKVPool:
         )  # fmt: skip
         _lib.check(status, "TieredKVPool.append")
         max_len = self.n_slots * self.chunk
-        split = split_tokens or self.lib.snapmind_paged_gqa_decode_split_tokens(self.B, self.H, max_len // 8,
-                                                                                self.chunk)
+        # split plan sized for the average resident length (the pool shared by the batch)
+        split = split_tokens or self.lib.snapmind_paged_gqa_decode_split_tokens(
+            self.B, self.H, max(self.chunk, 2 * self.n_slots * self.chunk // self.B), self.chunk)
         need = self.lib.snapmind_paged_gqa_decode_workspace_bytes(self.B, q.shape[2], self.H, self.D, max_len, split)
         if self._workspace is None or self._workspace.numel() < need:
             self._workspace = torch.zeros(need, dtype=torch.uint8, device=self.device)

@@ -164,3 +164,27 @@ def test_sparse_mla_decode_matches_oracle(cuda_device, sink, window, n_splits):
                               torch.from_numpy(selected).cuda(), sink=sink, window=window, scale=scale,
                               n_splits=n_splits)
     assert torch.equal(out, out2)
+
+
+@pytest.mark.parametrize("R,P,dt", [(512, 64, torch.float32), (256, 32, torch.bfloat16)])
+def test_sparse_mla_decode_cuda_core_path(cuda_device, R, P, dt):
+    """Shapes the tensor-core kernel does not take (fp32, other widths) run the CUDA-core kernel."""
+    B, H, bs, k = 3, 16, 64, 6
+    lens = [64 * 12 + 9, 300, 64 * 5]
+    pool, lat, rope, tables = _latent_pool(B, lens, bs=bs, R=R, P=P, seed=13, dtype=dt)
+    rng = np.random.RandomState(4)
+    selected = rng.randint(-1, 14, size=(B, k)).astype(np.int32)
+    q_lat = bf16.round_to_bf16(randn(31, (B, H, R)) * 0.05)
+    q_pe = bf16.round_to_bf16(randn(32, (B, H, P)) * 0.05)
+    scale = (128 + 64) ** -0.5
+    out = pool.sparse_decode(0, torch.from_numpy(q_lat).cuda().to(dt), torch.from_numpy(q_pe).cuda().to(dt),
+                             torch.from_numpy(selected).cuda(), sink=4, window=128, scale=scale, n_splits=2)
+    pool.check()
+    got = out.float().cpu().numpy()
+    tol = 1e-4 if dt == torch.float32 else 2e-2
+    for b in range(B):
+        sel_b = [int(c) for c in selected[b] if 0 <= c < (lens[b] + bs - 1) // bs]
+        pos = omla.sparse_positions(lens[b], sel_b, bs, 4, 128)
+        want = omla.sparse_mla_decode(q_lat[b], q_pe[b], _seq_rows(lat, tables, b, lens[b], bs),
+                                      _seq_rows(rope, tables, b, lens[b], bs), pos, scale)
+        np.testing.assert_allclose(got[b], want, rtol=tol, atol=tol)
