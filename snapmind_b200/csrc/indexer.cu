@@ -130,6 +130,8 @@ __global__ void __launch_bounds__(kPoolThreads) indexer_pool_kernel(PoolParams p
     // over the banks
     const TP* P = cache_proj ? wcache : reinterpret_cast<const TP*>(p.proj);
     const int qw = (W + 3) / 4;
+    constexpr int EPP = 16 / (int)sizeof(TP);  // projection elements per 16-byte vector
+    const bool pvec = (qw % EPP == 0) && (W % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) & 15) == 0);
     for (int base = 0; base < p.out_dim * 4; base += kPoolThreads) {  // uniform trip count (shuffles)
       const int task = base + tid;
       const bool active = task < p.out_dim * 4;
@@ -137,12 +139,25 @@ __global__ void __launch_bounds__(kPoolThreads) indexer_pool_kernel(PoolParams p
       const int d_lo = qd * qw, d_hi = min(W, d_lo + qw), n_d = active ? max(0, d_hi - d_lo) : 0;
       const TP* prow = P + (int64_t)o * W + d_lo;
       const float* mrow = mean + d_lo;
-      float a = 0.f;
-      int i = n_d > 0 ? o % n_d : 0;
-      for (int it2 = 0; it2 < n_d; ++it2) {
-        a = fmaf(Conv<TP>::to_f(prow[i]), mrow[i], a);
-        if (++i == n_d) i = 0;
+      float a0 = 0.f, a1 = 0.f;
+      if (pvec) {
+        // 16-byte vectors, visited from a per-lane rotation so a quarter-warp hits distinct banks
+        const int nv = n_d / EPP;
+        int v = nv > 0 ? (tid & 31) % nv : 0;
+        for (int j = 0; j < nv; ++j) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(prow + v * EPP);
+          const TP* w = reinterpret_cast<const TP*>(&wv);
+#pragma unroll
+          for (int e = 0; e < EPP; e += 2) {
+            a0 = fmaf(Conv<TP>::to_f(w[e]), mrow[v * EPP + e], a0);
+            a1 = fmaf(Conv<TP>::to_f(w[e + 1]), mrow[v * EPP + e + 1], a1);
+          }
+          if (++v == nv) v = 0;
+        }
+      } else {
+        for (int i = 0; i < n_d; ++i) a0 = fmaf(Conv<TP>::to_f(prow[i]), mrow[i], a0);
       }
+      float a = a0 + a1;
       a += __shfl_xor_sync(0xffffffffu, a, 1);
       a += __shfl_xor_sync(0xffffffffu, a, 2);
       if (active && qd == 0) out[o] = a;
