@@ -337,7 +337,16 @@ def run_tiered(args, dev, seed, dist, world) -> dict:
 
     from snapmind_b200.tiered_pool import TieredKVPool
 
-    B = args.tiered_batch
+    # every chunk lives in host-pinned backing (4 GiB per 32768-token sequence at this
+    # shape): bound the batch by the host memory the ranks of this node share
+    per_seq = TIER_L * 2 * H * D * 2 * (TIER_CTX + 4096)
+    try:
+        import psutil
+
+        avail = psutil.virtual_memory().available
+    except ImportError:
+        avail = 64 << 30
+    B = max(1, min(args.tiered_batch, int(0.6 * avail / world / per_seq)))
     steps = min(args.steps, 100)
     warmup = args.warmup
     max_tokens = TIER_CTX + 2 * (steps + warmup) + 2 * TIER_CHUNK
