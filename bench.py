@@ -130,6 +130,31 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def host_memory_budget() -> int:
+    """Bytes of host memory this process tree may still use: the smaller of the
+    available RAM and what the container's cgroup limit leaves."""
+    avail = None
+    try:
+        import psutil
+
+        avail = psutil.virtual_memory().available
+    except ImportError:
+        pass
+    for limit_f, usage_f in (("/sys/fs/cgroup/memory.max", "/sys/fs/cgroup/memory.current"),
+                             ("/sys/fs/cgroup/memory/memory.limit_in_bytes",
+                              "/sys/fs/cgroup/memory/memory.usage_in_bytes")):
+        try:
+            raw = Path(limit_f).read_text().strip()
+            if raw == "max":
+                continue
+            left = int(raw) - int(Path(usage_f).read_text().strip())
+            avail = left if avail is None else min(avail, left)
+            break
+        except (OSError, ValueError):
+            continue
+    return int(avail if avail is not None else 32 << 30)
+
+
 def seeded_lengths(seed: int, n: int, lo: int, hi: int) -> np.ndarray:
     return np.random.RandomState(seed).randint(lo, hi + 1, size=n).astype(np.int64)
 
@@ -340,13 +365,8 @@ def run_tiered(args, dev, seed, dist, world) -> dict:
     # every chunk lives in host-pinned backing (4 GiB per 32768-token sequence at this
     # shape): bound the batch by the host memory the ranks of this node share
     per_seq = TIER_L * 2 * H * D * 2 * (TIER_CTX + 4096)
-    try:
-        import psutil
-
-        avail = psutil.virtual_memory().available
-    except ImportError:
-        avail = 64 << 30
-    B = max(1, min(args.tiered_batch, int(0.6 * avail / world / per_seq)))
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+    B = max(1, min(args.tiered_batch, int(0.4 * host_memory_budget() / local_world / per_seq)))
     steps = min(args.steps, 100)
     warmup = args.warmup
     max_tokens = TIER_CTX + 2 * (steps + warmup) + 2 * TIER_CHUNK
