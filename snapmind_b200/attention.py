@@ -1,0 +1,125 @@
+"""Grouped-query attention that attends straight from the paged KV pool.
+
+``PagedGroupedQueryAttention`` is a drop-in for snapmind's
+``GroupedQueryAttention`` (snapmind/layers/attention/gqa.py:11-85), registered
+as ``"gqa_paged"`` in this package's ``ATTENTION``: the same constructor, the
+same submodules (``q_proj``, ``k_proj``, ``v_proj``, ``out_proj``, created in
+the same order, so state dicts load either way and a seeded construction gives
+the same weights), the same forward signature and output.
+
+The reference layer grows the layer's cache dict with ``torch.cat`` and runs
+dense attention over ``repeat_interleave``-d K/V (gqa.py:62-85), re-reading and
+re-copying the whole history every step.  This layer, given the layer view of a
+``"paged"`` cache of this package (``PagedKVCache.layer_dicts()[i]``):
+
+* appends the new K/V rows into the cache's pool with the append kernel
+  (``PagedKVCache.store``: the reference's block allocation order);
+* runs the paged GQA decode kernel over the layer's block table
+  (``PagedKVCache.attend``): one query is a decode step; ``T`` queries are a
+  causal prefill, one kernel row per query sharing the table row.
+
+The projections, RoPE (``pe.apply_to_qk``) and the output projection stay
+torch, as in the reference.  Without a cache (``kv_cache=None``) the layer
+attends causally over its own ``T`` tokens through a transient one-layer pool.
+
+Differences a caller can see: the attention weights are not materialised (the
+second output is ``None``); ``mask`` must be ``None`` or the causal mask of
+snapmind/layers/attention/sdpa.py ``create_causal_mask`` (what the reference
+models pass), anything else raises ``ValueError``; dropout is not applied
+(inference only); the batch is 1, as in the reference cache.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from snapmind_b200.kv_cache.paged import PagedKVCache, PagedLayerView
+from snapmind_b200.registry import ATTENTION
+
+
+def _is_causal_mask(mask: torch.Tensor, n_q: int, n_k: int) -> bool:
+    """True if ``mask`` is ``triu(full(-inf), diagonal=1)`` of shape (n_q, n_k), n_q == n_k."""
+    if mask.shape[-2:] != (n_q, n_k) or n_q != n_k:
+        return False
+    m = mask.reshape(n_q, n_k)
+    upper = torch.ones((n_q, n_k), dtype=torch.bool, device=m.device).triu(1)
+    ok = torch.where(upper, torch.isneginf(m), m == 0)
+    return bool(ok.all())
+
+
+@ATTENTION.register("gqa_paged")
+class PagedGroupedQueryAttention(nn.Module):
+    def __init__(
+        self,
+        d_model: int,
+        n_heads: int,
+        n_kv_heads: int | None = None,
+        dropout: float = 0.0,
+        bias: bool = False,
+        pe: nn.Module | None = None,
+        head_dim: int | None = None,
+    ):
+        super().__init__()
+        if head_dim is None:
+            assert d_model % n_heads == 0
+        self.d_model = d_model
+        self.n_heads = n_heads
+        self.n_kv_heads = n_kv_heads if n_kv_heads is not None else n_heads
+        self.n_rep = self.n_heads // self.n_kv_heads
+        self.head_dim = head_dim if head_dim is not None else d_model // n_heads
+        self.dropout = dropout
+        self.pe = pe
+
+        self.q_proj = nn.Linear(d_model, n_heads * self.head_dim, bias=bias)
+        self.k_proj = nn.Linear(d_model, self.n_kv_heads * self.head_dim, bias=bias)
+        self.v_proj = nn.Linear(d_model, self.n_kv_heads * self.head_dim, bias=bias)
+        self.out_proj = nn.Linear(n_heads * self.head_dim, d_model, bias=bias)
+
+    def _split_heads(self, x: torch.Tensor, n_heads: int) -> torch.Tensor:
+        batch, seq_len, _ = x.shape
+        return x.view(batch, seq_len, n_heads, self.head_dim).transpose(1, 2)
+
+    def forward(
+        self,
+        x: torch.Tensor,
+        kv_cache: PagedLayerView | None = None,
+        position_ids: torch.Tensor | None = None,
+        mask: torch.Tensor | None = None,
+    ) -> tuple[torch.Tensor, None]:
+        if x.shape[0] != 1:
+            raise ValueError("gqa_paged: the paged cache holds one sequence (batch 1)")
+        q = self._split_heads(self.q_proj(x), self.n_heads)
+        k = self._split_heads(self.k_proj(x), self.n_kv_heads)
+        v = self._split_heads(self.v_proj(x), self.n_kv_heads)
+        if self.pe is not None:
+            q, k = self.pe.apply_to_qk(q, k, position_ids)
+
+        n_new = x.shape[1]
+        if kv_cache is None:
+            cache = PagedKVCache(n_new, 1, self.n_kv_heads, self.head_dim, dtype=k.dtype, device=x.device)
+            layer = 0
+        elif isinstance(kv_cache, PagedLayerView):
+            cache, layer = kv_cache.cache, kv_cache.layer_idx
+        else:
+            raise TypeError(
+                "gqa_paged attends from a snapmind_b200 paged cache: pass PagedKVCache.layer_dicts()[i], "
+                f"got {type(kv_cache).__name__}"
+            )
+        if cache.n_heads != self.n_kv_heads or cache.head_dim != self.head_dim:
+            raise ValueError(
+                f"gqa_paged: cache holds {cache.n_heads} heads x {cache.head_dim}, "
+                f"layer needs {self.n_kv_heads} x {self.head_dim}"
+            )
+        cached = cache.num_tokens(layer)
+        causal = True
+        if mask is not None:
+            if not _is_causal_mask(mask, n_new, cached + n_new):
+                raise ValueError("gqa_paged supports no mask or the causal mask only")
+        elif n_new > 1 and cached > 0:
+            causal = False  # the reference attends every new query to every token here
+
+        cache.store(layer, k, v, cached)
+        qd = q if q.dtype == cache.dtype else q.to(cache.dtype)
+        out = cache.attend(layer, qd, scale=self.head_dim ** -0.5, causal=causal)
+        out = out.to(x.dtype).transpose(1, 2).reshape(1, n_new, self.n_heads * self.head_dim)
+        return self.out_proj(out), None

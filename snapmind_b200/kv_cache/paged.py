@@ -13,11 +13,18 @@ the C ABI): every byte of K/V — the append of ``store``, the tile gather of
 Differences a caller can see: the pool and the tensors ``fetch`` returns live on
 the CUDA device; the pool dtype is ``dtype`` (default float32, the reference's
 default).  Device block tables are mirrored in an int32 tensor updated when a
-table grows.
+table grows.  ``layer_dicts`` returns per-layer views (:class:`PagedLayerView`)
+instead of detached copies: they read like the reference's dicts, and what an
+attention layer assigns to them is written into the pool — the reference's
+models grow copies with ``torch.cat`` and never write its pool
+(snapmind/engine/generate.py:88-90, snapmind/layers/attention/gqa.py:62-67).
+``attend`` runs paged GQA attention for the newest tokens of a layer straight
+from the pool.
 """
 from __future__ import annotations
 
 import ctypes
+from collections.abc import MutableMapping
 
 import torch
 
@@ -70,6 +77,9 @@ class PagedKVCache(KVCacheABC):
         self._slot_counts: list[int] = [0] * n_layers
         self._tables_dev = torch.zeros((n_layers, max_blocks), dtype=torch.int32, device=self.device)
         self._err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._version = 0  # bumped by every change of the cached contents
+        self._ladder: torch.Tensor | None = None  # int32 [1, 2, ..., max_blocks * block_size]
+        self._workspace: torch.Tensor | None = None
 
     # ------------------------------------------------------------------ helpers
     def _stream(self) -> int:
@@ -141,6 +151,7 @@ class PagedKVCache(KVCacheABC):
                 self._err.data_ptr(), self._stream(),
             )  # fmt: skip
             _lib.check(status, "PagedKVCache.store")
+        self._version += 1
         if failed:
             raise RuntimeError(_lib.OUT_OF_BLOCKS_MSG)
         self._slot_counts[layer_idx] = slot_start + num_tokens
@@ -199,6 +210,7 @@ class PagedKVCache(KVCacheABC):
         this implementation reproduces that state and raises the same type.
         """
         bs = self.block_size
+        self._version += 1
         for layer_idx in range(self.n_layers):
             total = self._slot_counts[layer_idx]
             if total <= tokens_to_keep:
@@ -255,6 +267,7 @@ class PagedKVCache(KVCacheABC):
         self._block_tables = [[] for _ in range(self.n_layers)]
         self._slot_counts = [0] * self.n_layers
         self._tables_dev.zero_()
+        self._version += 1
 
     def memory_usage(self) -> dict:
         total_bytes = self._k_buffer.numel() * self._k_buffer.element_size()
@@ -266,14 +279,133 @@ class PagedKVCache(KVCacheABC):
             "max_blocks": self.max_blocks,
         }
 
-    def layer_dicts(self) -> dict[int, dict[str, torch.Tensor | None]]:
-        result: dict[int, dict[str, torch.Tensor | None]] = {}
-        for i in range(self.n_layers):
-            k, v = self.fetch(i)
-            result[i] = {"k": None, "v": None} if k.numel() == 0 else {"k": k, "v": v}
-        return result
+    def layer_dicts(self) -> dict[int, "PagedLayerView"]:
+        """One :class:`PagedLayerView` per layer (snapmind/kv_cache/paged.py:137-145
+        returns ``{"k": None, "v": None}`` or fetched copies; the views read the
+        same and write assignments through to the pool)."""
+        return {i: PagedLayerView(self, i) for i in range(self.n_layers)}
+
+    def num_tokens(self, layer_idx: int) -> int:
+        return self._slot_counts[layer_idx]
+
+    def _lens_ladder(self) -> torch.Tensor:
+        if self._ladder is None:
+            n = self.max_blocks * self.block_size
+            self._ladder = torch.arange(1, n + 1, dtype=torch.int32, device=self.device)
+        return self._ladder
+
+    def attend(self, layer_idx: int, q: torch.Tensor, scale: float | None = None, causal: bool = True,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        """Paged GQA attention of the queries of the newest ``T`` tokens of a layer.
+
+        ``q``: ``(1, Hq, T, D)`` in the pool dtype, ``Hq`` a multiple of the
+        cache's kv heads.  With ``causal`` query ``t`` attends to the first
+        ``n - T + t + 1`` cached tokens (``n`` = tokens in the layer), the
+        causal mask of snapmind/layers/attention/sdpa.py ``create_causal_mask``
+        shifted to the end of the cache; otherwise every query attends to all
+        ``n`` tokens (the reference's decode with ``mask=None``).  Every query
+        is one row of the paged decode kernel: all rows share this layer's
+        block table (row stride 0), and the causal lengths are read from a
+        constant device array ``1, 2, 3, ...``, so no lengths are copied.
+        Returns ``(1, Hq, T, D)``.
+        """
+        if q.dim() != 4 or q.shape[0] != 1 or q.shape[-1] != self.head_dim:
+            raise ValueError(f"attend: expected q of shape (1, Hq, T, {self.head_dim}), got {tuple(q.shape)}")
+        if q.dtype != self.dtype:
+            raise TypeError(f"attend: q dtype {q.dtype} != cache dtype {self.dtype}")
+        n_q, n_t = q.shape[1], q.shape[2]
+        n = self._slot_counts[layer_idx]
+        if n_t > n:
+            raise ValueError(f"attend: {n_t} queries but only {n} cached tokens in layer {layer_idx}")
+        if q.stride(-1) != 1:
+            q = q.contiguous()
+        if out is None:
+            out = torch.empty((1, n_q, n_t, self.head_dim), dtype=self.dtype, device=self.device)
+        if n_t == 0:
+            return out
+        if causal:
+            lens = self._lens_ladder()
+            lens_ptr = lens.data_ptr() + 4 * (n - n_t)
+        else:
+            lens = torch.full((n_t,), n, dtype=torch.int32, device=self.device)
+            lens_ptr = lens.data_ptr()
+        scale = self.head_dim ** -0.5 if scale is None else scale
+        lib = _lib.load()
+        split = lib.snapmind_paged_gqa_decode_split_tokens(n_t, self.n_heads, n, self.block_size)
+        need = lib.snapmind_paged_gqa_decode_workspace_bytes(n_t, n_q, self.n_heads, self.head_dim, n, split)
+        if self._workspace is None or self._workspace.numel() < need:
+            # zero-filled once; the kernel leaves its tickets at zero
+            self._workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+        status = lib.snapmind_paged_gqa_decode(
+            q.data_ptr(), q.stride(2), q.stride(1),
+            self._k_buffer.data_ptr(), self._v_buffer.data_ptr(), _lib.dtype_code(self.dtype),
+            self._tables_dev[layer_idx].data_ptr(), 0, self.max_blocks, lens_ptr,
+            out.data_ptr(), out.stride(2), out.stride(1),
+            float(scale), n_t, n_q, self.n_heads, self.head_dim, self.block_size, self.max_blocks,
+            n, split, 0, self._workspace.data_ptr(), self._workspace.numel(), self._err.data_ptr(),
+            self._stream(),
+        )  # fmt: skip
+        _lib.check(status, "PagedKVCache.attend")
+        return out
 
     # ------------------------------------------------------- introspection
     def block_tables(self) -> list[list[int]]:
         """Copy of the per-layer block tables (host lists)."""
         return [list(bt) for bt in self._block_tables]
+
+
+class PagedLayerView(MutableMapping):
+    """The ``kv_cache`` dict of one layer, backed by a :class:`PagedKVCache`.
+
+    Reads follow the reference's ``layer_dicts`` entries: keys ``"k"`` and
+    ``"v"`` always present, ``None`` while the layer is empty, else the layer's
+    ``(1, H, T, D)`` contents (one gather for both, reused until the cache
+    changes).  Writes follow the protocol of the reference attention layers
+    (snapmind/layers/attention/gqa.py:62-67): ``kv_cache["k"], kv_cache["v"] =
+    cat(cached, new)``; the rows past the cached length are stored (appended
+    on the GPU) once both tensors are assigned.  Attention plugins of this
+    package recognise the view and append and attend without a gather.
+    """
+
+    KEYS = ("k", "v")
+
+    def __init__(self, cache: PagedKVCache, layer_idx: int):
+        self.cache, self.layer_idx = cache, layer_idx
+        self._snap: tuple[int, torch.Tensor, torch.Tensor] | None = None
+        self._pending: torch.Tensor | None = None
+
+    def __getitem__(self, key):
+        if key not in self.KEYS:
+            raise KeyError(key)
+        if self.cache.num_tokens(self.layer_idx) == 0:
+            return None
+        if self._snap is None or self._snap[0] != self.cache._version:
+            k, v = self.cache.fetch(self.layer_idx)
+            self._snap = (self.cache._version, k, v)
+        return self._snap[1] if key == "k" else self._snap[2]
+
+    def __setitem__(self, key, value):
+        if key == "k":
+            self._pending = value
+            return
+        if key != "v" or self._pending is None:
+            raise KeyError(f"PagedLayerView expects 'k' then 'v' assignments, got {key!r}")
+        k, v = self._pending, value
+        self._pending = None
+        n = self.cache.num_tokens(self.layer_idx)
+        total = k.shape[-2]
+        if k.shape[0] != 1 or v.shape[-2] != total:
+            raise ValueError("PagedLayerView: expected (1, H, T, D) key and value of one length")
+        if total < n:
+            raise ValueError(f"PagedLayerView: the cache holds {n} tokens, got {total}; it cannot shrink")
+        if total > n:
+            self.cache.store(self.layer_idx, k[:, :, n:], v[:, :, n:], n)
+
+    def __delitem__(self, key):
+        raise TypeError("PagedLayerView entries cannot be deleted")
+
+    def __iter__(self):
+        return iter(self.KEYS)
+
+    def __len__(self):
+        return len(self.KEYS)

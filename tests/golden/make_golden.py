@@ -16,7 +16,12 @@ Writes, next to this script:
   * gqa_decode.npz / gqa_decode.json — the reference ``GroupedQueryAttention``
                           forward for one decode token over a ``PagedKVCache``
                           (q/k/v projections saved, out_proj set to identity so
-                          the output is the attention result itself).
+                          the output is the attention result itself);
+  * tiered_ops.json, mla.npz/json, indexer.npz/json — the tiered cache, MLA
+                          layer and lookahead indexer driven the same way;
+  * e2e_llama.npz / e2e_llama.json — the reference ``LlamaModel`` generating
+                          greedily from a seeded prompt with seeded N(0, 0.02)
+                          weights (a small shape and the TinyLlama shape).
 
 Inputs are regenerated from seeds with ``inputs.randn`` (frozen RandomState
 stream), so the fixtures hold seeds, small tensors and digests only.
@@ -567,20 +572,109 @@ def make_indexer(out_npz: Path, out_json: Path):
     out_json.write_text(json.dumps(meta, indent=1))
 
 
+E2E_CASES = [
+    # (name, shape name, weight seed, prompt seed, prompt length, generated ids, cache sample per layer)
+    ("small", "SMALL", 7, 11, 24, 8, None),
+    ("tinyllama", "TINYLLAMA", 0, 1, 256, 64, 512),
+]
+
+
+def make_e2e(out_npz: Path, out_json: Path, names=None):
+    """The reference ``LlamaModel`` (snapmind/models/llama.py) generating greedily
+    from a seeded prompt, with its cache dicts taken from ``PagedKVCache.layer_dicts()``
+    as ``GenerateEngine._make_kv_cache`` does (snapmind/engine/generate.py:88-90):
+    generated ids, each step's top-2 logits, per-parameter checksums of the
+    seeded weights and the final cache (whole for the small case; per-layer sums
+    and a seeded sample of entries for the TinyLlama case)."""
+    import torch
+    from llama_harness import SMALL, TINYLLAMA, init_weights, param_checksums, prompt_ids
+    from snapmind.core.config import ModelConfig
+    from snapmind.engine.prefill import prefill
+    from snapmind.kv_cache.paged import PagedKVCache
+    from snapmind.models.llama import LlamaModel
+    from snapmind.sampling.greedy import GreedySampler
+
+    shapes = {"SMALL": SMALL, "TINYLLAMA": TINYLLAMA}
+    arrays, meta = {}, {}
+    if out_json.exists():
+        meta = json.loads(out_json.read_text())
+        with np.load(out_npz) as z:
+            arrays = dict(z)
+    for name, shape_name, wseed, pseed, plen, n_gen, n_sample in E2E_CASES:
+        if names and name not in names:
+            continue
+        sh = shapes[shape_name]
+        cfg = ModelConfig(model_type="llama", d_model=sh.d_model, n_heads=sh.n_heads, n_kv_heads=sh.n_kv_heads,
+                          n_layers=sh.n_layers, d_ff=sh.d_ff, vocab_size=sh.vocab_size,
+                          max_seq_len=sh.max_seq_len, norm_eps=sh.norm_eps, rope_theta=sh.rope_theta)
+        model = LlamaModel(cfg)
+        init_weights(model, wseed)
+        model.eval()
+        hd = sh.d_model // sh.n_heads
+        cache = PagedKVCache(max_seq_len=sh.max_seq_len, n_layers=sh.n_layers, n_heads=sh.n_kv_heads, head_dim=hd)
+        cache.reset()
+        kv = cache.layer_dicts()
+        prompt = prompt_ids(sh.vocab_size, plen, pseed)
+        sampler = GreedySampler()
+        logits, _ = prefill(model, prompt[None], kv)
+        logits = logits[0]
+        ids, tops = [], []
+        step = plen
+        for i in range(n_gen):
+            top = torch.topk(logits, 2)
+            tops.append((top.values.tolist(), top.indices.tolist()))
+            ids.append(int(sampler.sample(logits).item()))
+            if i == n_gen - 1:
+                break
+            with torch.no_grad():  # the body of snapmind/engine/decode.py decode_step, keeping the logits
+                logits = model(torch.tensor([[ids[-1]]]), kv_cache=kv, position_ids=torch.tensor([step]))[0, -1]
+            step += 1
+        ks = torch.stack([kv[i]["k"][0] for i in range(sh.n_layers)]).numpy()  # (L, H, T, D)
+        vs = torch.stack([kv[i]["v"][0] for i in range(sh.n_layers)]).numpy()
+        rec = {"shape": shape_name, "weight_seed": wseed, "prompt_seed": pseed, "prompt_len": plen,
+               "n_generated": n_gen, "ids": ids, "top2": tops, "cache_shape": list(ks.shape),
+               "params": param_checksums(model),
+               "k_sums": ks.astype(np.float64).sum(axis=(1, 2, 3)).tolist(),
+               "v_sums": vs.astype(np.float64).sum(axis=(1, 2, 3)).tolist()}
+        if n_sample is None:
+            arrays[f"{name}_k"], arrays[f"{name}_v"] = ks, vs
+        else:
+            rng = np.random.RandomState(wseed + 100)
+            flat = rng.choice(ks[0].size, size=n_sample, replace=False)
+            arrays[f"{name}_sample_idx"] = flat.astype(np.int64)
+            arrays[f"{name}_k_sample"] = ks.reshape(sh.n_layers, -1)[:, flat]
+            arrays[f"{name}_v_sample"] = vs.reshape(sh.n_layers, -1)[:, flat]
+        meta[name] = rec
+        print(f"e2e {name}: ids {ids[:8]}...")
+    np.savez_compressed(out_npz, **arrays)
+    out_json.write_text(json.dumps(meta, indent=1))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SNAPMIND_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="fixtures to regenerate: paged, gqa, tiered, mla, indexer, e2e (default: all)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
+    sys.path.insert(0, str(HERE.parent))
     import torch
 
     torch.set_num_threads(4)
-    make_paged_ops(HERE / "paged_ops.json")
-    make_paged_batched(HERE / "paged_batched.json")
-    make_gqa(HERE / "gqa_decode.npz", HERE / "gqa_decode.json")
-    make_tiered(HERE / "tiered_ops.json")
-    make_mla(HERE / "mla.npz", HERE / "mla.json")
-    make_indexer(HERE / "indexer.npz", HERE / "indexer.json")
+    want = set(args.only) if args.only else {"paged", "gqa", "tiered", "mla", "indexer", "e2e"}
+    if "paged" in want:
+        make_paged_ops(HERE / "paged_ops.json")
+        make_paged_batched(HERE / "paged_batched.json")
+    if "gqa" in want:
+        make_gqa(HERE / "gqa_decode.npz", HERE / "gqa_decode.json")
+    if "tiered" in want:
+        make_tiered(HERE / "tiered_ops.json")
+    if "mla" in want:
+        make_mla(HERE / "mla.npz", HERE / "mla.json")
+    if "indexer" in want:
+        make_indexer(HERE / "indexer.npz", HERE / "indexer.json")
+    if "e2e" in want:
+        make_e2e(HERE / "e2e_llama.npz", HERE / "e2e_llama.json")
     print("golden vectors written to", HERE)
 
 
