@@ -41,41 +41,236 @@ struct PoolParams {
 constexpr int kPoolThreads = 512;
 constexpr int kPoolUnroll = 8;
 
-// Persistent: each CTA loops over (sequence, chunk) items.  The projection
-// matrix is staged once per CTA in shared memory (when it fits), the rows of a
-// chunk are summed by row groups with 16-byte loads (kPoolUnroll rows in
-// flight per thread), and the group partials are reduced in shared memory.
-// smem: [proj cache (optional)][mean: width][partials: groups x width]
+// Where item `it` (sequence b, chunk c) lives: its pool block and row count
+// (phys < 0: nothing to read, the output is zero).  Out-of-range block ids
+// are flagged and skipped.
+__device__ __forceinline__ void pool_item(const PoolParams& p, int64_t it, int& b, int& c, int& n, int& phys) {
+  b = (int)(it / p.chunk_count);
+  c = p.chunk_begin + (int)(it - (int64_t)b * p.chunk_count);
+  // without lengths every chunk is full
+  n = p.seq_lens ? min(p.block_size, p.seq_lens[b] - c * p.block_size) : p.block_size;
+  phys = -1;
+  if (n > 0 && c < p.table_width) {
+    phys = p.tables[(int64_t)b * p.table_stride + c];
+    if (phys < 0 || phys >= p.num_blocks) {
+      if (threadIdx.x == 0) flag_error(p.err, SNAPMIND_DEVERR_BLOCK_ID);
+      phys = -1;
+    }
+  }
+}
+
+// out[o] = P[o] . mean for o < out_dim.  4 threads per output, each over a
+// quarter of the width.  Lane l of a warp takes quarter l / 8 of output
+// (warp slot * 8 + l % 8): the 8 lanes of one shared-memory phase read 8
+// padded projection rows at the same column (distinct bank groups) and the
+// same mean elements (a broadcast).
+template <typename TP>
+__device__ __forceinline__ void project_mean(const TP* P, int w_stride, const float* mean, int W, int out_dim,
+                                             float* out) {
+  const int tid = threadIdx.x;
+  const int qw = (W + 3) / 4;
+  constexpr int EPP = 16 / (int)sizeof(TP);  // projection elements per 16-byte vector
+  const bool pvec = (qw % EPP == 0) && (W % 4 == 0) && (w_stride % EPP == 0) &&
+                    ((reinterpret_cast<uintptr_t>(P) & 15) == 0);
+  for (int base = 0; base < out_dim * 4; base += kPoolThreads) {  // uniform trip count (shuffles)
+    const int task = base + tid;
+    const int lane = task & 31, qd = lane >> 3;
+    const int o = (task >> 5) * 8 + (lane & 7);
+    const bool active = o < out_dim;
+    const int d_lo = qd * qw, d_hi = min(W, d_lo + qw), n_d = active ? max(0, d_hi - d_lo) : 0;
+    const TP* prow = P + (int64_t)(active ? o : 0) * w_stride + d_lo;
+    const float* mrow = mean + d_lo;
+    float a0 = 0.f, a1 = 0.f;
+    if (pvec) {
+      const int nv = n_d / EPP;
+      for (int v = 0; v < nv; ++v) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(prow + v * EPP);
+        const TP* w = reinterpret_cast<const TP*>(&wv);
+#pragma unroll
+        for (int e = 0; e < EPP; e += 2) {
+          a0 = fmaf(Conv<TP>::to_f(w[e]), mrow[v * EPP + e], a0);
+          a1 = fmaf(Conv<TP>::to_f(w[e + 1]), mrow[v * EPP + e + 1], a1);
+        }
+      }
+    } else {
+      for (int i = 0; i < n_d; ++i) a0 = fmaf(Conv<TP>::to_f(prow[i]), mrow[i], a0);
+    }
+    float a = a0 + a1;
+    a += __shfl_xor_sync(0xffffffffu, a, 8);
+    a += __shfl_xor_sync(0xffffffffu, a, 16);
+    if (active && qd == 0) out[o] = a;
+  }
+}
+
+// out[o] = P[o] . mean, sliced: warp s takes columns [32 s, 32 s + 32) and
+// lane l the outputs l, l + 32, l + 64, l + 96.  The slice of the mean is read
+// once into registers (broadcast loads); projection rows are padded so their
+// stride is an odd number of 16-byte granules, which puts the 8 lanes of a
+// shared-memory phase (8 consecutive rows, one column) on 8 distinct bank
+// groups.  Slice partials meet in `red` ([W / 32][out_dim] floats) and are
+// summed in slice order.  Needs W % 32 == 0, W / 32 <= warps, out_dim <= 128.
+template <typename TP>
+__device__ __forceinline__ void project_mean_sliced(const TP* P, int w_stride, const float* mean, int W,
+                                                    int out_dim, float* out, float* red) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_slices = W / 32;
+  constexpr int EPP = 16 / (int)sizeof(TP);
+  constexpr int NV = 32 / EPP;
+  if (warp < n_slices) {
+    float m[32];
+    const float4* m4 = reinterpret_cast<const float4*>(mean + warp * 32);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float4 t = m4[k];
+      m[4 * k] = t.x;
+      m[4 * k + 1] = t.y;
+      m[4 * k + 2] = t.z;
+      m[4 * k + 3] = t.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int o = lane + 32 * i;
+      if (o < out_dim) {
+        const uint4* row = reinterpret_cast<const uint4*>(P + (int64_t)o * w_stride + warp * 32);
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+          const uint4 wv = row[v];
+          const TP* w = reinterpret_cast<const TP*>(&wv);
+#pragma unroll
+          for (int e = 0; e < EPP; e += 2) {
+            a0 = fmaf(Conv<TP>::to_f(w[e]), m[v * EPP + e], a0);
+            a1 = fmaf(Conv<TP>::to_f(w[e + 1]), m[v * EPP + e + 1], a1);
+          }
+        }
+        red[warp * out_dim + o] = a0 + a1;
+      }
+    }
+  }
+  __syncthreads();
+  for (int o = tid; o < out_dim; o += kPoolThreads) {
+    float acc = 0.f;
+    for (int w = 0; w < n_slices; ++w) acc += red[w * out_dim + o];
+    out[o] = acc;
+  }
+}
+
+// Persistent: each CTA loops over (sequence, chunk) items with a stride of
+// the grid.  The projection matrix is staged once per CTA in shared memory
+// (when it fits), its rows padded by 16 bytes.  A chunk's rows are summed by
+// row groups of threads with 16-byte loads and the group partials reduced in
+// shared memory.
+//
+// Pipelined path (16-byte rows, a chunk fits one batch of kPoolUnroll rows per
+// thread): the loads of item i+1 are issued right after item i's registers
+// were summed, and the block id of item i+2 is looked up at the same time, so
+// HBM traffic of the next chunk overlaps the reduction and the projection of
+// the current one.  Otherwise a plain loop does one item after another.
+//
+// smem: [proj cache (optional), out_dim rows of width + pad][mean: width][partials: groups x width]
 template <typename T, typename TP>
-__global__ void __launch_bounds__(kPoolThreads) indexer_pool_kernel(PoolParams p, int cache_proj, int vec_ok) {
+__global__ void __launch_bounds__(kPoolThreads, 1) indexer_pool_kernel(PoolParams p, int cache_proj, int vec_ok) {
   extern __shared__ __align__(16) unsigned char pool_smem[];
   const int W = p.width;
-  const int64_t proj_elems = cache_proj ? (int64_t)p.out_dim * W : 0;
+  constexpr int kPad = 16 / (int)sizeof(TP);
+  const int w_stride = cache_proj ? W + kPad : W;  // elements between projection rows
+  const int64_t proj_elems = cache_proj ? (int64_t)p.out_dim * w_stride : 0;
   TP* wcache = reinterpret_cast<TP*>(pool_smem);
   float* mean = reinterpret_cast<float*>(pool_smem + ((proj_elems * (int64_t)sizeof(TP) + 15) / 16) * 16);
   float* part = mean + W;
   const int tid = threadIdx.x;
   if (cache_proj) {
     const TP* P = reinterpret_cast<const TP*>(p.proj);
-    for (int64_t i = tid; i < proj_elems; i += kPoolThreads) wcache[i] = P[i];
+    const int64_t n = (int64_t)p.out_dim * W;
+    for (int64_t i = tid; i < n; i += kPoolThreads) wcache[(i / W) * w_stride + i % W] = P[i];
   }
+  const TP* P = cache_proj ? wcache : reinterpret_cast<const TP*>(p.proj);
   constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte vector
   const int n_vec = W / EPV;
   const int groups = vec_ok ? kPoolThreads / n_vec : 1;
   const int out_w = p.proj ? p.out_dim : W;
   const int64_t items = (int64_t)p.batch * p.chunk_count;
-  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
-    const int b = (int)(it / p.chunk_count);
-    const int c = p.chunk_begin + (int)(it - (int64_t)b * p.chunk_count);
-    float* out = p.out + ((int64_t)b * p.max_chunks + c) * out_w;
-    // without lengths every chunk is full
-    const int n = p.seq_lens ? min(p.block_size, p.seq_lens[b] - c * p.block_size) : p.block_size;
-    int32_t phys = -1;
-    if (n > 0 && c < p.table_width) phys = p.tables[(int64_t)b * p.table_stride + c];
-    if (n > 0 && c < p.table_width && (phys < 0 || phys >= p.num_blocks)) {
-      if (tid == 0) flag_error(p.err, SNAPMIND_DEVERR_BLOCK_ID);
-      phys = -1;
+  const int64_t stride = gridDim.x;
+  // the sliced projection reuses the partials buffer (groups x W floats) for its slice sums
+  constexpr int EPP = 16 / (int)sizeof(TP);
+  const bool sliced = p.proj && W % 32 == 0 && W / 32 <= kPoolThreads / 32 && p.out_dim <= 128 &&
+                      (W / 32) * p.out_dim <= groups * W && w_stride % EPP == 0 &&
+                      (reinterpret_cast<uintptr_t>(P) & 15) == 0;
+  auto project = [&](float* out) {
+    if (sliced) project_mean_sliced(P, w_stride, mean, W, p.out_dim, out, part);
+    else project_mean(P, w_stride, mean, W, p.out_dim, out);
+  };
+
+  if (vec_ok && p.block_size <= groups * kPoolUnroll) {
+    const int j = tid % n_vec, g = tid / n_vec;
+    const bool loader = g < groups;
+    uint4 v[kPoolUnroll];
+    auto issue = [&](int phys, int n) {
+      const T* rows = reinterpret_cast<const T*>(p.pool) + (int64_t)(phys < 0 ? 0 : phys) * p.block_size * p.row_width;
+#pragma unroll
+      for (int u = 0; u < kPoolUnroll; ++u) {
+        const int r = g + u * groups;
+        v[u] = (loader && phys >= 0 && r < n) ? *reinterpret_cast<const uint4*>(rows + (int64_t)r * p.row_width + j * EPV)
+                                             : make_uint4(0, 0, 0, 0);
+      }
+    };
+    int64_t it = blockIdx.x;
+    int b, c, n, phys, b1 = 0, c1 = 0, n1 = 0, phys1 = -1;
+    if (it < items) {
+      pool_item(p, it, b, c, n, phys);
+      issue(phys, n);
+      if (it + stride < items) pool_item(p, it + stride, b1, c1, n1, phys1);
     }
+    __syncthreads();  // projection cache loaded
+    for (; it < items; it += stride) {
+      float acc[EPV];
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) acc[e] = 0.f;
+#pragma unroll
+      for (int u = 0; u < kPoolUnroll; ++u) {
+        const T* x = reinterpret_cast<const T*>(&v[u]);
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) acc[e] += Conv<T>::to_f(x[e]);
+      }
+      if (loader) {
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) part[g * W + j * EPV + e] = acc[e];
+      }
+      // the next item's rows fly while this one is reduced and projected
+      int b2 = 0, c2 = 0, n2 = 0, phys2 = -1;
+      if (it + stride < items) {
+        issue(phys1, n1);
+        if (it + 2 * stride < items) pool_item(p, it + 2 * stride, b2, c2, n2, phys2);
+      }
+      __syncthreads();  // partials written
+      float* out = p.out + ((int64_t)b * p.max_chunks + c) * out_w;
+      if (phys < 0) {
+        for (int i = tid; i < out_w; i += kPoolThreads) out[i] = 0.f;
+      } else {
+        const float inv = 1.f / (float)n;
+        for (int d = tid; d < W; d += kPoolThreads) {
+          float s = 0.f;
+          for (int gg = 0; gg < groups; ++gg) s += part[gg * W + d];
+          mean[d] = s * inv;
+        }
+        __syncthreads();  // mean complete
+        if (!p.proj) {
+          for (int d = tid; d < W; d += kPoolThreads) out[d] = mean[d];
+        } else {
+          project(out);
+        }
+      }
+      __syncthreads();  // mean and partials consumed
+      b = b1; c = c1; n = n1; phys = phys1;
+      b1 = b2; c1 = c2; n1 = n2; phys1 = phys2;
+    }
+    return;
+  }
+
+  for (int64_t it = blockIdx.x; it < items; it += stride) {
+    int b, c, n, phys;
+    pool_item(p, it, b, c, n, phys);
+    float* out = p.out + ((int64_t)b * p.max_chunks + c) * out_w;
     __syncthreads();  // previous item's mean/part reads are done (and the cache is loaded)
     if (phys < 0) {
       for (int i = tid; i < out_w; i += kPoolThreads) out[i] = 0.f;
@@ -125,43 +320,7 @@ __global__ void __launch_bounds__(kPoolThreads) indexer_pool_kernel(PoolParams p
       for (int d = tid; d < W; d += kPoolThreads) out[d] = mean[d];
       continue;
     }
-    // projection: 4 consecutive threads per output, each over a quarter of the
-    // width, reading at a per-thread rotation so that a warp spreads its loads
-    // over the banks
-    const TP* P = cache_proj ? wcache : reinterpret_cast<const TP*>(p.proj);
-    const int qw = (W + 3) / 4;
-    constexpr int EPP = 16 / (int)sizeof(TP);  // projection elements per 16-byte vector
-    const bool pvec = (qw % EPP == 0) && (W % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) & 15) == 0);
-    for (int base = 0; base < p.out_dim * 4; base += kPoolThreads) {  // uniform trip count (shuffles)
-      const int task = base + tid;
-      const bool active = task < p.out_dim * 4;
-      const int o = task >> 2, qd = task & 3;
-      const int d_lo = qd * qw, d_hi = min(W, d_lo + qw), n_d = active ? max(0, d_hi - d_lo) : 0;
-      const TP* prow = P + (int64_t)o * W + d_lo;
-      const float* mrow = mean + d_lo;
-      float a0 = 0.f, a1 = 0.f;
-      if (pvec) {
-        // 16-byte vectors, visited from a per-lane rotation so a quarter-warp hits distinct banks
-        const int nv = n_d / EPP;
-        int v = nv > 0 ? (tid & 31) % nv : 0;
-        for (int j = 0; j < nv; ++j) {
-          const uint4 wv = *reinterpret_cast<const uint4*>(prow + v * EPP);
-          const TP* w = reinterpret_cast<const TP*>(&wv);
-#pragma unroll
-          for (int e = 0; e < EPP; e += 2) {
-            a0 = fmaf(Conv<TP>::to_f(w[e]), mrow[v * EPP + e], a0);
-            a1 = fmaf(Conv<TP>::to_f(w[e + 1]), mrow[v * EPP + e + 1], a1);
-          }
-          if (++v == nv) v = 0;
-        }
-      } else {
-        for (int i = 0; i < n_d; ++i) a0 = fmaf(Conv<TP>::to_f(prow[i]), mrow[i], a0);
-      }
-      float a = a0 + a1;
-      a += __shfl_xor_sync(0xffffffffu, a, 1);
-      a += __shfl_xor_sync(0xffffffffu, a, 2);
-      if (active && qd == 0) out[o] = a;
-    }
+    project(out);
   }
 }
 
@@ -306,7 +465,7 @@ int snapmind_indexer_pool_chunks(const void* pool, int dtype, int64_t row_width,
                      ((reinterpret_cast<uintptr_t>(pool) & 15) == 0);
   const int groups = vec_ok ? kPoolThreads / n_vec : 1;
   const int pd = proj ? proj_dtype : SNAPMIND_DTYPE_F32;
-  const int64_t proj_bytes = proj ? (int64_t)out_dim * width * dtype_size(pd) : 0;
+  const int64_t proj_bytes = proj ? (int64_t)out_dim * (width + 16 / dtype_size(pd)) * dtype_size(pd) : 0;
   const int cache_proj = proj && proj_bytes <= 160 * 1024;
   const size_t smem = (size_t)(cache_proj ? (proj_bytes + 15) / 16 * 16 : 0) + sizeof(float) * width * (1 + groups);
   SNAPMIND_CHECK_ARG(smem <= 220 * 1024, "indexer_pool_chunks: width too large for shared memory");
