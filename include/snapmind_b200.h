@@ -252,7 +252,17 @@ SNAPMIND_API int snapmind_indexer_score_ref(const float *q, const float *w, int3
 SNAPMIND_API int snapmind_indexer_topk(const void *q, const void *keys, int dtype, const int32_t *n_chunks,
                           int32_t n_chunks0, int32_t batch, int32_t max_chunks, int32_t dim, float scale,
                           float bias, int32_t k, int32_t *out_idx, float *out_score, float *all_scores,
-                          void *stream);
+                          void *workspace, int64_t workspace_bytes, void *stream);
+
+/*
+ * Bytes of device workspace snapmind_indexer_topk uses for its many-CTA form
+ * (chunks scored and pre-selected 128 per CTA, the last CTA of a sequence
+ * merging the candidates); 0 for invalid sizes.  The workspace must be
+ * zero-filled before its first use and is left zeroed by every call; calls
+ * sharing one workspace must not overlap on the GPU.  With workspace NULL the
+ * call uses one CTA per sequence instead (same result).
+ */
+SNAPMIND_API int64_t snapmind_indexer_topk_workspace_bytes(int32_t batch, int32_t max_chunks, int32_t k);
 
 /*
  * Sparse MLA decode attention over the positions of an attention sink

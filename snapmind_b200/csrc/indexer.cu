@@ -435,6 +435,129 @@ __global__ void __launch_bounds__(kTopkThreads) indexer_topk_kernel(
   }
 }
 
+
+// Descending bitonic sort of n (a power of two) keys in shared memory; every
+// thread of the block calls it.
+__device__ __forceinline__ void bitonic_sort_desc(unsigned long long* sk, int n) {
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool desc = (i & size) == 0;
+          const unsigned long long a = sk[i], c2 = sk[j];
+          if (desc ? (a < c2) : (a > c2)) {
+            sk[i] = c2;
+            sk[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+constexpr int kSliceChunks = 128;  // chunks scored and pre-selected by one CTA
+constexpr int kSliceThreads = 256;
+
+// Two-phase top-k over many CTAs.  CTA (slice, b) scores chunks
+// [slice * 128, slice * 128 + 128) of sequence b, sorts their (ordered score,
+// inverted id) keys and keeps the best `keep` = min(k, 128) as candidates.
+// Every member of the sequence's top-k is among the candidates of its slice,
+// so the top-k of the union of candidates is the exact answer.  The CTA that
+// takes the sequence's last ticket merges (sorts the union) and resets the
+// ticket; no CTA waits for another.
+template <typename T>
+__global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
+    const T* q, const T* keys, const int32_t* n_chunks_arr, int n_chunks0, int max_chunks, int dim, float scale,
+    float bias, int k, int n_slices, int keep, int merge_n, unsigned long long* cand, int32_t* tickets,
+    int32_t* out_idx, float* out_score, float* all_scores) {
+  extern __shared__ unsigned long long sk[];  // [max(kSliceChunks, merge_n)]
+  __shared__ int s_last;
+  const int slice = blockIdx.x, b = blockIdx.y;
+  int nc = n_chunks_arr ? n_chunks_arr[b] : n_chunks0;
+  nc = max(0, min(nc, max_chunks));
+  const int c_begin = slice * kSliceChunks;
+  const T* qb = q + (int64_t)b * dim;
+  const T* kb = keys + (int64_t)b * max_chunks * dim;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  constexpr int kU = 8;  // chunks per warp pass: 8 independent key rows in flight
+  for (int l0 = warp * kU; l0 < kSliceChunks; l0 += nw * kU) {
+    float dot[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) dot[u] = 0.f;
+    for (int d = lane; d < dim; d += 32) {
+      const float qd = Conv<T>::to_f(qb[d]);
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int c = c_begin + l0 + u;
+        if (c < nc) dot[u] = fmaf(qd, Conv<T>::to_f(kb[(int64_t)c * dim + d]), dot[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], off);
+    }
+    if (lane < kU) {
+      float mine = dot[0];
+#pragma unroll
+      for (int u = 1; u < kU; ++u)
+        if (lane == u) mine = dot[u];
+      const int c = c_begin + l0 + lane;
+      unsigned long long key = 0ull;  // below every real key
+      if (c < nc) {
+        const float s = 1.f / (1.f + expf(-(mine * scale + bias)));
+        if (all_scores) all_scores[(int64_t)b * max_chunks + c] = s;
+        key = ((unsigned long long)ordered_bits(s) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)c);
+      }
+      sk[l0 + lane] = key;
+    }
+  }
+  __syncthreads();
+  bitonic_sort_desc(sk, kSliceChunks);
+  unsigned long long* mine = cand + ((int64_t)b * n_slices + slice) * keep;
+  for (int i = threadIdx.x; i < keep; i += blockDim.x) mine[i] = sk[i];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&tickets[b], 1) == n_slices - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const unsigned long long* all = cand + (int64_t)b * n_slices * keep;
+  const int n_cand = n_slices * keep;
+  for (int i = threadIdx.x; i < merge_n; i += blockDim.x) sk[i] = i < n_cand ? __ldcg(all + i) : 0ull;
+  __syncthreads();
+  bitonic_sort_desc(sk, merge_n);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const bool ok = i < nc;
+    const unsigned long long key = sk[i];
+    out_idx[(int64_t)b * k + i] = ok ? (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull)) : -1;
+    if (out_score) {
+      const uint32_t ob = (uint32_t)(key >> 32);
+      const uint32_t u = (ob & 0x80000000u) ? (ob & 0x7FFFFFFFu) : ~ob;
+      out_score[(int64_t)b * k + i] = ok ? __uint_as_float(u) : -INFINITY;
+    }
+  }
+  if (threadIdx.x == 0) tickets[b] = 0;
+}
+
+struct TopkPlan {
+  int n_slices, keep, merge_n;
+  int64_t tickets_bytes, total;
+};
+
+TopkPlan topk_plan(int batch, int max_chunks, int k) {
+  TopkPlan t;
+  t.n_slices = (max_chunks + kSliceChunks - 1) / kSliceChunks;
+  t.keep = k < kSliceChunks ? k : kSliceChunks;
+  t.merge_n = 1;
+  while (t.merge_n < t.n_slices * t.keep) t.merge_n <<= 1;
+  if (t.merge_n < kSliceChunks) t.merge_n = kSliceChunks;
+  t.tickets_bytes = ((int64_t)batch * 4 + 255) / 256 * 256;
+  t.total = t.tickets_bytes + (int64_t)batch * t.n_slices * t.keep * 8;
+  return t;
+}
 }  // namespace
 }  // namespace snapmind
 
@@ -510,18 +633,53 @@ int snapmind_indexer_score_ref(const float* q, const float* w, int32_t n_rows, i
   SNAPMIND_LAUNCH_CHECK("indexer_score_ref launch");
 }
 
+int64_t snapmind_indexer_topk_workspace_bytes(int32_t batch, int32_t max_chunks, int32_t k) {
+  if (batch <= 0 || max_chunks <= 0 || k <= 0 || k > max_chunks) return 0;
+  return topk_plan(batch, max_chunks, k).total;
+}
+
 int snapmind_indexer_topk(const void* q, const void* keys, int dtype, const int32_t* n_chunks, int32_t n_chunks0,
                           int32_t batch, int32_t max_chunks, int32_t dim, float scale, float bias, int32_t k,
-                          int32_t* out_idx, float* out_score, float* all_scores, void* stream) {
+                          int32_t* out_idx, float* out_score, float* all_scores, void* workspace,
+                          int64_t workspace_bytes, void* stream) {
   SNAPMIND_CHECK_ARG(dtype_size(dtype) > 0, "indexer_topk: unknown dtype");
   SNAPMIND_CHECK_ARG(batch >= 0 && max_chunks > 0 && max_chunks <= 16384 && dim > 0 && k > 0 && k <= max_chunks,
                      "indexer_topk: bad sizes (max_chunks <= 16384, 0 < k <= max_chunks)");
   if (batch == 0) return SNAPMIND_OK;
   SNAPMIND_CHECK_ARG(q && keys && out_idx, "indexer_topk: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (workspace) {
+    const TopkPlan t = topk_plan(batch, max_chunks, k);
+    SNAPMIND_CHECK_ARG(workspace_bytes >= t.total, "indexer_topk: workspace needs %lld bytes, got %lld",
+                       (long long)t.total, (long long)workspace_bytes);
+    SNAPMIND_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 7) == 0, "indexer_topk: workspace not 8-byte aligned");
+    SNAPMIND_CHECK_ARG(batch <= 65535, "indexer_topk: batch > 65535");
+    int32_t* tickets = static_cast<int32_t*>(workspace);
+    auto* cand = reinterpret_cast<unsigned long long*>(static_cast<char*>(workspace) + t.tickets_bytes);
+    const size_t smem = sizeof(unsigned long long) * (size_t)t.merge_n;
+    auto go2 = [&](auto kernel, const auto* qq, const auto* kk) -> int {
+      if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return cuda_status(e, "indexer_topk smem attribute");
+      }
+      kernel<<<dim3(t.n_slices, batch), kSliceThreads, smem, st>>>(
+          qq, kk, n_chunks, n_chunks0, max_chunks, dim, scale, bias, k, t.n_slices, t.keep, t.merge_n, cand, tickets,
+          out_idx, out_score, all_scores);
+      return cuda_status(cudaGetLastError(), "indexer_topk launch");
+    };
+    switch (dtype) {
+      case SNAPMIND_DTYPE_F32:
+        return go2(indexer_topk_sliced_kernel<float>, static_cast<const float*>(q), static_cast<const float*>(keys));
+      case SNAPMIND_DTYPE_BF16:
+        return go2(indexer_topk_sliced_kernel<__nv_bfloat16>, static_cast<const __nv_bfloat16*>(q),
+                   static_cast<const __nv_bfloat16*>(keys));
+      default:
+        return go2(indexer_topk_sliced_kernel<__half>, static_cast<const __half*>(q), static_cast<const __half*>(keys));
+    }
+  }
   int sort_n = 1;
   while (sort_n < max_chunks) sort_n <<= 1;
   const size_t smem = sizeof(unsigned long long) * sort_n;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto go = [&](auto kernel, const auto* qq, const auto* kk) -> int {
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -1,18 +1,22 @@
 // Tensor-core sparse MLA decode (bf16/f16, kv_lora_rank 512, rope 64,
 // 64-token chunks) for sm_100a.
 //
-// CTA = (split, group of 16 heads, sequence), 4 warps.  The 16 heads of the
-// group are the M dimension of mma.sync m16n8k16 — a dense tile, which is why
-// this kernel uses tensor cores while the paged GQA decode (query group <= 8)
-// is byte-bound anyway.  Per 64-token tile of attended positions:
+// CTA = (split, group of 16 MT heads, sequence), 4 MT warps (MT = 2 when the
+// heads divide by 32).  Each m-tile of 16 heads is the M dimension of
+// mma.sync m16n8k16 — a dense tile, which is why this kernel uses tensor cores
+// while the paged GQA decode (query group <= 8) is byte-bound anyway.  Per
+// 64-token tile of attended positions:
 //   * latent + rope rows (1152 bytes) are staged by cp.async into rows padded
 //     to 1168 bytes (ldmatrix of 8 consecutive rows hits 8 distinct bank
 //     groups), double-buffered; rows outside the selection are zero-filled;
-//   * S = Q K^T: warp w owns tokens [16w, 16w+16): 36 k-steps x 2 MMAs;
-//   * the tile's row maxima / sums are merged across the 4 warps in shared
-//     memory (online softmax in base 2, scale folded in), P is staged as bf16;
-//   * O += P V: warp w owns output dims [128w, 128w+128): 4 k-steps x 16 MMAs,
-//     V^T fragments via ldmatrix.trans.
+//     the staged tile serves every m-tile of the CTA;
+//   * S = Q K^T: warp (mt, w4) owns tokens [16 w4, 16 w4 + 16) of m-tile mt:
+//     36 k-steps x 2 MMAs on two alternating accumulator chains;
+//   * the tile's row maxima / sums are merged across the 4 warps of an m-tile
+//     in shared memory (online softmax in base 2, scale folded in), P is
+//     staged as bf16;
+//   * O += P V: warp (mt, w4) owns output dims [128 w4, 128 w4 + 128):
+//     4 k-steps x 16 MMAs, V^T fragments via ldmatrix.trans.
 // Splits merge through the last-ticket combine of the paged GQA decode.
 #include "common.cuh"
 #include "paged_decode.cuh"
@@ -25,8 +29,6 @@ constexpr int kR = 512, kP = 64, kRow = kR + kP;  // 576 elements
 constexpr int kRowBytes = kRow * 2 + 16;          // padded smem row: 1168 bytes
 constexpr int kTileRows = 64;
 constexpr int kPRowBytes = kTileRows * 2 + 16;    // P row: 144 bytes
-constexpr int kWarps = 4;
-constexpr int kThreadsTc = kWarps * 32;
 constexpr int kBits = 8192;                       // chunks per sequence (bitmaps)
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -76,20 +78,22 @@ __device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
   return (uint32_t)(*reinterpret_cast<uint16_t*>(&a)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&b)) << 16);
 }
 
+constexpr int kMaxWarps = 8;
+
 struct TcSmem {
   uint32_t sel_bits[kBits / 32];
   uint32_t inc_bits[kBits / 32];
   int32_t word_pre[kBits / 32 + 1];  // included chunks before each bitmap word
-  float red_max[kWarps][16];
-  float red_sum[kWarps][16];
+  float red_max[kMaxWarps][16];
+  float red_sum[kMaxWarps][16];
   int32_t tile_chunk[2];
 };
 
-// smem: [Q: 16 rows][KV: 2 x 64 rows][P: 16 rows x 144 B][TcSmem]
-constexpr size_t kQBytes = 16 * kRowBytes;
+// smem: [Q: 16 MT rows][KV: 2 x 64 rows][P: 16 MT rows x 144 B][TcSmem]
 constexpr size_t kKvBytes = (size_t)kTileRows * kRowBytes;
-constexpr size_t kPBytes = 16 * kPRowBytes;
-constexpr size_t kTcSmem = kQBytes + 2 * kKvBytes + kPBytes + sizeof(TcSmem) + 128;
+constexpr size_t tc_smem_bytes(int mt) {
+  return (size_t)16 * mt * kRowBytes + 2 * kKvBytes + (size_t)16 * mt * kPRowBytes + sizeof(TcSmem) + 128;
+}
 
 // chunk id of the rank-th included chunk (rank < count)
 __device__ __forceinline__ int chunk_of_rank(const TcSmem& S, int words, int rank) {
@@ -104,8 +108,17 @@ __device__ __forceinline__ int chunk_of_rank(const TcSmem& S, int words, int ran
   return lo * 32 + __ffs(word) - 1;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparseParams p) {
+// MT m-tiles of 16 heads per CTA, 4 warps per m-tile: warp = 4 mt + w4.
+// S = Q K^T: warp (mt, w4) scores heads [16 mt, 16 mt + 16) against tokens
+// [16 w4, 16 w4 + 16) of the tile; O += P V: warp (mt, w4) owns those heads x
+// latent dims [128 w4, 128 w4 + 128).  The K/V tile in shared memory serves
+// all m-tiles.
+template <typename T, int MT>
+__global__ void __launch_bounds__(128 * MT, 1) sparse_mla_tc_kernel(SparseParams p) {
+  constexpr int kWarps = 4 * MT;
+  constexpr int kThreads = 32 * kWarps;
+  constexpr size_t kQBytes = (size_t)16 * MT * kRowBytes;
+  constexpr size_t kPBytes = (size_t)16 * MT * kPRowBytes;
   extern __shared__ __align__(128) unsigned char sm_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(sm_raw) + 127) & ~uintptr_t(127));
   unsigned char* q_s = base;
@@ -116,6 +129,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
 
   const int s = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int mt = warp >> 2, w4 = warp & 3;
   const int g = lane >> 2, tig = lane & 3;
   const int bs = kTileRows;
 
@@ -128,12 +142,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
     len = kBits * bs;
   }
   const int words = (n_chunks + 31) / 32;
-  for (int i = tid; i < words; i += kThreadsTc) {
+  for (int i = tid; i < words; i += kThreads) {
     S.sel_bits[i] = 0u;
     S.inc_bits[i] = 0u;
   }
   __syncthreads();
-  for (int i = tid; i < p.k; i += kThreadsTc) {
+  for (int i = tid; i < p.k; i += kThreads) {
     const int c = p.selected[(int64_t)b * p.k + i];
     if (c >= 0 && c < n_chunks) {
       atomicOr(&S.sel_bits[c >> 5], 1u << (c & 31));
@@ -144,7 +158,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
   const int wstart = max(0, len - p.window);
   if (tid == 0 && sink > 0) atomicOr(&S.inc_bits[0], 1u);
   if (len > wstart)
-    for (int c = wstart / bs + tid; c < n_chunks; c += kThreadsTc) atomicOr(&S.inc_bits[c >> 5], 1u << (c & 31));
+    for (int c = wstart / bs + tid; c < n_chunks; c += kThreads) atomicOr(&S.inc_bits[c >> 5], 1u << (c & 31));
   __syncthreads();
   if (warp == 0) {  // exclusive prefix of popcounts per word
     int carry = 0;
@@ -164,9 +178,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
       s_count = carry;
     }
   }
-  // Q rows of the head group (q_lat | q_pe), bf16/f16, padded
-  const int h0 = hg * 16;
-  for (int i = tid; i < 16 * (kRow / 8); i += kThreadsTc) {
+  // Q rows of the CTA's heads (q_lat | q_pe), bf16/f16, padded
+  const int h0 = hg * 16 * MT;
+  for (int i = tid; i < 16 * MT * (kRow / 8); i += kThreads) {
     const int h = i / (kRow / 8), v = i - h * (kRow / 8);
     const T* src = v < kR / 8 ? reinterpret_cast<const T*>(p.q_lat) + ((int64_t)b * p.n_heads + h0 + h) * kR + v * 8
                               : reinterpret_cast<const T*>(p.q_pe) + ((int64_t)b * p.n_heads + h0 + h) * kP + (v - kR / 8) * 8;
@@ -176,7 +190,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
   const int count = s_count;
   if (count == 0) {
     if (s == 0) {
-      for (int i = tid; i < 16 * kR; i += kThreadsTc) {
+      for (int i = tid; i < 16 * MT * kR; i += kThreads) {
         T* o = reinterpret_cast<T*>(p.dp.out) + (int64_t)b * p.dp.out_stride_seq +
                (int64_t)(h0 + i / kR) * p.dp.out_stride_head;
         o[i % kR] = Conv<T>::from_f(0.f);
@@ -188,7 +202,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
   const int r_lo = min(count, s * per), r_hi = min(count, r_lo + per);
   const int n_tiles = r_hi - r_lo;
 
-  // stage one chunk's rows into buffer `buf`
+  // stage one chunk's rows into buffer `buf`: warp w copies rows w, w + kWarps, ...;
+  // lanes copy the 72 16-byte vectors of a row (latent 64, rope 8)
   auto stage = [&](int tile, int buf) {
     const int c = chunk_of_rank(S, words, r_lo + tile);
     int32_t phys = c < p.table_width ? p.tables[(int64_t)b * p.table_stride + c] : -1;
@@ -199,29 +214,32 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
     const T* lat = reinterpret_cast<const T*>(p.latent) + (int64_t)max(phys, 0) * bs * kR;
     const T* rp = reinterpret_cast<const T*>(p.rope) + (int64_t)max(phys, 0) * bs * kP;
     unsigned char* dst = kv_s + buf * kKvBytes;
-    for (int i = tid; i < bs * (kRow / 8); i += kThreadsTc) {
-      const int r = i / (kRow / 8), v = i - r * (kRow / 8);
+    for (int r = warp; r < bs; r += kWarps) {
       const int pos = c * bs + r;
       const bool valid = phys >= 0 && pos < len && (selected || pos < sink || pos >= wstart);
-      const T* src = v < kR / 8 ? lat + (int64_t)r * kR + v * 8 : rp + (int64_t)r * kP + (v - kR / 8) * 8;
-      cp_async16(smem_u32(dst + r * kRowBytes + v * 16), src, valid);
+      const uint32_t drow = smem_u32(dst + r * kRowBytes);
+      cp_async16(drow + lane * 16, lat + (int64_t)r * kR + lane * 8, valid);
+      cp_async16(drow + (lane + 32) * 16, lat + (int64_t)r * kR + (lane + 32) * 8, valid);
+      if (lane < kRow / 8 - 64) cp_async16(drow + (lane + 64) * 16, rp + (int64_t)r * kP + lane * 8, valid);
     }
   };
 
   const float c2 = p.scale * 1.4426950408889634f;
-  float m_run[2] = {-INFINITY, -INFINITY};  // heads g, g+8
+  float m_run[2] = {-INFINITY, -INFINITY};  // heads g, g+8 of this warp's m-tile
   float l_run[2] = {0.f, 0.f};
   float o[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
   // ldmatrix lane addressing
-  const int a_row = (lane & 7) + ((lane >> 3) & 1) * 8;  // Q / P rows 0-15
+  const int a_row = (lane & 7) + ((lane >> 3) & 1) * 8;  // Q / P rows 0-15 of the m-tile
   const int a_kof = (lane >> 4) * 8;                      // +8 elements for matrices 2,3
   const int b_tok = (lane & 7) + ((lane >> 4) & 1) * 8;   // K rows (tokens) for B non-trans
   const int b_kof = ((lane >> 3) & 1) * 8;
   const int v_tok = (lane & 7) + ((lane >> 3) & 1) * 8;   // V^T: tokens 0-15 (matrices 0,1 / 2,3)
   const int v_dof = (lane >> 4) * 8;
+  const unsigned char* q_rows = q_s + (16 * mt + a_row) * kRowBytes;
+  unsigned char* p_rows = p_s + 16 * mt * kPRowBytes;
 
   if (n_tiles > 0) {
     stage(0, 0);
@@ -235,23 +253,33 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
     __syncthreads();
     const int c = S.tile_chunk[buf];
     const unsigned char* kv = kv_s + buf * kKvBytes;
-    // ---- S = Q K^T for tokens [16w, 16w+16)
+    // ---- S = Q K^T for tokens [16 w4, 16 w4 + 16): two accumulator chains (even / odd k)
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll 4
-    for (int k = 0; k < kRow / 16; ++k) {
+    float sd[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const unsigned char* k_rows = kv + (16 * w4 + b_tok) * kRowBytes;
+#pragma unroll 2
+    for (int k = 0; k < kRow / 16; k += 2) {
       uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-      ldsm4(smem_u32(q_s + a_row * kRowBytes + (k * 16 + a_kof) * 2), a0, a1, a2, a3);
-      ldsm4(smem_u32(kv + (16 * warp + b_tok) * kRowBytes + (k * 16 + b_kof) * 2), b0, b1, b2, b3);
+      ldsm4(smem_u32(q_rows + (k * 16 + a_kof) * 2), a0, a1, a2, a3);
+      ldsm4(smem_u32(k_rows + (k * 16 + b_kof) * 2), b0, b1, b2, b3);
       mma<T>(sc[0], a0, a1, a2, a3, b0, b1);
       mma<T>(sc[1], a0, a1, a2, a3, b2, b3);
+      ldsm4(smem_u32(q_rows + ((k + 1) * 16 + a_kof) * 2), a0, a1, a2, a3);
+      ldsm4(smem_u32(k_rows + ((k + 1) * 16 + b_kof) * 2), b0, b1, b2, b3);
+      mma<T>(sd[0], a0, a1, a2, a3, b0, b1);
+      mma<T>(sd[1], a0, a1, a2, a3, b2, b3);
     }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[nt][e] += sd[nt][e];
     // validity of this thread's 4 token columns
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int r = 16 * warp + nt * 8 + 2 * tig + e;
+        const int r = 16 * w4 + nt * 8 + 2 * tig + e;
         const int pos = c * bs + r;
         const bool selected = c >= 0 && ((S.sel_bits[c >> 5] >> (c & 31)) & 1u);
         const bool valid = c >= 0 && pos < len && (selected || pos < sink || pos >= wstart);
@@ -278,7 +306,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
     for (int hh = 0; hh < 2; ++hh) {
       float tm = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) tm = fmaxf(tm, S.red_max[w][g + 8 * hh]);
+      for (int w = 0; w < 4; ++w) tm = fmaxf(tm, S.red_max[4 * mt + w][g + 8 * hh]);
       m_new[hh] = fmaxf(m_run[hh], tm);
       alpha[hh] = (m_run[hh] == -INFINITY) ? 0.f : exp2f((m_run[hh] - m_new[hh]) * c2);
     }
@@ -292,9 +320,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
         pv[e] = (m_new[hh] == -INFINITY) ? 0.f : exp2f((sc[nt][e] - m_new[hh]) * c2);
         ps[hh] += pv[e];
       }
-      const int col = 16 * warp + nt * 8 + 2 * tig;
-      *reinterpret_cast<uint32_t*>(p_s + g * kPRowBytes + col * 2) = pack_pair<T>(pv[0], pv[1]);
-      *reinterpret_cast<uint32_t*>(p_s + (g + 8) * kPRowBytes + col * 2) = pack_pair<T>(pv[2], pv[3]);
+      const int col = 16 * w4 + nt * 8 + 2 * tig;
+      *reinterpret_cast<uint32_t*>(p_rows + g * kPRowBytes + col * 2) = pack_pair<T>(pv[0], pv[1]);
+      *reinterpret_cast<uint32_t*>(p_rows + (g + 8) * kPRowBytes + col * 2) = pack_pair<T>(pv[2], pv[3]);
     }
 #pragma unroll
     for (int off = 1; off < 4; off <<= 1) {
@@ -310,11 +338,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
     for (int hh = 0; hh < 2; ++hh) {
       float tsum = 0.f;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) tsum += S.red_sum[w][g + 8 * hh];
+      for (int w = 0; w < 4; ++w) tsum += S.red_sum[4 * mt + w][g + 8 * hh];
       l_run[hh] = l_run[hh] * alpha[hh] + tsum;
       m_run[hh] = m_new[hh];
     }
-    // ---- O (16 heads x dims [128w, 128w+128)) += P V
+    // ---- O (16 heads x dims [128 w4, 128 w4 + 128)) += P V
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt) {
       o[nt][0] *= alpha[0];
@@ -325,10 +353,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
 #pragma unroll
     for (int ks = 0; ks < kTileRows / 16; ++ks) {
       uint32_t a0, a1, a2, a3;
-      ldsm4(smem_u32(p_s + a_row * kPRowBytes + (ks * 16 + a_kof) * 2), a0, a1, a2, a3);
+      ldsm4(smem_u32(p_rows + a_row * kPRowBytes + (ks * 16 + a_kof) * 2), a0, a1, a2, a3);
 #pragma unroll
       for (int np = 0; np < 8; ++np) {
-        const int d0 = 128 * warp + np * 16;
+        const int d0 = 128 * w4 + np * 16;
         uint32_t b0, b1, b2, b3;
         ldsm4t(smem_u32(kv + (ks * 16 + v_tok) * kRowBytes + (d0 + v_dof) * 2), b0, b1, b2, b3);
         mma<T>(o[2 * np], a0, a1, a2, a3, b0, b1);
@@ -347,8 +375,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int hh = e >> 1;
-      const int head = g + 8 * hh;
-      const int d = 128 * warp + nt * 8 + 2 * tig + (e & 1);
+      const int head = 16 * mt + g + 8 * hh;
+      const int d = 128 * w4 + nt * 8 + 2 * tig + (e & 1);
       if (direct) {
         T* out = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)(h0 + head) * dp.out_stride_head;
         out[d] = Conv<T>::from_f(l_run[hh] > 0.f ? o[nt][e] / l_run[hh] : 0.f);
@@ -363,18 +391,21 @@ __global__ void __launch_bounds__(kThreadsTc, 1) sparse_mla_tc_kernel(SparsePara
     }
   }
   if (direct) return;
+  // one ticket per CTA, on the counter of its first 16-head group
   __shared__ int s_last;
   __threadfence();
   __syncthreads();
+  const int grp0 = hg * MT;
   if (tid == 0) {
-    const int ticket = atomicAdd(&dp.counters[b * dp.n_kv_heads + hg], 1);
+    const int ticket = atomicAdd(&dp.counters[b * dp.n_kv_heads + grp0], 1);
     s_last = (ticket == p.n_splits - 1);
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  combine_splits<T>(dp, b, hg, p.n_splits, reinterpret_cast<float*>(base));
-  if (tid == 0) dp.counters[b * dp.n_kv_heads + hg] = 0;
+#pragma unroll
+  for (int m = 0; m < MT; ++m) combine_splits<T>(dp, b, grp0 + m, p.n_splits, reinterpret_cast<float*>(base));
+  if (tid == 0) dp.counters[b * dp.n_kv_heads + grp0] = 0;
 }
 
 }  // namespace
@@ -387,14 +418,20 @@ bool sparse_mla_tc_supported(const SparseParams& p, int dtype) {
 }
 
 int launch_sparse_mla_tc(const SparseParams& p, int dtype, cudaStream_t st) {
-  dim3 grid(p.n_splits, p.n_heads / 16, p.batch);
-  auto go = [&](auto kernel) -> int {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+  // 32 heads (two m-tiles, 8 warps) per CTA when they divide evenly
+  const int mt = p.n_heads % 32 == 0 ? 2 : 1;
+  dim3 grid(p.n_splits, p.n_heads / (16 * mt), p.batch);
+  auto go = [&](auto kernel, size_t smem) -> int {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_status(e, "sparse_mla_tc smem attribute");
-    kernel<<<grid, kThreadsTc, kTcSmem, st>>>(p);
+    kernel<<<grid, 128 * mt, smem, st>>>(p);
     return cuda_status(cudaGetLastError(), "sparse_mla_tc launch");
   };
-  return dtype == SNAPMIND_DTYPE_BF16 ? go(sparse_mla_tc_kernel<__nv_bfloat16>) : go(sparse_mla_tc_kernel<__half>);
+  if (dtype == SNAPMIND_DTYPE_BF16) {
+    return mt == 2 ? go(sparse_mla_tc_kernel<__nv_bfloat16, 2>, tc_smem_bytes(2))
+                   : go(sparse_mla_tc_kernel<__nv_bfloat16, 1>, tc_smem_bytes(1));
+  }
+  return mt == 2 ? go(sparse_mla_tc_kernel<__half, 2>, tc_smem_bytes(2)) : go(sparse_mla_tc_kernel<__half, 1>, tc_smem_bytes(1));
 }
 
 }  // namespace snapmind

@@ -146,6 +146,7 @@ class ChunkSelector:
         self.bias = float(torch.randn(1, generator=g).item() * 0.02)
         self.max_chunks = pool.max_blocks_per_seq
         self.keys = torch.zeros((pool.max_seqs, self.max_chunks, index_dim), dtype=torch.float32, device=pool.device)
+        self._topk_ws: torch.Tensor | None = None
 
     def update_keys(self, layer: int, chunk_begin: int, chunk_count: int, batch: int | None = None) -> None:
         """Pool + project chunks [chunk_begin, chunk_begin + chunk_count) of each sequence."""
@@ -171,9 +172,14 @@ class ChunkSelector:
         sc = torch.empty((batch, k), dtype=torch.float32, device=q.device)
         full = torch.empty((batch, self.max_chunks), dtype=torch.float32, device=q.device) if all_scores else None
         nc_ptr, nc0 = (None, int(n_chunks)) if isinstance(n_chunks, int) else (n_chunks.data_ptr(), 0)
-        status = _lib.load().snapmind_indexer_topk(
+        lib = _lib.load()
+        need = lib.snapmind_indexer_topk_workspace_bytes(batch, self.max_chunks, k)
+        if self._topk_ws is None or self._topk_ws.numel() < need:
+            self._topk_ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=q.device)  # left zeroed
+        status = lib.snapmind_indexer_topk(
             q.data_ptr(), self.keys.data_ptr(), _lib.dtype_code(torch.float32), nc_ptr, nc0, batch,
             self.max_chunks, self.index_dim, self.index_dim ** -0.5, self.bias, k,
-            idx.data_ptr(), sc.data_ptr(), None if full is None else full.data_ptr(), _lib.stream_handle(q.device))
+            idx.data_ptr(), sc.data_ptr(), None if full is None else full.data_ptr(),
+            self._topk_ws.data_ptr(), self._topk_ws.numel(), _lib.stream_handle(q.device))
         _lib.check(status, "ChunkSelector.select")
         return (idx, sc, full) if all_scores else (idx, sc)

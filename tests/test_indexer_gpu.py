@@ -113,19 +113,67 @@ def test_chunk_selector_keys_and_stable_topk(cuda_device):
         np.testing.assert_allclose(sc[b, : len(valid)].cpu().numpy(), s_all[valid], rtol=0, atol=0)
 
 
-def test_topk_tie_break_on_equal_scores(cuda_device):
+@pytest.mark.parametrize("sliced", [False, True])
+def test_topk_tie_break_on_equal_scores(cuda_device, sliced):
     from snapmind_b200 import _lib
 
-    B, C, D, k = 2, 100, 8, 10
+    B, C, D, k = 2, 300, 8, 10
     keys = torch.zeros((B, C, D), device="cuda")
     keys[:, ::7, 0] = 1.0  # chunks 0, 7, 14, ... tie at the top score, the rest tie below
     q = torch.ones((B, D), device="cuda")
     idx = torch.empty((B, k), dtype=torch.int32, device="cuda")
-    rc = _lib.load().snapmind_indexer_topk(q.data_ptr(), keys.data_ptr(), 0, None, C, B, C, D, 1.0, 0.0, k,
-                                           idx.data_ptr(), None, None, _lib.stream_handle())
+    lib = _lib.load()
+    ws = torch.zeros(lib.snapmind_indexer_topk_workspace_bytes(B, C, k), dtype=torch.uint8, device="cuda")
+    rc = lib.snapmind_indexer_topk(q.data_ptr(), keys.data_ptr(), 0, None, C, B, C, D, 1.0, 0.0, k,
+                                   idx.data_ptr(), None, None, ws.data_ptr() if sliced else None, ws.numel(),
+                                   _lib.stream_handle())
     _lib.check(rc, "topk")
     want = [0, 7, 14, 21, 28, 35, 42, 49, 56, 63]
     assert idx.cpu().tolist() == [want, want]
+    assert int(ws[: 4 * B].count_nonzero()) == 0  # tickets reset; candidates are scratch
+    # only the chunks past 128 tie at the top: the winners come from later slices
+    keys.zero_()
+    keys[:, 130::9, 0] = 1.0
+    rc = lib.snapmind_indexer_topk(q.data_ptr(), keys.data_ptr(), 0, None, C, B, C, D, 1.0, 0.0, k,
+                                   idx.data_ptr(), None, None, ws.data_ptr() if sliced else None, ws.numel(),
+                                   _lib.stream_handle())
+    _lib.check(rc, "topk")
+    want = list(range(130, 300, 9))[:k]
+    assert idx.cpu().tolist() == [want, want]
+
+
+@pytest.mark.parametrize("k,n_chunks", [(32, [2048, 1500, 7]), (200, [600, 129, 1000]), (5, [1, 0, 257])])
+def test_topk_sliced_equals_single_cta(cuda_device, k, n_chunks):
+    """Both kernels against the oracle's stable top-k of the scores, at sizes
+    where slices, ragged lengths and k > 128 (all candidates kept) occur."""
+    from snapmind_b200 import _lib
+
+    B, C, D = len(n_chunks), 2050, 128
+    g = torch.Generator(device="cpu").manual_seed(k)
+    keys = torch.randn((B, C, D), generator=g).cuda()
+    keys[0, 1000:1010] = keys[0, 999]  # exact ties across a slice boundary
+    q = torch.randn((B, D), generator=g).cuda()
+    nct = torch.tensor(n_chunks, dtype=torch.int32, device="cuda")
+    lib = _lib.load()
+    ws = torch.zeros(lib.snapmind_indexer_topk_workspace_bytes(B, C, k), dtype=torch.uint8, device="cuda")
+    got = []
+    for sliced in (False, True):
+        idx = torch.empty((B, k), dtype=torch.int32, device="cuda")
+        sc = torch.empty((B, k), dtype=torch.float32, device="cuda")
+        full = torch.empty((B, C), dtype=torch.float32, device="cuda")
+        rc = lib.snapmind_indexer_topk(q.data_ptr(), keys.data_ptr(), 0, nct.data_ptr(), 0, B, C, D, D ** -0.5, 0.1,
+                                       k, idx.data_ptr(), sc.data_ptr(), full.data_ptr(),
+                                       ws.data_ptr() if sliced else None, ws.numel(), _lib.stream_handle())
+        _lib.check(rc, "topk")
+        got.append((idx.cpu().numpy(), sc.cpu().numpy(), full.cpu().numpy()))
+        for b in range(B):
+            s_all = full[b, : n_chunks[b]].cpu().numpy()
+            want = oidx.stable_topk(s_all, k).tolist()
+            assert idx[b].cpu().numpy().tolist() == want
+    assert (got[0][0] == got[1][0]).all()
+    for b in range(B):
+        np.testing.assert_array_equal(got[0][2][b, : n_chunks[b]], got[1][2][b, : n_chunks[b]])
+    assert int(ws[: 4 * B].count_nonzero()) == 0  # tickets reset
 
 
 @pytest.mark.parametrize("sink,window,n_splits", [(4, 1024, 4), (0, 0, 1), (4, 200, 3), (70, 5000, 2)])
