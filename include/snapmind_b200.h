@@ -227,7 +227,16 @@ SNAPMIND_API int snapmind_indexer_pool_chunks(const void *pool, int dtype, int64
                                  const int32_t *seq_lens, int32_t batch, int32_t block_size,
                                  int32_t num_blocks, int32_t chunk_begin, int32_t chunk_count,
                                  int32_t max_chunks, const void *proj, int proj_dtype, int32_t out_dim,
-                                 float *out, int32_t *err_word, void *stream);
+                                 float *out, void *workspace, int64_t workspace_bytes, int32_t *err_word,
+                                 void *stream);
+
+/*
+ * Bytes of workspace (fp32 chunk means) that lets snapmind_indexer_pool_chunks
+ * pool many chunks and project them in two kernels (a streaming mean over
+ * many chunks in flight, then a tiled projection).  Without it, or for a few
+ * chunks, one fused kernel does both (same result up to fp32 rounding).
+ */
+SNAPMIND_API int64_t snapmind_indexer_pool_workspace_bytes(int32_t batch, int32_t chunk_count, int32_t width);
 
 /*
  * The reference chunk score for every chunk at once (lookahead.py:82-106):

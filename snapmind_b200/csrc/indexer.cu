@@ -325,6 +325,168 @@ __global__ void __launch_bounds__(kPoolThreads, 1) indexer_pool_kernel(PoolParam
 }
 
 // ---------------------------------------------------------------------------
+// chunk means then projection, as two kernels (many chunks at once)
+// ---------------------------------------------------------------------------
+constexpr int kMeanThreads = 256;
+
+// One CTA per item: the mean of the chunk's rows (first W columns), fp32, into
+// means[item][W].  Row groups of threads sum with 16-byte loads, kPoolUnroll
+// rows in flight per thread; several CTAs per SM keep many chunks in flight.
+template <typename T>
+__global__ void __launch_bounds__(kMeanThreads) indexer_mean_kernel(PoolParams p, float* means, int vec_ok) {
+  extern __shared__ __align__(16) float mpart[];  // [groups][W]
+  const int W = p.width;
+  const int64_t it = blockIdx.x;
+  int b, c, n, phys;
+  pool_item(p, it, b, c, n, phys);
+  float* out = means + it * W;
+  const int tid = threadIdx.x;
+  if (phys < 0) {
+    for (int d = tid; d < W; d += kMeanThreads) out[d] = 0.f;
+    return;
+  }
+  const T* rows = reinterpret_cast<const T*>(p.pool) + (int64_t)phys * p.block_size * p.row_width;
+  const float inv = 1.f / (float)n;
+  if (!vec_ok) {
+    for (int d = tid; d < W; d += kMeanThreads) {
+      float acc = 0.f;
+      for (int r = 0; r < n; ++r) acc += Conv<T>::to_f(rows[(int64_t)r * p.row_width + d]);
+      out[d] = acc * inv;
+    }
+    return;
+  }
+  constexpr int EPV = 16 / (int)sizeof(T);
+  const int n_vec = W / EPV;
+  const int groups = kMeanThreads / n_vec;
+  const int j = tid % n_vec, g = tid / n_vec;
+  if (g < groups) {
+    float acc[EPV];
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) acc[e] = 0.f;
+    for (int r0 = g; r0 < n; r0 += groups * kPoolUnroll) {
+      uint4 v[kPoolUnroll];
+#pragma unroll
+      for (int u = 0; u < kPoolUnroll; ++u) {
+        const int r = r0 + u * groups;
+        v[u] = r < n ? *reinterpret_cast<const uint4*>(rows + (int64_t)r * p.row_width + j * EPV)
+                     : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kPoolUnroll; ++u) {
+        const T* x = reinterpret_cast<const T*>(&v[u]);
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) acc[e] += Conv<T>::to_f(x[e]);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) mpart[g * W + j * EPV + e] = acc[e];
+  }
+  __syncthreads();
+  for (int d = tid; d < W; d += kMeanThreads) {
+    float acc = 0.f;
+    for (int gg = 0; gg < groups; ++gg) acc += mpart[gg * W + d];
+    out[d] = acc * inv;
+  }
+}
+
+constexpr int kProjTile = 64;   // items and outputs per CTA
+constexpr int kProjK = 32;      // columns per step
+constexpr int kProjPad = 68;    // smem row stride (floats): 16-byte aligned rows
+
+// 8 consecutive elements as floats; 16-byte loads when `vec` (aligned rows).
+__device__ __forceinline__ void load8(const float* src, bool valid, bool vec, int n_left, float* dst) {
+  if (valid && vec) {
+    const float4 x = *reinterpret_cast<const float4*>(src), y = *reinterpret_cast<const float4*>(src + 4);
+    dst[0] = x.x; dst[1] = x.y; dst[2] = x.z; dst[3] = x.w;
+    dst[4] = y.x; dst[5] = y.y; dst[6] = y.z; dst[7] = y.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dst[e] = (valid && e < n_left) ? src[e] : 0.f;
+  }
+}
+template <typename TP>
+__device__ __forceinline__ void load8(const TP* src, bool valid, bool vec, int n_left, float* dst) {
+  if (valid && vec) {
+    const uint4 x = *reinterpret_cast<const uint4*>(src);
+    const TP* t = reinterpret_cast<const TP*>(&x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dst[e] = Conv<TP>::to_f(t[e]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dst[e] = (valid && e < n_left) ? Conv<TP>::to_f(src[e]) : 0.f;
+  }
+}
+
+// out[b][c][o] = sum_d means[item][d] * P[o][d] for 64 items x 64 outputs per
+// CTA; each thread accumulates 4 items x 4 outputs in fp32, summing d in order.
+// The next 32 columns of both operands are loaded into registers while the
+// current ones are multiplied.
+template <typename TP>
+__global__ void __launch_bounds__(256) indexer_project_kernel(PoolParams p, const float* means, int64_t items) {
+  __shared__ __align__(16) float As[kProjK][kProjPad];  // [d][item]
+  __shared__ __align__(16) float Bs[kProjK][kProjPad];  // [d][output]
+  const int tid = threadIdx.x;
+  const int W = p.width, O = p.out_dim;
+  const int64_t item0 = (int64_t)blockIdx.x * kProjTile;
+  const int o0 = blockIdx.y * kProjTile;
+  const TP* P = reinterpret_cast<const TP*>(p.proj);
+  const int ti = tid >> 4, to = tid & 15;            // 4 items x 4 outputs
+  const int l_row = tid & 63, l_k = (tid >> 6) * 8;  // loader: row, 8 columns
+  const int64_t l_item = item0 + l_row;
+  const int l_o = o0 + l_row;
+  const bool a_ok = l_item < items, b_ok = l_o < O;
+  const bool vec_a = (W % 4 == 0) && ((reinterpret_cast<uintptr_t>(means) & 15) == 0);
+  const bool vec_b = (W % 8 == 0) && ((reinterpret_cast<uintptr_t>(P) & 15) == 0) && sizeof(TP) == 2;
+  const float* a_src = means + (a_ok ? l_item : 0) * W + l_k;
+  const TP* b_src = P + (int64_t)(b_ok ? l_o : 0) * W + l_k;
+  float a_reg[8], b_reg[8];
+  auto fetch = [&](int k0) {
+    const int left = W - (k0 + l_k);
+    load8(a_src + k0, a_ok && left > 0, vec_a && left >= 8, left, a_reg);
+    load8(b_src + k0, b_ok && left > 0, vec_b && left >= 8, left, b_reg);
+  };
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  fetch(0);
+  for (int k0 = 0; k0 < W; k0 += kProjK) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      As[l_k + e][l_row] = a_reg[e];
+      Bs[l_k + e][l_row] = b_reg[e];
+    }
+    __syncthreads();
+    if (k0 + kProjK < W) fetch(k0 + kProjK);
+#pragma unroll 8
+    for (int kk = 0; kk < kProjK; ++kk) {
+      const float4 a = *reinterpret_cast<const float4*>(&As[kk][ti * 4]);
+      const float4 w = *reinterpret_cast<const float4*>(&Bs[kk][to * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t item = item0 + ti * 4 + i;
+    if (item >= items) continue;
+    const int b = (int)(item / p.chunk_count);
+    const int c = p.chunk_begin + (int)(item - (int64_t)b * p.chunk_count);
+    float* out = p.out + ((int64_t)b * p.max_chunks + c) * O;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int o = o0 + to * 4 + j;
+      if (o < O) out[o] = acc[i][j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // reference score: one warp per chunk
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) indexer_score_ref_kernel(const float* q, const float* w, int n_rows,
@@ -565,11 +727,17 @@ using namespace snapmind;
 
 extern "C" {
 
+int64_t snapmind_indexer_pool_workspace_bytes(int32_t batch, int32_t chunk_count, int32_t width) {
+  if (batch <= 0 || chunk_count <= 0 || width <= 0) return 0;
+  return (int64_t)batch * chunk_count * width * (int64_t)sizeof(float);
+}
+
 int snapmind_indexer_pool_chunks(const void* pool, int dtype, int64_t row_width, int32_t width,
                                  const int32_t* block_tables, int64_t table_stride, int32_t table_width,
                                  const int32_t* seq_lens, int32_t batch, int32_t block_size, int32_t num_blocks,
                                  int32_t chunk_begin, int32_t chunk_count, int32_t max_chunks, const void* proj,
-                                 int proj_dtype, int32_t out_dim, float* out, int32_t* err_word, void* stream) {
+                                 int proj_dtype, int32_t out_dim, float* out, void* workspace,
+                                 int64_t workspace_bytes, int32_t* err_word, void* stream) {
   SNAPMIND_CHECK_ARG(dtype_size(dtype) > 0, "indexer_pool_chunks: unknown dtype");
   SNAPMIND_CHECK_ARG(width > 0 && width <= row_width && width <= 16384 && batch >= 0 && batch <= 65535 &&
                          block_size > 0 && chunk_begin >= 0 && chunk_count >= 0 &&
@@ -593,9 +761,35 @@ int snapmind_indexer_pool_chunks(const void* pool, int dtype, int64_t row_width,
   const size_t smem = (size_t)(cache_proj ? (proj_bytes + 15) / 16 * 16 : 0) + sizeof(float) * width * (1 + groups);
   SNAPMIND_CHECK_ARG(smem <= 220 * 1024, "indexer_pool_chunks: width too large for shared memory");
   const int64_t items = (int64_t)batch * chunk_count;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // many chunks with a projection and room for the means: two kernels
+  const int64_t ws_need = snapmind_indexer_pool_workspace_bytes(batch, chunk_count, width);
+  if (proj && workspace && workspace_bytes >= ws_need && items >= 4 * (int64_t)num_sms() &&
+      items <= 0x7fffffff && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0) {
+    float* means = static_cast<float*>(workspace);
+    const int mean_vec = vec_ok && kMeanThreads % n_vec == 0 && n_vec <= kMeanThreads;
+    const size_t msmem = mean_vec ? sizeof(float) * (size_t)width * (kMeanThreads / n_vec) : 0;
+    SNAPMIND_CHECK_ARG(msmem <= 48 * 1024, "indexer_pool_chunks: width too large for the mean kernel");
+    auto mean_go = [&](auto kernel) -> int {
+      kernel<<<(unsigned)items, kMeanThreads, msmem, st>>>(p, means, mean_vec);
+      return cuda_status(cudaGetLastError(), "indexer_mean launch");
+    };
+    int rc = dtype == SNAPMIND_DTYPE_F32    ? mean_go(indexer_mean_kernel<float>)
+             : dtype == SNAPMIND_DTYPE_BF16 ? mean_go(indexer_mean_kernel<__nv_bfloat16>)
+                                            : mean_go(indexer_mean_kernel<__half>);
+    if (rc != SNAPMIND_OK) return rc;
+    dim3 pgrid((unsigned)((items + kProjTile - 1) / kProjTile), (unsigned)((out_dim + kProjTile - 1) / kProjTile));
+    SNAPMIND_CHECK_ARG(pgrid.y <= 65535, "indexer_pool_chunks: out_dim too large");
+    auto proj_go = [&](auto kernel) -> int {
+      kernel<<<pgrid, 256, 0, st>>>(p, means, items);
+      return cuda_status(cudaGetLastError(), "indexer_project launch");
+    };
+    if (pd == SNAPMIND_DTYPE_F32) return proj_go(indexer_project_kernel<float>);
+    if (pd == SNAPMIND_DTYPE_BF16) return proj_go(indexer_project_kernel<__nv_bfloat16>);
+    return proj_go(indexer_project_kernel<__half>);
+  }
   const int per_sm = smem > 110 * 1024 ? 1 : 2;
   const int grid = (int)(items < (int64_t)num_sms() * per_sm ? items : (int64_t)num_sms() * per_sm);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto go = [&](auto kernel) -> int {
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -51,7 +51,7 @@ def chunk_means(k: torch.Tensor, width: int) -> torch.Tensor:
         status = lib.snapmind_indexer_pool_chunks(
             k3[i].data_ptr(), _lib.dtype_code(k3.dtype), w, width,
             table.data_ptr(), 1, 1, None, 1, t, 1, 0, 1, 1,
-            None, 0, 0, out[i].data_ptr(), None, _lib.stream_handle(k.device),
+            None, 0, 0, out[i].data_ptr(), None, 0, None, _lib.stream_handle(k.device),
         )  # fmt: skip
         _lib.check(status, "indexer chunk mean")
     return out.reshape(*lead, 1, width)
@@ -147,18 +147,27 @@ class ChunkSelector:
         self.max_chunks = pool.max_blocks_per_seq
         self.keys = torch.zeros((pool.max_seqs, self.max_chunks, index_dim), dtype=torch.float32, device=pool.device)
         self._topk_ws: torch.Tensor | None = None
+        self._pool_ws: torch.Tensor | None = None
 
     def update_keys(self, layer: int, chunk_begin: int, chunk_count: int, batch: int | None = None) -> None:
         """Pool + project chunks [chunk_begin, chunk_begin + chunk_count) of each sequence."""
         pool = self.pool
         batch = pool.max_seqs if batch is None else batch
-        status = _lib.load().snapmind_indexer_pool_chunks(
+        lib = _lib.load()
+        need = lib.snapmind_indexer_pool_workspace_bytes(batch, chunk_count, pool.kv_lora_rank)
+        if chunk_count * batch >= 1024:  # a bulk (re)build: room for the fp32 means
+            if self._pool_ws is None or self._pool_ws.numel() < need:
+                self._pool_ws = torch.empty(need, dtype=torch.uint8, device=pool.device)
+            ws, ws_bytes = self._pool_ws.data_ptr(), self._pool_ws.numel()
+        else:
+            ws, ws_bytes = None, 0
+        status = lib.snapmind_indexer_pool_chunks(
             pool.latent[layer].data_ptr(), pool._dcode, pool.kv_lora_rank, pool.kv_lora_rank,
             pool.block_tables.data_ptr(), pool.max_blocks_per_seq, pool.max_blocks_per_seq,
             pool.seq_lens.data_ptr(), batch, pool.block_size, pool.num_blocks,
             chunk_begin, chunk_count, self.max_chunks,
             self.w_k.data_ptr(), _lib.dtype_code(self.w_k.dtype), self.index_dim,
-            self.keys.data_ptr(), pool.err.data_ptr(), pool._stream(),
+            self.keys.data_ptr(), ws, ws_bytes, pool.err.data_ptr(), pool._stream(),
         )  # fmt: skip
         _lib.check(status, "ChunkSelector.update_keys")
 

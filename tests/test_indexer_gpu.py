@@ -113,6 +113,42 @@ def test_chunk_selector_keys_and_stable_topk(cuda_device):
         np.testing.assert_allclose(sc[b, : len(valid)].cpu().numpy(), s_all[valid], rtol=0, atol=0)
 
 
+def test_chunk_keys_bulk_two_kernel_path(cuda_device):
+    """A bulk key rebuild (>= 1024 chunks) goes through the mean + projection
+    kernels with a workspace; ragged last chunks and chunks past a sequence's
+    length (zeros) included.  Checked against the float64 mean and projection,
+    and against the fused kernel (no workspace) on the same chunks."""
+    from snapmind_b200 import _lib
+    from snapmind_b200.indexer import ChunkSelector
+
+    B, bs = 4, 64
+    lens = [64 * 300, 64 * 299 + 5, 64 * 120 + 63, 64 * 250]
+    pool, lat, rope, tables = _latent_pool(B, lens, bs=bs, seed=21)
+    sel = ChunkSelector(pool, d_model=256, index_dim=128, seed=2)
+    max_c = int(pool.max_blocks_per_seq)
+    sel.update_keys(0, 0, max_c, batch=B)  # 4 x 301 chunks: two-kernel path
+    assert sel._pool_ws is not None
+    two = sel.keys.clone()
+    # the fused kernel over the same chunks, through the ABI without a workspace
+    fused = torch.zeros_like(sel.keys)
+    rc = _lib.load().snapmind_indexer_pool_chunks(
+        pool.latent[0].data_ptr(), pool._dcode, 512, 512, pool.block_tables.data_ptr(), max_c, max_c,
+        pool.seq_lens.data_ptr(), B, bs, pool.num_blocks, 0, max_c, max_c, sel.w_k.data_ptr(),
+        _lib.dtype_code(sel.w_k.dtype), 128, fused.data_ptr(), None, 0, pool.err.data_ptr(), _lib.stream_handle())
+    _lib.check(rc, "pool fused")
+    pool.check()
+    wk = sel.w_k.float().cpu().numpy().astype(np.float64)
+    two_np, fused_np = two.cpu().numpy(), fused.cpu().numpy()
+    for b in range(B):
+        n_chunks = (lens[b] + bs - 1) // bs
+        rows = _seq_rows(lat, tables, b, lens[b], bs)
+        for c in range(n_chunks):
+            want = wk @ rows[c * bs:(c + 1) * bs].astype(np.float64).mean(axis=0)
+            np.testing.assert_allclose(two_np[b, c], want, rtol=1e-4, atol=1e-4)
+        assert not two_np[b, n_chunks:].any()
+    np.testing.assert_allclose(two_np, fused_np, rtol=1e-5, atol=1e-6)
+
+
 @pytest.mark.parametrize("sliced", [False, True])
 def test_topk_tie_break_on_equal_scores(cuda_device, sliced):
     from snapmind_b200 import _lib
