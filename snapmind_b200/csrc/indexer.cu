@@ -522,10 +522,65 @@ __device__ __forceinline__ uint32_t ordered_bits(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// 4 consecutive elements as float4 (aligned: 16 bytes for fp32, 8 for 16-bit types)
+__device__ __forceinline__ float4 load4f(const float* p) { return *reinterpret_cast<const float4*>(p); }
+template <typename T>
+__device__ __forceinline__ float4 load4f(const T* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const T* t = reinterpret_cast<const T*>(&u);
+  return make_float4(Conv<T>::to_f(t[0]), Conv<T>::to_f(t[1]), Conv<T>::to_f(t[2]), Conv<T>::to_f(t[3]));
+}
+
+constexpr int kDotChunks = 16;  // chunks per warp pass
+
+// One warp: q . key[c] for the kDotChunks chunks c0 .. c0 + 15 (0 for c >= nc);
+// lane u < kDotChunks returns chunk c0 + u.  With `vec` each lane reads 4
+// consecutive dims of every chunk row at once, so a pass is one round trip.
+template <typename T>
+__device__ __forceinline__ float warp_chunk_dots(const T* qb, const T* kb, int dim, int c0, int nc, bool vec,
+                                                 int lane) {
+  float dot[kDotChunks];
+#pragma unroll
+  for (int u = 0; u < kDotChunks; ++u) dot[u] = 0.f;
+  if (vec) {
+    for (int d = lane * 4; d < dim; d += 128) {
+      const float4 qv = load4f(qb + d);
+      float4 kv[kDotChunks];
+#pragma unroll
+      for (int u = 0; u < kDotChunks; ++u)
+        kv[u] = c0 + u < nc ? load4f(kb + (int64_t)(c0 + u) * dim + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < kDotChunks; ++u) {
+        dot[u] = fmaf(qv.x, kv[u].x, dot[u]);
+        dot[u] = fmaf(qv.y, kv[u].y, dot[u]);
+        dot[u] = fmaf(qv.z, kv[u].z, dot[u]);
+        dot[u] = fmaf(qv.w, kv[u].w, dot[u]);
+      }
+    }
+  } else {
+    for (int d = lane; d < dim; d += 32) {
+      const float qd = Conv<T>::to_f(qb[d]);
+#pragma unroll
+      for (int u = 0; u < kDotChunks; ++u)
+        if (c0 + u < nc) dot[u] = fmaf(qd, Conv<T>::to_f(kb[(int64_t)(c0 + u) * dim + d]), dot[u]);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kDotChunks; ++u) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], off);
+  }
+  float mine = dot[0];
+#pragma unroll
+  for (int u = 1; u < kDotChunks; ++u)
+    if (lane == u) mine = dot[u];
+  return mine;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kTopkThreads) indexer_topk_kernel(
     const T* q, const T* keys, const int32_t* n_chunks_arr, int n_chunks0, int max_chunks, int dim, float scale,
-    float bias, int k, int sort_n, int32_t* out_idx, float* out_score, float* all_scores) {
+    float bias, int k, int sort_n, int32_t* out_idx, float* out_score, float* all_scores, int vec) {
   extern __shared__ unsigned long long skeys[];  // [sort_n]
   const int b = blockIdx.x;
   int nc = n_chunks_arr ? n_chunks_arr[b] : n_chunks0;
@@ -533,30 +588,10 @@ __global__ void __launch_bounds__(kTopkThreads) indexer_topk_kernel(
   const T* qb = q + (int64_t)b * dim;
   const T* kb = keys + (int64_t)b * max_chunks * dim;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  // scores: each warp takes 8 chunks per pass so that 8 independent key rows are in flight
-  constexpr int kU = 8;
+  constexpr int kU = kDotChunks;
   for (int c0 = warp * kU; c0 < sort_n; c0 += nw * kU) {
-    float dot[kU];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) dot[u] = 0.f;
-    for (int d = lane; d < dim; d += 32) {
-      const float qd = Conv<T>::to_f(qb[d]);
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int c = c0 + u;
-        if (c < nc) dot[u] = fmaf(qd, Conv<T>::to_f(kb[(int64_t)c * dim + d]), dot[u]);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], off);
-    }
+    const float mine = warp_chunk_dots(qb, kb, dim, c0, nc, vec != 0, lane);
     if (lane < kU) {
-      float mine = dot[0];
-#pragma unroll
-      for (int u = 1; u < kU; ++u)
-        if (lane == u) mine = dot[u];
       const int c = c0 + lane;
       unsigned long long key = 0ull;  // below every real key
       if (c < nc) {
@@ -633,7 +668,7 @@ template <typename T>
 __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
     const T* q, const T* keys, const int32_t* n_chunks_arr, int n_chunks0, int max_chunks, int dim, float scale,
     float bias, int k, int n_slices, int keep, int merge_n, unsigned long long* cand, int32_t* tickets,
-    int32_t* out_idx, float* out_score, float* all_scores) {
+    int32_t* out_idx, float* out_score, float* all_scores, int vec) {
   extern __shared__ unsigned long long sk[];  // [max(kSliceChunks, merge_n)]
   __shared__ int s_last;
   const int slice = blockIdx.x, b = blockIdx.y;
@@ -643,29 +678,10 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
   const T* qb = q + (int64_t)b * dim;
   const T* kb = keys + (int64_t)b * max_chunks * dim;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  constexpr int kU = 8;  // chunks per warp pass: 8 independent key rows in flight
+  constexpr int kU = kDotChunks;
   for (int l0 = warp * kU; l0 < kSliceChunks; l0 += nw * kU) {
-    float dot[kU];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) dot[u] = 0.f;
-    for (int d = lane; d < dim; d += 32) {
-      const float qd = Conv<T>::to_f(qb[d]);
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int c = c_begin + l0 + u;
-        if (c < nc) dot[u] = fmaf(qd, Conv<T>::to_f(kb[(int64_t)c * dim + d]), dot[u]);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], off);
-    }
+    const float mine = warp_chunk_dots(qb, kb, dim, c_begin + l0, nc, vec != 0, lane);
     if (lane < kU) {
-      float mine = dot[0];
-#pragma unroll
-      for (int u = 1; u < kU; ++u)
-        if (lane == u) mine = dot[u];
       const int c = c_begin + l0 + lane;
       unsigned long long key = 0ull;  // below every real key
       if (c < nc) {
@@ -842,6 +858,9 @@ int snapmind_indexer_topk(const void* q, const void* keys, int dtype, const int3
   if (batch == 0) return SNAPMIND_OK;
   SNAPMIND_CHECK_ARG(q && keys && out_idx, "indexer_topk: null pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int esz = dtype_size(dtype);
+  const int vec = dim % 4 == 0 && (reinterpret_cast<uintptr_t>(q) % (4 * esz)) == 0 &&
+                  (reinterpret_cast<uintptr_t>(keys) % (4 * esz)) == 0;
   if (workspace) {
     const TopkPlan t = topk_plan(batch, max_chunks, k);
     SNAPMIND_CHECK_ARG(workspace_bytes >= t.total, "indexer_topk: workspace needs %lld bytes, got %lld",
@@ -858,7 +877,7 @@ int snapmind_indexer_topk(const void* q, const void* keys, int dtype, const int3
       }
       kernel<<<dim3(t.n_slices, batch), kSliceThreads, smem, st>>>(
           qq, kk, n_chunks, n_chunks0, max_chunks, dim, scale, bias, k, t.n_slices, t.keep, t.merge_n, cand, tickets,
-          out_idx, out_score, all_scores);
+          out_idx, out_score, all_scores, vec);
       return cuda_status(cudaGetLastError(), "indexer_topk launch");
     };
     switch (dtype) {
@@ -880,7 +899,7 @@ int snapmind_indexer_topk(const void* q, const void* keys, int dtype, const int3
       if (e != cudaSuccess) return cuda_status(e, "indexer_topk smem attribute");
     }
     kernel<<<batch, kTopkThreads, smem, st>>>(qq, kk, n_chunks, n_chunks0, max_chunks, dim, scale, bias, k, sort_n,
-                                              out_idx, out_score, all_scores);
+                                              out_idx, out_score, all_scores, vec);
     return cuda_status(cudaGetLastError(), "indexer_topk launch");
   };
   switch (dtype) {
