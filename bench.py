@@ -184,6 +184,12 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
     torch.cuda.set_device(dev)
     steps, warmup = args.steps, args.warmup
     seed = 1234 + 7919 * rank
+    if args.only == "e2e_llama":
+        r = run_e2e_llama(args, dev, seed, dist, world, cpu_baseline=not args.no_cpu_baseline and rank == 0)
+        return {"metric": METRIC, "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": steps,
+                "warmup": warmup, "ms_per_step": r["ms_per_token"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": r["workload"]},
+                "e2e_llama": r}
     if args.only in ("tiered", "mla"):
         fn = run_tiered if args.only == "tiered" else run_mla_sparse
         r = fn(args, dev, seed, dist, world)
@@ -341,10 +347,124 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
         "kv_append_gather": ag,
         "tiered": run_tiered(args, dev, seed, dist, world) if args.only == "all" else None,
         "mla_sparse": run_mla_sparse(args, dev, seed, dist, world) if args.only == "all" else None,
+        "e2e_llama": run_e2e_llama(args, dev, seed, dist, world, cpu_baseline=not args.no_cpu_baseline and rank == 0)
+        if args.only == "all" else None,
         "gpu_launches": launches_per_step * steps,
         "clocks": clocks.summary(),
     }
     return line
+
+
+# ----------------------------------------------------------------------------- TinyLlama end to end (config 1)
+E2E_PROMPT, E2E_GEN_MAX = 256, 256
+
+
+def _llama_harness():
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "tests"))
+    import llama_harness
+
+    return llama_harness
+
+
+def run_e2e_llama(args, dev, seed, dist, world, cpu_baseline: bool) -> dict:
+    """Greedy decode of a TinyLlama-shaped model (22 layers, d_model 2048, 32 q / 4 kv heads,
+    head_dim 64, fp32, random N(0, 0.02) weights) whose attention is the ``gqa_paged`` plugin
+    over a ``"paged"`` cache: one token per step, batch 1, after a 256-token prompt.  The next
+    token stays on the device (argmax), so steps queue without host syncs.  The CPU baseline
+    runs the same model with the reference attention math on the host cores."""
+    import torch
+
+    from snapmind_b200 import PagedGroupedQueryAttention, PagedKVCache
+
+    lh = _llama_harness()
+    sh = lh.TINYLLAMA
+    with torch.device(dev):
+        model = lh.LlamaHarness(sh, PagedGroupedQueryAttention)
+    g = torch.Generator(device=dev).manual_seed(seed + 60)
+    with torch.no_grad():
+        for _, prm in model.named_parameters():
+            if prm.dim() >= 2:
+                prm.normal_(0.0, 0.02, generator=g)
+            else:
+                prm.fill_(1.0)
+    model.eval()
+    hd = sh.d_model // sh.n_heads
+    cache = PagedKVCache(sh.max_seq_len, sh.n_layers, sh.n_kv_heads, hd,
+                         max_blocks=sh.n_layers * sh.max_seq_len // 16, device=dev)
+    kv = cache.layer_dicts()
+    prompt = lh.prompt_ids(sh.vocab_size, E2E_PROMPT, seed + 61).to(dev)
+    steps = max(1, min(args.steps, E2E_GEN_MAX))
+    warmup = args.warmup
+    with torch.no_grad():
+        logits = model(prompt[None], kv_cache=kv)[0, -1]
+        tok = logits.argmax(-1).view(1, 1)
+        pos = E2E_PROMPT
+
+        def step():
+            nonlocal tok, pos
+            out = model(tok, kv_cache=kv, position_ids=torch.tensor([pos], device=dev))
+            tok = out[0, -1].argmax(-1).view(1, 1)
+            pos += 1
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        barrier(dist)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(steps):
+            step()
+        t1.record()
+        torch.cuda.synchronize(dev)
+        barrier(dist)
+    cache.check_device_errors()
+    ms = reduce_max(dist, t0.elapsed_time(t1), dev)
+    res = {
+        "value": round(world * steps / (ms * 1e-3), 2),
+        "unit": "tok/s",
+        "workload": f"greedy decode, TinyLlama shape ({sh.n_layers} layers, d_model {sh.d_model}, "
+                    f"{sh.n_heads}/{sh.n_kv_heads} heads, head_dim {hd}, fp32), gqa_paged attention over a "
+                    f"paged cache (block 16), batch 1 per GPU, {E2E_PROMPT}-token prompt",
+        "ms_per_token": round(ms / steps, 4),
+        "tokens_timed": steps,
+        "gpu_launches_per_token": 2 * sh.n_layers,
+    }
+    del model, cache, kv
+    torch.cuda.empty_cache()
+    if cpu_baseline:
+        res["cpu_baseline"] = _e2e_cpu_baseline(lh, sh)
+    return res
+
+
+def _e2e_cpu_baseline(lh, sh) -> dict:
+    """The same model with the reference attention (dict growth + dense GQA) on the host
+    cores: prefill of the prompt, then timed greedy decode steps."""
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = lh.LlamaHarness(sh)
+    with torch.no_grad():
+        for _, prm in model.named_parameters():
+            if prm.dim() >= 2:
+                prm.normal_(0.0, 0.02)
+            else:
+                prm.fill_(1.0)
+    model.eval()
+    kv = {i: {"k": None, "v": None} for i in range(sh.n_layers)}
+    prompt = lh.prompt_ids(sh.vocab_size, E2E_PROMPT, 7)
+    n = 3
+    with torch.no_grad():
+        tok = model(prompt[None], kv_cache=kv)[0, -1].argmax(-1).view(1, 1)
+        pos = E2E_PROMPT
+        t = time.perf_counter()
+        for _ in range(n):
+            tok = model(tok, kv_cache=kv, position_ids=torch.tensor([pos]))[0, -1].argmax(-1).view(1, 1)
+            pos += 1
+        dt = time.perf_counter() - t
+    return {"value": round(n / dt, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} greedy decode steps after a {E2E_PROMPT}-token prefill, batch 1, torch on "
+                      f"{threads} host threads"}
 
 
 # ----------------------------------------------------------------------------- tiered (config 4)
@@ -815,7 +935,7 @@ def main():
     ap.add_argument("--batch", type=int, default=DECODE_BATCH, help="decode sequences per GPU")
     ap.add_argument("--ag-batch", type=int, default=AG_BATCH, help="append/gather sequences per GPU")
     ap.add_argument("--layers", type=int, default=L)
-    ap.add_argument("--only", choices=["all", "decode", "append_gather", "tiered", "mla"], default="all")
+    ap.add_argument("--only", choices=["all", "decode", "append_gather", "tiered", "mla", "e2e_llama"], default="all")
     ap.add_argument("--tiered-batch", type=int, default=TIER_B)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup

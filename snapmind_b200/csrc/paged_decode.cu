@@ -22,9 +22,34 @@
 namespace snapmind {
 
 // ---------------------------------------------------------------------------
-// generic CUDA-core kernel: any head_dim <= 256, any group size <= 16
+// generic CUDA-core kernel: any head_dim <= 256, group sizes up to 32 (16 for
+// head_dim > 64, 8 for head_dim > 128); fp32, bf16 and f16 pools.
+//
+// Each warp takes 32-token tiles of its split (flash-decoding on CUDA cores):
+//   * scores: lane = token; the lane reads its key row (16-byte loads when
+//     aligned) against q in shared memory (broadcast reads), all query heads
+//     of the group at once;
+//   * online softmax: one warp max and one warp sum per head per tile;
+//   * P V: lane = dims; P is broadcast from shared memory and each valid
+//     token's value row is read coalesced.
+// Warps merge in shared memory; splits merge through the last-ticket combine.
 // ---------------------------------------------------------------------------
-constexpr int kGenericWarps = 4;
+constexpr int kGenericWarps = 8;
+constexpr int kTileTok = 32;
+
+__device__ __forceinline__ float4 load4_as_f(const float* p) { return *reinterpret_cast<const float4*>(p); }
+template <typename T>
+__device__ __forceinline__ float4 load4_as_f(const T* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const T* t = reinterpret_cast<const T*>(&u);
+  return make_float4(Conv<T>::to_f(t[0]), Conv<T>::to_f(t[1]), Conv<T>::to_f(t[2]), Conv<T>::to_f(t[3]));
+}
+
+template <int GMAX, int NI>
+constexpr int generic_smem_floats(int head_dim) {
+  return GMAX * 32 * NI + kGenericWarps * kTileTok * GMAX + 2 * kGenericWarps * GMAX +
+         kGenericWarps * GMAX * head_dim;
+}
 
 template <typename T, int NI, int GMAX>
 __global__ void __launch_bounds__(kGenericWarps * 32)
@@ -33,6 +58,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = p.group;
   const int D = p.head_dim;
+  constexpr int DP = 32 * NI;  // padded head_dim of the q copy
 
   int len = p.seq_lens[b];
   if (len < 0) len = 0;
@@ -58,18 +84,19 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
   const int t0 = s * p.split_tokens;
   const int t1 = min(len, t0 + p.split_tokens);
 
+  // smem: [q: GMAX x DP][P: warps x 32 tokens x GMAX][merge: m, l, acc]
+  extern __shared__ __align__(16) float sm[];
+  float* q_s = sm;
+  float* p_s = q_s + GMAX * DP;
+  float* mrg = p_s + kGenericWarps * kTileTok * GMAX;
+
   const T* qb = reinterpret_cast<const T*>(p.q) + (int64_t)b * p.q_stride_seq;
-  float qr[GMAX][NI];
-#pragma unroll
-  for (int g = 0; g < GMAX; ++g) {
-#pragma unroll
-    for (int i = 0; i < NI; ++i) {
-      const int d = lane + 32 * i;
-      qr[g][i] = (g < G && d < D)
-                     ? Conv<T>::to_f(qb[(int64_t)(kvh * G + g) * p.q_stride_head + d])
-                     : 0.f;
-    }
+  for (int e = threadIdx.x; e < GMAX * DP; e += blockDim.x) {
+    const int g = e / DP, d = e - g * DP;
+    q_s[e] = (g < G && d < D) ? Conv<T>::to_f(qb[(int64_t)(kvh * G + g) * p.q_stride_head + d]) : 0.f;
   }
+  __syncthreads();
+
   float m[GMAX], l[GMAX], acc[GMAX][NI];
 #pragma unroll
   for (int g = 0; g < GMAX; ++g) {
@@ -82,47 +109,101 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
   const T* kpool = reinterpret_cast<const T*>(p.k_pool);
   const T* vpool = reinterpret_cast<const T*>(p.v_pool);
   const int32_t* table = p.tables + (int64_t)b * p.table_stride;
-  for (int t = t0 + warp; t < t1; t += kGenericWarps) {
-    const int j = t / p.block_size;
-    const int off = t - j * p.block_size;
-    int32_t phys = -1;
-    if (j < p.table_width) phys = table[j];
-    if (phys < 0 || phys >= p.num_blocks) {
-      if (lane == 0) flag_error(p.err, j < p.table_width ? SNAPMIND_DEVERR_BLOCK_ID : SNAPMIND_DEVERR_TABLE);
-      continue;
+  const bool vec = (D % 4 == 0) && (reinterpret_cast<uintptr_t>(kpool) % (4 * sizeof(T)) == 0);
+  float* pw = p_s + warp * kTileTok * GMAX;  // this warp's P tile [token][GMAX]
+
+  for (int tile = t0 + warp * kTileTok; tile < t1; tile += kGenericWarps * kTileTok) {
+    // ---- scores: lane = token
+    const int t = tile + lane;
+    bool valid = t < t1;
+    int64_t row = 0;
+    if (valid) {
+      const int j = t / p.block_size;
+      const int off = t - j * p.block_size;
+      const int32_t phys = j < p.table_width ? table[j] : -1;
+      if (phys < 0 || phys >= p.num_blocks) {
+        flag_error(p.err, j < p.table_width ? SNAPMIND_DEVERR_BLOCK_ID : SNAPMIND_DEVERR_TABLE);
+        valid = false;
+      } else {
+        row = (((int64_t)phys * p.n_kv_heads + kvh) * p.block_size + off) * D;
+      }
     }
-    const int64_t row = (((int64_t)phys * p.n_kv_heads + kvh) * p.block_size + off) * D;
-    float kf[NI], vf[NI];
+    float sc[GMAX];
 #pragma unroll
-    for (int i = 0; i < NI; ++i) {
-      const int d = lane + 32 * i;
-      kf[i] = d < D ? Conv<T>::to_f(kpool[row + d]) : 0.f;
-      vf[i] = d < D ? Conv<T>::to_f(vpool[row + d]) : 0.f;
+    for (int g = 0; g < GMAX; ++g) sc[g] = 0.f;
+    if (valid) {
+      const T* kr = kpool + row;
+      if (vec) {
+        for (int d = 0; d < D; d += 4) {
+          const float4 kv = load4_as_f(kr + d);
+#pragma unroll
+          for (int g = 0; g < GMAX; ++g) {
+            const float4 qv = *reinterpret_cast<const float4*>(q_s + g * DP + d);
+            sc[g] = fmaf(qv.x, kv.x, sc[g]);
+            sc[g] = fmaf(qv.y, kv.y, sc[g]);
+            sc[g] = fmaf(qv.z, kv.z, sc[g]);
+            sc[g] = fmaf(qv.w, kv.w, sc[g]);
+          }
+        }
+      } else {
+        for (int d = 0; d < D; ++d) {
+          const float kv = Conv<T>::to_f(kr[d]);
+#pragma unroll
+          for (int g = 0; g < GMAX; ++g) sc[g] = fmaf(q_s[g * DP + d], kv, sc[g]);
+        }
+      }
     }
+    // ---- online softmax over the tile, per head
 #pragma unroll
     for (int g = 0; g < GMAX; ++g) {
-      if (g >= G) break;
-      float dot = 0.f;
+      const float x = valid ? sc[g] * p.scale : -INFINITY;
+      float tm = x;
 #pragma unroll
-      for (int i = 0; i < NI; ++i) dot = fmaf(qr[g][i], kf[i], dot);
+      for (int o = 16; o > 0; o >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, o));
+      const float m_new = fmaxf(m[g], tm);
+      float corr = 1.f, pe = 0.f;
+      if (m_new != -INFINITY) {
+        corr = (m[g] == -INFINITY) ? 0.f : expf(m[g] - m_new);
+        pe = valid ? expf(x - m_new) : 0.f;
+      }
+      float ps = pe;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      const float sc = dot * p.scale;
-      const float m_new = fmaxf(m[g], sc);
-      const float corr = expf(m[g] - m_new);
-      const float pe = expf(sc - m_new);
-      l[g] = l[g] * corr + pe;
+      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      l[g] = l[g] * corr + ps;
 #pragma unroll
-      for (int i = 0; i < NI; ++i) acc[g][i] = fmaf(pe, vf[i], acc[g][i] * corr);
+      for (int i = 0; i < NI; ++i) acc[g][i] *= corr;
       m[g] = m_new;
+      pw[lane * GMAX + g] = pe;
     }
+    __syncwarp();
+    // ---- P V: lane = dims
+    const unsigned vmask = __ballot_sync(0xffffffffu, valid);
+#pragma unroll 4
+    for (int jt = 0; jt < kTileTok; ++jt) {
+      const int64_t rj = __shfl_sync(0xffffffffu, row, jt);
+      if (!((vmask >> jt) & 1u)) continue;
+      const T* vr = vpool + rj;
+      float vf[NI];
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const int d = lane + 32 * i;
+        vf[i] = d < D ? Conv<T>::to_f(vr[d]) : 0.f;
+      }
+      const float* pj = pw + jt * GMAX;
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g) {
+        const float pg = pj[g];
+#pragma unroll
+        for (int i = 0; i < NI; ++i) acc[g][i] = fmaf(pg, vf[i], acc[g][i]);
+      }
+    }
+    __syncwarp();  // the P tile is rewritten next iteration
   }
 
   // ---- merge the warps of this CTA ------------------------------------------
-  extern __shared__ float sm[];
-  float* sm_m = sm;                                   // [warps][GMAX]
-  float* sm_l = sm + kGenericWarps * GMAX;            // [warps][GMAX]
-  float* sm_acc = sm + 2 * kGenericWarps * GMAX;      // [warps][GMAX][D]
+  float* sm_m = mrg;                                  // [warps][GMAX]
+  float* sm_l = mrg + kGenericWarps * GMAX;           // [warps][GMAX]
+  float* sm_acc = mrg + 2 * kGenericWarps * GMAX;     // [warps][GMAX][D]
   __shared__ int s_last;
   if (lane == 0) {
 #pragma unroll
@@ -187,9 +268,9 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
 
 template <typename T, int NI>
 static int launch_generic_g(const DecodeParams& p, dim3 grid, cudaStream_t st) {
-  const size_t smem_base = sizeof(float) * 2 * kGenericWarps;
   auto go = [&](auto kernel, int gmax) -> int {
-    size_t smem = smem_base * gmax + sizeof(float) * kGenericWarps * gmax * p.head_dim;
+    size_t smem = sizeof(float) * ((size_t)gmax * 32 * NI + (size_t)kGenericWarps * kTileTok * gmax +
+                                   2 * (size_t)kGenericWarps * gmax + (size_t)kGenericWarps * gmax * p.head_dim);
     const size_t comb = combine_smem_bytes(p);
     if (comb > smem) smem = comb;
     if (smem > 48 * 1024) {
