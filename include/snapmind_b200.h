@@ -55,6 +55,7 @@ extern "C" {
 #define SNAPMIND_DEVERR_SPLIT 4         /* sequence longer than the split plan covers */
 #define SNAPMIND_DEVERR_OUT_OF_BLOCKS 8 /* reserve found too few free blocks */
 #define SNAPMIND_DEVERR_TIMEOUT 16      /* a bounded device wait gave up */
+#define SNAPMIND_DEVERR_POSITION 32     /* rotary position outside the cos/sin tables */
 
 /* decode flags */
 #define SNAPMIND_DECODE_FORCE_GENERIC 1 /* use the CUDA-core kernel even where the tensor-core one applies */
@@ -209,6 +210,25 @@ SNAPMIND_API int snapmind_tiered_move(void *k_pool, void *v_pool, int64_t layer_
  */
 SNAPMIND_API int snapmind_copy_2d(void *dst, int64_t dst_pitch, const void *src, int64_t src_pitch, int64_t width,
                      int64_t height, void *stream);
+
+/*
+ * Rotary position encoding of q and k in place, one launch for both — the
+ * rotate-half RoPE of RotaryPositionalEncoding.apply_to_qk
+ * (snapmind/layers/positional/rope.py:47-61), bit-identical to it on the same
+ * device: cos/sin rows cast to the tensor's dtype, x*cos and
+ * rotate_half(x)*sin and their sum each rounded to the dtype.  q is
+ * [batch][n_q_heads][n_tok][head_dim] and k [batch][n_kv_heads][n_tok][head_dim]
+ * with the given element strides (head_dim contiguous), both of `dtype`;
+ * cos_table / sin_table are fp32 [n_pos][head_dim].  Token t uses row
+ * positions[t] (int64, device), or row t when positions is NULL.  A position
+ * outside [0, n_pos) leaves its row unchanged and sets
+ * SNAPMIND_DEVERR_POSITION.
+ */
+SNAPMIND_API int snapmind_rope_qk(void *q, int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_t,
+                                  int32_t n_q_heads, void *k, int64_t k_stride_b, int64_t k_stride_h,
+                                  int64_t k_stride_t, int32_t n_kv_heads, int dtype, int32_t batch, int32_t n_tok,
+                                  int32_t head_dim, const float *cos_table, const float *sin_table, int64_t n_pos,
+                                  const int64_t *positions, int32_t *err_word, void *stream);
 
 /*
  * Frozen chunk keys of the lookahead indexer: for chunks

@@ -28,6 +28,7 @@ DEVERR_TABLE = 2
 DEVERR_SPLIT = 4
 DEVERR_OUT_OF_BLOCKS = 8
 DEVERR_TIMEOUT = 16
+DEVERR_POSITION = 32
 
 DECODE_FORCE_GENERIC = 1
 
@@ -81,6 +82,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _p, _p, _i64, _p, _p],
     ),
     "snapmind_indexer_pool_workspace_bytes": (_i64, [_i32, _i32, _i32]),
+    "snapmind_rope_qk": (
+        _int,
+        [_p, _i64, _i64, _i64, _i32, _p, _i64, _i64, _i64, _i32, _int, _i32, _i32, _i32, _p, _p, _i64, _p, _p, _p],
+    ),
     "snapmind_indexer_score_ref": (_int, [_p, _p, _i32, _i32, _p, _i32, _i32, _p, _p]),
     "snapmind_indexer_topk": (
         _int,
@@ -192,4 +197,6 @@ def raise_device_error(word: int, what: str) -> None:
         parts.append("sequence longer than the split plan")
     if word & DEVERR_TIMEOUT:
         parts.append("bounded device wait timed out")
+    if word & DEVERR_POSITION:
+        parts.append("rotary position outside the cos/sin tables")
     raise RuntimeError(f"{what}: device error 0x{word:x} ({', '.join(parts)})")

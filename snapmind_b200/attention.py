@@ -18,7 +18,12 @@ re-copying the whole history every step.  This layer, given the layer view of a
   (``PagedKVCache.attend``): one query is a decode step; ``T`` queries are a
   causal prefill, one kernel row per query sharing the table row.
 
-The projections, RoPE (``pe.apply_to_qk``) and the output projection stay
+RoPE runs as one kernel over q and k in place (``snapmind_rope_qk``,
+bit-identical to ``apply_to_qk`` on the same device) when ``pe`` exposes the
+reference's rotate-half tables — ``cos_cached`` / ``sin_cached`` of shape
+``[n_pos, head_dim]`` and ``_rotate_half``, as
+snapmind/layers/positional/rope.py:11-61 does; any other ``pe`` is applied
+with its own ``apply_to_qk``.  The projections and the output projection stay
 torch, as in the reference.  Without a cache (``kv_cache=None``) the layer
 attends causally over its own ``T`` tokens through a transient one-layer pool.
 
@@ -33,8 +38,11 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
+from snapmind_b200 import _lib
 from snapmind_b200.kv_cache.paged import PagedKVCache, PagedLayerView
 from snapmind_b200.registry import ATTENTION
+
+_ROPE_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
 
 
 def _is_causal_mask(mask: torch.Tensor, n_q: int, n_k: int) -> bool:
@@ -79,6 +87,39 @@ class PagedGroupedQueryAttention(nn.Module):
         batch, seq_len, _ = x.shape
         return x.view(batch, seq_len, n_heads, self.head_dim).transpose(1, 2)
 
+    def _rope_tables(self, q: torch.Tensor):
+        """(cos, sin) for the fused kernel, or None to use ``pe.apply_to_qk``."""
+        pe = self.pe
+        cos, sin = getattr(pe, "cos_cached", None), getattr(pe, "sin_cached", None)
+        if not (isinstance(cos, torch.Tensor) and isinstance(sin, torch.Tensor) and hasattr(pe, "_rotate_half")):
+            return None
+        if cos.dim() != 2 or cos.shape != sin.shape or cos.shape[1] != self.head_dim or self.head_dim % 2:
+            return None
+        if q.dtype not in _ROPE_DTYPES or cos.device != q.device or torch.is_grad_enabled():
+            return None
+        if cos.dtype != torch.float32 or not cos.is_contiguous():
+            cos = cos.float().contiguous()
+        if sin.dtype != torch.float32 or not sin.is_contiguous():
+            sin = sin.float().contiguous()
+        return cos, sin
+
+    def _rope(self, q, k, position_ids, tables, err: torch.Tensor) -> None:
+        cos, sin = tables
+        n_tok = q.shape[2]
+        pos = None
+        if position_ids is not None:
+            pos = position_ids.reshape(-1)
+            if pos.numel() != n_tok:
+                raise ValueError(f"gqa_paged: {pos.numel()} positions for {n_tok} tokens")
+            pos = pos.to(device=q.device, dtype=torch.int64).contiguous()
+        status = _lib.load().snapmind_rope_qk(
+            q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), q.shape[1],
+            k.data_ptr(), k.stride(0), k.stride(1), k.stride(2), k.shape[1],
+            _lib.dtype_code(q.dtype), q.shape[0], n_tok, self.head_dim, cos.data_ptr(), sin.data_ptr(),
+            cos.shape[0], None if pos is None else pos.data_ptr(), err.data_ptr(), _lib.stream_handle(q.device),
+        )  # fmt: skip
+        _lib.check(status, "gqa_paged rope")
+
     def forward(
         self,
         x: torch.Tensor,
@@ -91,8 +132,6 @@ class PagedGroupedQueryAttention(nn.Module):
         q = self._split_heads(self.q_proj(x), self.n_heads)
         k = self._split_heads(self.k_proj(x), self.n_kv_heads)
         v = self._split_heads(self.v_proj(x), self.n_kv_heads)
-        if self.pe is not None:
-            q, k = self.pe.apply_to_qk(q, k, position_ids)
 
         n_new = x.shape[1]
         if kv_cache is None:
@@ -110,6 +149,12 @@ class PagedGroupedQueryAttention(nn.Module):
                 f"gqa_paged: cache holds {cache.n_heads} heads x {cache.head_dim}, "
                 f"layer needs {self.n_kv_heads} x {self.head_dim}"
             )
+        if self.pe is not None:
+            tables = self._rope_tables(q)
+            if tables is not None:
+                self._rope(q, k, position_ids, tables, cache._err)  # in place on the fresh projections
+            else:
+                q, k = self.pe.apply_to_qk(q, k, position_ids)
         cached = cache.num_tokens(layer)
         causal = True
         if mask is not None:

@@ -157,7 +157,9 @@ class ChunkSelector:
         need = lib.snapmind_indexer_pool_workspace_bytes(batch, chunk_count, pool.kv_lora_rank)
         if chunk_count * batch >= 1024:  # a bulk (re)build: room for the fp32 means
             if self._pool_ws is None or self._pool_ws.numel() < need:
-                self._pool_ws = torch.empty(need, dtype=torch.uint8, device=pool.device)
+                # room for a few more chunks per sequence, so growing sequences do not reallocate
+                grow = lib.snapmind_indexer_pool_workspace_bytes(batch, chunk_count + 64, pool.kv_lora_rank)
+                self._pool_ws = torch.empty(grow, dtype=torch.uint8, device=pool.device)
             ws, ws_bytes = self._pool_ws.data_ptr(), self._pool_ws.numel()
         else:
             ws, ws_bytes = None, 0
