@@ -426,6 +426,7 @@ def run_e2e_llama(args, dev, seed, dist, world, cpu_baseline: bool) -> dict:
     prompt = lh.prompt_ids(sh.vocab_size, E2E_PROMPT, seed + 61).to(dev)
     steps = max(1, min(args.steps, E2E_GEN_MAX))
     warmup = args.warmup
+    # eager: one model forward per token, as the reference engine runs it
     with torch.no_grad():
         logits = model(prompt[None], kv_cache=kv)[0, -1]
         tok = logits.argmax(-1).view(1, 1)
@@ -449,16 +450,37 @@ def run_e2e_llama(args, dev, seed, dist, world, cpu_baseline: bool) -> dict:
         torch.cuda.synchronize(dev)
         barrier(dist)
     cache.check_device_errors()
-    ms = reduce_max(dist, t0.elapsed_time(t1), dev)
+    eager_ms = reduce_max(dist, t0.elapsed_time(t1), dev)
+    # the same decode with the step captured in a CUDA graph (GraphDecoder)
+    from snapmind_b200.engine import GraphDecoder
+
+    cache.reset()
+    eng = GraphDecoder(model, cache)
+    eng.prefill(prompt)
+    eng.begin(warmup + steps)
+    eng.step(warmup)  # warm-up + capture, then replays
+    torch.cuda.synchronize(dev)
+    barrier(dist)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    eng.step(steps)
+    g1.record()
+    torch.cuda.synchronize(dev)
+    barrier(dist)
+    eng.finish()
+    ms = reduce_max(dist, g0.elapsed_time(g1), dev)
     res = {
         "value": round(world * steps / (ms * 1e-3), 2),
         "unit": "tok/s",
         "workload": f"greedy decode, TinyLlama shape ({sh.n_layers} layers, d_model {sh.d_model}, "
                     f"{sh.n_heads}/{sh.n_kv_heads} heads, head_dim {hd}, fp32), gqa_paged attention over a "
-                    f"paged cache (block 16), batch 1 per GPU, {E2E_PROMPT}-token prompt",
+                    f"paged cache (block 16), batch 1 per GPU, {E2E_PROMPT}-token prompt; decode step "
+                    f"captured in a CUDA graph (GraphDecoder)",
         "ms_per_token": round(ms / steps, 4),
+        "eager_tok_s": round(world * steps / (eager_ms * 1e-3), 2),
+        "eager_ms_per_token": round(eager_ms / steps, 4),
         "tokens_timed": steps,
-        "gpu_launches_per_token": 2 * sh.n_layers,
+        "gpu_launches_per_token": 3 * sh.n_layers,
     }
     del model, cache, kv
     torch.cuda.empty_cache()

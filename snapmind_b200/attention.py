@@ -155,6 +155,14 @@ class PagedGroupedQueryAttention(nn.Module):
                 self._rope(q, k, position_ids, tables, cache._err)  # in place on the fresh projections
             else:
                 q, k = self.pe.apply_to_qk(q, k, position_ids)
+        if cache.device_steps_active:  # one token at the device counters (a captured decode step)
+            if n_new != 1 or mask is not None:
+                raise ValueError("gqa_paged: device steps take one token and no mask")
+            cache.store_device(layer, k, v)
+            qd = q if q.dtype == cache.dtype else q.to(cache.dtype)
+            out = cache.attend_device(layer, qd, scale=self.head_dim ** -0.5)
+            out = out.to(x.dtype).transpose(1, 2).reshape(1, 1, self.n_heads * self.head_dim)
+            return self.out_proj(out), None
         cached = cache.num_tokens(layer)
         causal = True
         if mask is not None:

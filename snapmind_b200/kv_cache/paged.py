@@ -80,6 +80,11 @@ class PagedKVCache(KVCacheABC):
         self._version = 0  # bumped by every change of the cached contents
         self._ladder: torch.Tensor | None = None  # int32 [1, 2, ..., max_blocks * block_size]
         self._workspace: torch.Tensor | None = None
+        # device-counter steps (begin_device_steps): slot of the next token, and length after it
+        self._dev_len: torch.Tensor | None = None
+        self._dev_len_p1: torch.Tensor | None = None
+        self._dev_steps = 0
+        self._dev_capacity = 0
 
     # ------------------------------------------------------------------ helpers
     def _stream(self) -> int:
@@ -347,6 +352,112 @@ class PagedKVCache(KVCacheABC):
         )  # fmt: skip
         _lib.check(status, "PagedKVCache.attend")
         return out
+
+    # ------------------------------------------- device-counter steps (CUDA graphs)
+    @property
+    def device_steps_active(self) -> bool:
+        return self._dev_len is not None
+
+    def begin_device_steps(self, n_steps: int) -> None:
+        """Prepare ``n_steps`` one-token steps whose slot and length live in device
+        counters, so that a whole decode step can be captured in a CUDA graph and
+        replayed without host work.
+
+        Every layer must hold the same number of tokens.  The blocks those steps
+        need are taken now, in the order the reference's per-token stores would
+        take them (step by step, layer by layer: snapmind/kv_cache/paged.py:43-47),
+        so the block tables end up as an eager run's; the steps must then all be
+        run before ``end_device_steps``.
+        """
+        if self._dev_len is not None:
+            raise RuntimeError("PagedKVCache: device steps already active")
+        counts = set(self._slot_counts)
+        if len(counts) != 1:
+            raise ValueError("PagedKVCache.begin_device_steps: every layer must hold the same number of tokens")
+        n0 = counts.pop()
+        if n_steps <= 0:
+            raise ValueError("PagedKVCache.begin_device_steps: n_steps must be positive")
+        old = [len(bt) for bt in self._block_tables]
+        for step in range(n_steps):
+            blk = (n0 + step) // self.block_size
+            for layer_idx in range(self.n_layers):
+                bt = self._block_tables[layer_idx]
+                while len(bt) <= blk:
+                    if not self._free_blocks:
+                        for li in range(self.n_layers):
+                            self._sync_table(li, old[li])
+                        raise RuntimeError(_lib.OUT_OF_BLOCKS_MSG)
+                    bt.append(self._free_blocks.pop())
+        for layer_idx in range(self.n_layers):
+            self._sync_table(layer_idx, old[layer_idx])
+        self._dev_len = torch.full((1,), n0, dtype=torch.int32, device=self.device)
+        self._dev_len_p1 = torch.full((1,), n0 + 1, dtype=torch.int32, device=self.device)
+        self._dev_steps = n_steps
+        self._dev_capacity = n0 + n_steps
+
+    def store_device(self, layer_idx: int, key: torch.Tensor, value: torch.Tensor) -> None:
+        """Append one token (``key``/``value`` ``(1, H, 1, D)``) at the slot held by the
+        device counter.  No host work, no sync: capturable in a CUDA graph."""
+        k = self._as_input(key[0])
+        v = self._as_input(value[0])
+        if v.stride() != k.stride() or v.dtype != k.dtype:
+            k, v = k.contiguous(), v.to(k.dtype).contiguous()
+        status = _lib.load().snapmind_kv_append(
+            self._k_buffer.data_ptr(), self._v_buffer.data_ptr(), _lib.dtype_code(self.dtype), 0,
+            k.data_ptr(), v.data_ptr(), _lib.dtype_code(k.dtype),
+            0, 0, k.stride(0), k.stride(1),
+            self._tables_dev[layer_idx].data_ptr(), 0, 0, self.max_blocks,
+            self._dev_len.data_ptr(), 0,
+            1, 1, 1, self.n_heads, self.head_dim, self.block_size, self.max_blocks,
+            self._err.data_ptr(), self._stream(),
+        )  # fmt: skip
+        _lib.check(status, "PagedKVCache.store_device")
+
+    def attend_device(self, layer_idx: int, q: torch.Tensor, scale: float | None = None) -> torch.Tensor:
+        """Decode attention of one query ``(1, Hq, 1, D)`` over the tokens up to and
+        including the device counter's slot; the split plan is fixed by the
+        capacity reserved in ``begin_device_steps``."""
+        if q.dtype != self.dtype:
+            raise TypeError(f"attend_device: q dtype {q.dtype} != cache dtype {self.dtype}")
+        if q.stride(-1) != 1:
+            q = q.contiguous()
+        n_q = q.shape[1]
+        out = torch.empty((1, n_q, 1, self.head_dim), dtype=self.dtype, device=self.device)
+        scale = self.head_dim ** -0.5 if scale is None else scale
+        lib = _lib.load()
+        cap = self._dev_capacity
+        split = lib.snapmind_paged_gqa_decode_split_tokens(1, self.n_heads, cap, self.block_size)
+        need = lib.snapmind_paged_gqa_decode_workspace_bytes(1, n_q, self.n_heads, self.head_dim, cap, split)
+        if self._workspace is None or self._workspace.numel() < need:
+            self._workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+        status = lib.snapmind_paged_gqa_decode(
+            q.data_ptr(), q.stride(2), q.stride(1),
+            self._k_buffer.data_ptr(), self._v_buffer.data_ptr(), _lib.dtype_code(self.dtype),
+            self._tables_dev[layer_idx].data_ptr(), 0, self.max_blocks, self._dev_len_p1.data_ptr(),
+            out.data_ptr(), out.stride(2), out.stride(1),
+            float(scale), 1, n_q, self.n_heads, self.head_dim, self.block_size, self.max_blocks,
+            cap, split, 0, self._workspace.data_ptr(), self._workspace.numel(), self._err.data_ptr(),
+            self._stream(),
+        )  # fmt: skip
+        _lib.check(status, "PagedKVCache.attend_device")
+        return out
+
+    def advance_device_step(self) -> None:
+        """Move the device counters to the next token (two device adds)."""
+        self._dev_len.add_(1)
+        self._dev_len_p1.add_(1)
+
+    def end_device_steps(self, n_done: int) -> None:
+        """Account the ``n_done`` device steps on the host; must equal the steps begun."""
+        if self._dev_len is None:
+            raise RuntimeError("PagedKVCache: no device steps active")
+        if n_done != self._dev_steps:
+            raise ValueError(f"PagedKVCache.end_device_steps: {n_done} steps run, {self._dev_steps} begun")
+        for layer_idx in range(self.n_layers):
+            self._slot_counts[layer_idx] += n_done
+        self._dev_len = self._dev_len_p1 = None
+        self._dev_steps = self._dev_capacity = 0
+        self._version += 1
 
     # ------------------------------------------------------- introspection
     def block_tables(self) -> list[list[int]]:

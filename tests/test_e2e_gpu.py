@@ -204,3 +204,35 @@ def test_e2e_tinyllama_matches_reference(cuda_device):
         np.testing.assert_allclose(vf[idx], z["tinyllama_v_sample"][layer], rtol=1e-3, atol=1e-4)
         np.testing.assert_allclose(kf.astype(np.float64).sum(), rec["k_sums"][layer], rtol=1e-3, atol=1e-2)
         np.testing.assert_allclose(vf.astype(np.float64).sum(), rec["v_sums"][layer], rtol=1e-3, atol=1e-2)
+
+
+@torch.no_grad()
+@pytest.mark.parametrize("use_graph", [True, False])
+def test_graph_decoder_matches_reference_and_eager(cuda_device, use_graph):
+    """Greedy generation with the decode step captured in a CUDA graph: the
+    reference's ids for the TinyLlama case, the same final cache and block
+    tables as the eager run (the small case compares them exactly)."""
+    from snapmind_b200 import PagedGroupedQueryAttention, PagedKVCache
+    from snapmind_b200.engine import GraphDecoder
+
+    meta, z = _golden()
+    for name, shape, n_blocks in (("small", SMALL, None), ("tinyllama", TINYLLAMA, TINYLLAMA.n_layers * 128)):
+        rec = meta[name]
+        model = LlamaHarness(shape, PagedGroupedQueryAttention)
+        init_weights(model, rec["weight_seed"])
+        model.to(cuda_device)
+        hd = shape.d_model // shape.n_heads
+        prompt = prompt_ids(shape.vocab_size, rec["prompt_len"], rec["prompt_seed"])
+        cache = PagedKVCache(shape.max_seq_len, shape.n_layers, shape.n_kv_heads, hd, max_blocks=n_blocks)
+        ids = GraphDecoder(model, cache, use_graph=use_graph).generate(prompt, rec["n_generated"])
+        assert ids == rec["ids"], name
+        eager = PagedKVCache(shape.max_seq_len, shape.n_layers, shape.n_kv_heads, hd, max_blocks=n_blocks)
+        ids_e, _ = generate(model, prompt, rec["n_generated"], eager.layer_dicts())
+        assert ids_e == ids
+        assert cache.block_tables() == eager.block_tables()
+        assert cache.memory_usage() == eager.memory_usage()
+        for layer in range(shape.n_layers):
+            k, v = cache.fetch(layer)
+            ke, ve = eager.fetch(layer)
+            torch.testing.assert_close(k, ke, rtol=1e-5, atol=1e-6)
+            torch.testing.assert_close(v, ve, rtol=1e-5, atol=1e-6)
