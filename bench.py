@@ -185,7 +185,7 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
     steps, warmup = args.steps, args.warmup
     seed = 1234 + 7919 * rank
     if args.only == "e2e_llama":
-        r = run_e2e_llama(args, dev, seed, dist, world, cpu_baseline=not args.no_cpu_baseline and rank == 0)
+        r = run_e2e_llama(args, dev, seed, dist, world, cpu_baseline=not args.no_cpu_baseline and world == 1)
         return {"metric": METRIC, "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": steps,
                 "warmup": warmup, "ms_per_step": r["ms_per_token"], "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": r["workload"]},
@@ -378,7 +378,7 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
         "kv_append_gather": ag,
         "tiered": run_tiered(args, dev, seed, dist, world) if args.only == "all" else None,
         "mla_sparse": run_mla_sparse(args, dev, seed, dist, world) if args.only == "all" else None,
-        "e2e_llama": run_e2e_llama(args, dev, seed, dist, world, cpu_baseline=not args.no_cpu_baseline and rank == 0)
+        "e2e_llama": run_e2e_llama(args, dev, seed, dist, world, cpu_baseline=not args.no_cpu_baseline and world == 1)
         if args.only == "all" else None,
         "gpu_launches": launches_per_step * steps,
         "clocks": clocks.summary(),
