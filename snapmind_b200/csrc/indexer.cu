@@ -633,37 +633,17 @@ __global__ void __launch_bounds__(kTopkThreads) indexer_topk_kernel(
 }
 
 
-// Descending bitonic sort of n (a power of two) keys in shared memory; every
-// thread of the block calls it.
-__device__ __forceinline__ void bitonic_sort_desc(unsigned long long* sk, int n) {
-  for (int size = 2; size <= n; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const bool desc = (i & size) == 0;
-          const unsigned long long a = sk[i], c2 = sk[j];
-          if (desc ? (a < c2) : (a > c2)) {
-            sk[i] = c2;
-            sk[j] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-}
-
 constexpr int kSliceChunks = 128;  // chunks scored and pre-selected by one CTA
 constexpr int kSliceThreads = 256;
 
 // Two-phase top-k over many CTAs.  CTA (slice, b) scores chunks
-// [slice * 128, slice * 128 + 128) of sequence b, sorts their (ordered score,
-// inverted id) keys and keeps the best `keep` = min(k, 128) as candidates.
-// Every member of the sequence's top-k is among the candidates of its slice,
-// so the top-k of the union of candidates is the exact answer.  The CTA that
-// takes the sequence's last ticket merges (sorts the union) and resets the
-// ticket; no CTA waits for another.
+// [slice * 128, slice * 128 + 128) of sequence b and keeps the best
+// `keep` = min(k, 128) of their (ordered score, inverted id) keys as
+// candidates, in rank order.  Every member of the sequence's top-k is among the
+// candidates of its slice, so the top-k of the union of candidates is the exact
+// answer.  The CTA that takes the sequence's last ticket ranks the union and
+// resets the ticket; no CTA waits for another.  Both selections rank keys
+// instead of sorting them (no barrier stages).
 template <typename T>
 __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
     const T* q, const T* keys, const int32_t* n_chunks_arr, int n_chunks0, int max_chunks, int dim, float scale,
@@ -693,9 +673,18 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
     }
   }
   __syncthreads();
-  bitonic_sort_desc(sk, kSliceChunks);
+  // selection by rank (no sort): rank = keys ahead of this one, ties to the lower index;
+  // ranks are distinct, and the best `keep` land in rank order
   unsigned long long* mine = cand + ((int64_t)b * n_slices + slice) * keep;
-  for (int i = threadIdx.x; i < keep; i += blockDim.x) mine[i] = sk[i];
+  for (int i = threadIdx.x; i < kSliceChunks; i += blockDim.x) {
+    const unsigned long long key = sk[i];
+    int r = 0;
+    for (int j = 0; j < kSliceChunks; ++j) {
+      const unsigned long long kj = sk[j];
+      r += (kj > key) || (kj == key && j < i);
+    }
+    if (r < keep) mine[r] = key;
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(&tickets[b], 1) == n_slices - 1;
@@ -704,17 +693,48 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
   __threadfence();
   const unsigned long long* all = cand + (int64_t)b * n_slices * keep;
   const int n_cand = n_slices * keep;
-  for (int i = threadIdx.x; i < merge_n; i += blockDim.x) sk[i] = i < n_cand ? __ldcg(all + i) : 0ull;
+  for (int i = threadIdx.x; i < n_cand; i += blockDim.x) sk[i] = __ldcg(all + i);
   __syncthreads();
-  bitonic_sort_desc(sk, merge_n);
+  // the same rank selection over the union of candidates; output slots past the
+  // valid chunks are -1 (real keys rank before the zero fillers)
+  const int n_out = min(k, nc);
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    const bool ok = i < nc;
+    if (i >= n_out) {
+      out_idx[(int64_t)b * k + i] = -1;
+      if (out_score) out_score[(int64_t)b * k + i] = -INFINITY;
+    }
+  }
+  // each slice's candidates are in rank order (descending): a candidate's global
+  // rank is its place in its own list plus, per other list, the keys ahead of it
+  // (binary search; equal keys count as ahead when their list comes first)
+  for (int i = threadIdx.x; i < n_cand; i += blockDim.x) {
+    const int L = i / keep;
     const unsigned long long key = sk[i];
-    out_idx[(int64_t)b * k + i] = ok ? (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull)) : -1;
-    if (out_score) {
-      const uint32_t ob = (uint32_t)(key >> 32);
-      const uint32_t u = (ob & 0x80000000u) ? (ob & 0x7FFFFFFFu) : ~ob;
-      out_score[(int64_t)b * k + i] = ok ? __uint_as_float(u) : -INFINITY;
+    int r = i - L * keep;
+    for (int M = 0; M < n_slices; ++M) {
+      if (M == L) continue;
+      const unsigned long long* lst = sk + M * keep;
+      int lo = 0, hi = keep;
+      if (M < L) {
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (lst[mid] >= key) lo = mid + 1; else hi = mid;
+        }
+      } else {
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (lst[mid] > key) lo = mid + 1; else hi = mid;
+        }
+      }
+      r += lo;
+    }
+    if (r < n_out) {
+      out_idx[(int64_t)b * k + r] = (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+      if (out_score) {
+        const uint32_t ob = (uint32_t)(key >> 32);
+        const uint32_t u = (ob & 0x80000000u) ? (ob & 0x7FFFFFFFu) : ~ob;
+        out_score[(int64_t)b * k + r] = __uint_as_float(u);
+      }
     }
   }
   if (threadIdx.x == 0) tickets[b] = 0;
@@ -729,8 +749,7 @@ TopkPlan topk_plan(int batch, int max_chunks, int k) {
   TopkPlan t;
   t.n_slices = (max_chunks + kSliceChunks - 1) / kSliceChunks;
   t.keep = k < kSliceChunks ? k : kSliceChunks;
-  t.merge_n = 1;
-  while (t.merge_n < t.n_slices * t.keep) t.merge_n <<= 1;
+  t.merge_n = t.n_slices * t.keep;  // candidates held in shared memory by the merging CTA
   if (t.merge_n < kSliceChunks) t.merge_n = kSliceChunks;
   t.tickets_bytes = ((int64_t)batch * 4 + 255) / 256 * 256;
   t.total = t.tickets_bytes + (int64_t)batch * t.n_slices * t.keep * 8;

@@ -49,10 +49,15 @@ inline int default_split_tokens(int batch, int n_kv_heads, int max_seq_len, int 
                        (max_seq_len > 0 ? max_seq_len : 1) / 2;
   const int64_t target = (int64_t)num_sms() * 16;
   int64_t split = (work + target - 1) / target;
-  if (split < 512) split = 512;
-  if (split > 8192) split = 8192;
   int64_t unit = block_size;
   if (64 % block_size == 0) unit = 64;
+  // splits of at least 512 tokens keep the TMA pipeline full; a small problem (fewer
+  // than about two CTAs per SM at 512) takes shorter splits, down to one 64-token tile
+  const int64_t rows = (int64_t)(batch > 0 ? batch : 1) * (n_kv_heads > 0 ? n_kv_heads : 1);
+  const int64_t ctas_512 = rows * (((max_seq_len > 0 ? max_seq_len : 1) + 511) / 512);
+  const int64_t min_split = ctas_512 < 2 * (int64_t)num_sms() ? unit : 512;
+  if (split < min_split) split = min_split;
+  if (split > 8192) split = 8192;
   split = (split + unit - 1) / unit * unit;
   return (int)split;
 }
