@@ -387,7 +387,7 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
 
 
 # ----------------------------------------------------------------------------- TinyLlama end to end (config 1)
-E2E_PROMPT, E2E_GEN_MAX = 256, 256
+E2E_PROMPT, E2E_GEN_MAX, E2E_BATCH = 256, 256, 64
 
 
 def _llama_harness():
@@ -469,6 +469,29 @@ def run_e2e_llama(args, dev, seed, dist, world, cpu_baseline: bool) -> dict:
     barrier(dist)
     eng.finish()
     ms = reduce_max(dist, g0.elapsed_time(g1), dev)
+    # many sequences decoded together on a PagedKVPool (BatchedGraphDecoder)
+    from snapmind_b200 import PagedKVPool
+    from snapmind_b200.engine import BatchedGraphDecoder
+
+    nb_seq = (E2E_PROMPT + warmup + steps + 1 + 15) // 16
+    pool = PagedKVPool(sh.n_layers, sh.n_kv_heads, hd, num_blocks=E2E_BATCH * nb_seq, max_seqs=E2E_BATCH,
+                       max_blocks_per_seq=nb_seq, block_size=16, dtype=torch.float32, device=dev)
+    prompts = torch.stack([lh.prompt_ids(sh.vocab_size, E2E_PROMPT, seed + 70 + i) for i in range(E2E_BATCH)])
+    bdec = BatchedGraphDecoder(model, pool, E2E_BATCH)
+    bdec.prefill(prompts)
+    bdec.begin(warmup + steps)
+    bdec.step(warmup)
+    torch.cuda.synchronize(dev)
+    barrier(dist)
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record()
+    bdec.step(steps)
+    b1.record()
+    torch.cuda.synchronize(dev)
+    barrier(dist)
+    bdec.finish()
+    batched_ms = reduce_max(dist, b0.elapsed_time(b1), dev)
+    del pool, bdec
     res = {
         "value": round(world * steps / (ms * 1e-3), 2),
         "unit": "tok/s",
@@ -481,6 +504,14 @@ def run_e2e_llama(args, dev, seed, dist, world, cpu_baseline: bool) -> dict:
         "eager_ms_per_token": round(eager_ms / steps, 4),
         "tokens_timed": steps,
         "gpu_launches_per_token": 3 * sh.n_layers,
+        "batched": {
+            "value": round(world * E2E_BATCH * steps / (batched_ms * 1e-3), 1),
+            "unit": "tok/s",
+            "batch_per_gpu": E2E_BATCH,
+            "ms_per_step": round(batched_ms / steps, 4),
+            "workload": f"{E2E_BATCH} sequences per GPU decoded together on a PagedKVPool (BatchedGraphDecoder: "
+                        "device-side block reserve, batched append and paged decode, step in a CUDA graph)",
+        },
     }
     del model, cache, kv
     torch.cuda.empty_cache()

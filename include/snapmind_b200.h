@@ -219,16 +219,17 @@ SNAPMIND_API int snapmind_copy_2d(void *dst, int64_t dst_pitch, const void *src,
  * rotate_half(x)*sin and their sum each rounded to the dtype.  q is
  * [batch][n_q_heads][n_tok][head_dim] and k [batch][n_kv_heads][n_tok][head_dim]
  * with the given element strides (head_dim contiguous), both of `dtype`;
- * cos_table / sin_table are fp32 [n_pos][head_dim].  Token t uses row
- * positions[t] (int64, device), or row t when positions is NULL.  A position
- * outside [0, n_pos) leaves its row unchanged and sets
+ * cos_table / sin_table are fp32 [n_pos][head_dim].  Token t of sequence b
+ * uses row positions[b * pos_stride_b + t] (int64, device; pos_stride_b = 0
+ * shares one position list across the batch), or row t when positions is
+ * NULL.  A position outside [0, n_pos) leaves its row unchanged and sets
  * SNAPMIND_DEVERR_POSITION.
  */
 SNAPMIND_API int snapmind_rope_qk(void *q, int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_t,
                                   int32_t n_q_heads, void *k, int64_t k_stride_b, int64_t k_stride_h,
                                   int64_t k_stride_t, int32_t n_kv_heads, int dtype, int32_t batch, int32_t n_tok,
                                   int32_t head_dim, const float *cos_table, const float *sin_table, int64_t n_pos,
-                                  const int64_t *positions, int32_t *err_word, void *stream);
+                                  const int64_t *positions, int64_t pos_stride_b, int32_t *err_word, void *stream);
 
 /*
  * Frozen chunk keys of the lookahead indexer: for chunks

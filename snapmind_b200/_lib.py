@@ -84,7 +84,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "snapmind_indexer_pool_workspace_bytes": (_i64, [_i32, _i32, _i32]),
     "snapmind_rope_qk": (
         _int,
-        [_p, _i64, _i64, _i64, _i32, _p, _i64, _i64, _i64, _i32, _int, _i32, _i32, _i32, _p, _p, _i64, _p, _p, _p],
+        [_p, _i64, _i64, _i64, _i32, _p, _i64, _i64, _i64, _i32, _int, _i32, _i32, _i32, _p, _p, _i64, _p, _i64,
+         _p, _p],
     ),
     "snapmind_indexer_score_ref": (_int, [_p, _p, _i32, _i32, _p, _i32, _i32, _p, _p]),
     "snapmind_indexer_topk": (

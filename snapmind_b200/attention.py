@@ -40,6 +40,7 @@ import torch.nn as nn
 
 from snapmind_b200 import _lib
 from snapmind_b200.kv_cache.paged import PagedKVCache, PagedLayerView
+from snapmind_b200.paged_pool import PoolLayerView
 from snapmind_b200.registry import ATTENTION
 
 _ROPE_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
@@ -105,18 +106,21 @@ class PagedGroupedQueryAttention(nn.Module):
 
     def _rope(self, q, k, position_ids, tables, err: torch.Tensor) -> None:
         cos, sin = tables
-        n_tok = q.shape[2]
-        pos = None
+        batch, n_tok = q.shape[0], q.shape[2]
+        pos, pos_stride = None, 0
         if position_ids is not None:
             pos = position_ids.reshape(-1)
-            if pos.numel() != n_tok:
-                raise ValueError(f"gqa_paged: {pos.numel()} positions for {n_tok} tokens")
+            if pos.numel() == batch * n_tok and batch > 1:
+                pos_stride = n_tok  # one position list per sequence
+            elif pos.numel() != n_tok:
+                raise ValueError(f"gqa_paged: {pos.numel()} positions for {batch} x {n_tok} tokens")
             pos = pos.to(device=q.device, dtype=torch.int64).contiguous()
         status = _lib.load().snapmind_rope_qk(
             q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), q.shape[1],
             k.data_ptr(), k.stride(0), k.stride(1), k.stride(2), k.shape[1],
             _lib.dtype_code(q.dtype), q.shape[0], n_tok, self.head_dim, cos.data_ptr(), sin.data_ptr(),
-            cos.shape[0], None if pos is None else pos.data_ptr(), err.data_ptr(), _lib.stream_handle(q.device),
+            cos.shape[0], None if pos is None else pos.data_ptr(), pos_stride, err.data_ptr(),
+            _lib.stream_handle(q.device),
         )  # fmt: skip
         _lib.check(status, "gqa_paged rope")
 
@@ -127,8 +131,10 @@ class PagedGroupedQueryAttention(nn.Module):
         position_ids: torch.Tensor | None = None,
         mask: torch.Tensor | None = None,
     ) -> tuple[torch.Tensor, None]:
+        if isinstance(kv_cache, PoolLayerView):
+            return self._forward_pool(x, kv_cache, position_ids, mask)
         if x.shape[0] != 1:
-            raise ValueError("gqa_paged: the paged cache holds one sequence (batch 1)")
+            raise ValueError("gqa_paged: the paged cache holds one sequence (batch 1); use a pool view for more")
         q = self._split_heads(self.q_proj(x), self.n_heads)
         k = self._split_heads(self.k_proj(x), self.n_kv_heads)
         v = self._split_heads(self.v_proj(x), self.n_kv_heads)
@@ -175,4 +181,44 @@ class PagedGroupedQueryAttention(nn.Module):
         qd = q if q.dtype == cache.dtype else q.to(cache.dtype)
         out = cache.attend(layer, qd, scale=self.head_dim ** -0.5, causal=causal)
         out = out.to(x.dtype).transpose(1, 2).reshape(1, n_new, self.n_heads * self.head_dim)
+        return self.out_proj(out), None
+
+    def _forward_pool(self, x, view: PoolLayerView, position_ids, mask):
+        """B sequences of a ``PagedKVPool`` (grown by the caller's ``reserve`` for this
+        forward): one token each is a batched decode step; ``T`` tokens each (the
+        same ``T`` for all) is a causal prefill, attended per sequence."""
+        pool, layer = view.pool, view.layer
+        batch, n_new = x.shape[0], x.shape[1]
+        if batch != view.batch:
+            raise ValueError(f"gqa_paged: view holds {view.batch} sequences, input has {batch}")
+        if pool.n_kv_heads != self.n_kv_heads or pool.head_dim != self.head_dim:
+            raise ValueError("gqa_paged: pool heads / head_dim do not match the layer")
+        q = self._split_heads(self.q_proj(x), self.n_heads)
+        k = self._split_heads(self.k_proj(x), self.n_kv_heads)
+        v = self._split_heads(self.v_proj(x), self.n_kv_heads)
+        if self.pe is not None:
+            tables = self._rope_tables(q)
+            if tables is not None:
+                self._rope(q, k, position_ids, tables, pool.err)
+            else:
+                q, k = self.pe.apply_to_qk(q, k, position_ids)
+        qd = q if q.dtype == pool.dtype else q.to(pool.dtype)
+        if n_new == 1:
+            if mask is not None:
+                raise ValueError("gqa_paged: a decode step takes no mask")
+            pool.append(layer, k[:, :, 0], v[:, :, 0])
+            out = pool.decode(layer, qd[:, :, 0], max_seq_len=view.capacity)
+            out = out.to(x.dtype).reshape(batch, 1, self.n_heads * self.head_dim)
+        else:
+            if view.stored and mask is None:
+                raise ValueError("gqa_paged: pool views take multi-token steps as causal prefill only")
+            if mask is not None and not _is_causal_mask(mask, n_new, n_new):
+                raise ValueError("gqa_paged supports no mask or the causal mask only")
+            pool.append(layer, k, v)
+            out = torch.empty((batch, self.n_heads, n_new, self.head_dim), dtype=pool.dtype, device=x.device)
+            lens = pool.host_lens
+            for b in range(batch):
+                pool.attend_causal(layer, b, qd[b], out[b], int(lens[b]))
+            out = out.to(x.dtype).transpose(1, 2).reshape(batch, n_new, self.n_heads * self.head_dim)
+        view.stored += n_new
         return self.out_proj(out), None

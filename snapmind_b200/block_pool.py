@@ -88,6 +88,30 @@ class BlockPool:
         self._host_lens[:batch] += n_new
         self._host_free -= need
 
+    def blocks_needed(self, n_new: int, batch: int) -> int:
+        """Blocks the first ``batch`` sequences take to grow by ``n_new`` tokens."""
+        bs = self.block_size
+        lens = self._host_lens[:batch]
+        return int(((lens + n_new + bs - 1) // bs - (lens + bs - 1) // bs).sum())
+
+    def reserve_device(self, n_new: int, batch: int) -> None:
+        """The device part of ``reserve`` only (no host mirrors, no checks): a
+        launch that a CUDA graph can replay.  The caller checks the capacity
+        for all replays up front and accounts them with ``account_host``."""
+        status = _lib.load().snapmind_kv_reserve(
+            self.block_tables.data_ptr(), self.max_blocks_per_seq, self.max_blocks_per_seq,
+            self.seq_lens.data_ptr(), batch, n_new, self.block_size,
+            self.free_stack.data_ptr(), self.free_top.data_ptr(), self.num_blocks,
+            self.err.data_ptr(), self._stream(),
+        )  # fmt: skip
+        _lib.check(status, f"{type(self).__name__}.reserve_device")
+
+    def account_host(self, n_new: int, batch: int) -> None:
+        """Advance the host mirrors as ``reserve(n_new, batch)`` would."""
+        need = self.blocks_needed(n_new, batch)
+        self._host_lens[:batch] += n_new
+        self._host_free -= need
+
     def release(self, seq_ids: list[int]) -> None:
         """Return the blocks of finished sequences to the free stack."""
         if not seq_ids:

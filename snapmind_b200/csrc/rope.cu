@@ -8,8 +8,9 @@
 // with cos/sin rows of the module's tables (fp32, [n_pos][D]) cast to the
 // tensor's dtype first and each product and the sum rounded to that dtype, as
 // the three separate torch ops do — so the result is bit-identical to
-// apply_to_qk on the same device.  Position of token t: positions[t], or t
-// when positions is NULL (apply_to_qk without position_ids).
+// apply_to_qk on the same device.  Position of token t of sequence b:
+// positions[b * pos_stride_b + t], or t when positions is NULL (apply_to_qk
+// without position_ids).
 #include "common.cuh"
 
 namespace snapmind {
@@ -30,7 +31,7 @@ __device__ __forceinline__ T rope_round(float x) {
 template <typename T>
 __global__ void rope_qk_kernel(RopeTensor q, RopeTensor k, int batch, int n_tok, int head_dim,
                                const float* cos_t, const float* sin_t, int64_t n_pos, const int64_t* positions,
-                               int32_t* err) {
+                               int64_t pos_stride_b, int32_t* err) {
   const int half = head_dim / 2;
   const int64_t rows_q = (int64_t)batch * q.n_heads * n_tok;
   const int64_t rows = rows_q + (int64_t)batch * k.n_heads * n_tok;
@@ -45,7 +46,7 @@ __global__ void rope_qk_kernel(RopeTensor q, RopeTensor k, int batch, int n_tok,
     const int64_t bh = rr / n_tok;
     const int h = (int)(bh % ten.n_heads);
     const int b = (int)(bh / ten.n_heads);
-    const int64_t pos = positions ? positions[t] : t;
+    const int64_t pos = positions ? positions[(int64_t)b * pos_stride_b + t] : t;
     if (pos < 0 || pos >= n_pos) {
       flag_error(err, SNAPMIND_DEVERR_POSITION);
       continue;
@@ -77,8 +78,8 @@ extern "C" {
 int snapmind_rope_qk(void* q, int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_t, int32_t n_q_heads,
                      void* k, int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_t, int32_t n_kv_heads,
                      int dtype, int32_t batch, int32_t n_tok, int32_t head_dim, const float* cos_table,
-                     const float* sin_table, int64_t n_pos, const int64_t* positions, int32_t* err_word,
-                     void* stream) {
+                     const float* sin_table, int64_t n_pos, const int64_t* positions, int64_t pos_stride_b,
+                     int32_t* err_word, void* stream) {
   SNAPMIND_CHECK_ARG(dtype_size(dtype) > 0, "rope_qk: unknown dtype");
   SNAPMIND_CHECK_ARG(batch >= 0 && n_tok >= 0 && n_q_heads >= 0 && n_kv_heads >= 0 && head_dim > 0 &&
                          head_dim % 2 == 0 && n_pos > 0,
@@ -96,15 +97,15 @@ int snapmind_rope_qk(void* q, int64_t q_stride_b, int64_t q_stride_h, int64_t q_
   switch (dtype) {
     case SNAPMIND_DTYPE_F32:
       rope_qk_kernel<float><<<grid, threads, 0, st>>>(tq, tk, batch, n_tok, head_dim, cos_table, sin_table, n_pos,
-                                                      positions, err_word);
+                                                      positions, pos_stride_b, err_word);
       break;
     case SNAPMIND_DTYPE_BF16:
       rope_qk_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>(tq, tk, batch, n_tok, head_dim, cos_table, sin_table,
-                                                              n_pos, positions, err_word);
+                                                              n_pos, positions, pos_stride_b, err_word);
       break;
     default:
       rope_qk_kernel<__half><<<grid, threads, 0, st>>>(tq, tk, batch, n_tok, head_dim, cos_table, sin_table, n_pos,
-                                                       positions, err_word);
+                                                       positions, pos_stride_b, err_word);
   }
   return cuda_status(cudaGetLastError(), "rope_qk launch");
 }

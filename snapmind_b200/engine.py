@@ -18,12 +18,19 @@ batch 1 is bound by host launch overhead: hundreds of small launches per token.
   and decode kernels included, becomes one graph launch.
 
 The generated ids equal an eager run's; the cache ends in the same state.
+
+``BatchedGraphDecoder`` is the many-sequence form (the reference engine holds
+one sequence): B prompts of one length are prefilled into a ``PagedKVPool``,
+then every decode step grows all B sequences on the device
+(``snapmind_kv_reserve``), appends their K/V rows and runs one batched paged
+decode per layer — captured once and replayed, like ``GraphDecoder``.
 """
 from __future__ import annotations
 
 import torch
 
 from snapmind_b200.kv_cache.paged import PagedKVCache
+from snapmind_b200.paged_pool import PagedKVPool
 
 
 class GraphDecoder:
@@ -102,6 +109,94 @@ class GraphDecoder:
         self.prefill(prompt)
         if n_tokens <= 1:
             return [int(self.tok.item())][:n_tokens]
+        self.begin(n_tokens - 1)
+        self.step(n_tokens - 1)
+        return self.finish()
+
+
+class BatchedGraphDecoder:
+    def __init__(self, model: torch.nn.Module, pool: PagedKVPool, batch: int, use_graph: bool = True):
+        self.model, self.pool, self.batch, self.use_graph = model, pool, batch, use_graph
+        self.views = pool.layer_views(batch)
+        self._graph: torch.cuda.CUDAGraph | None = None
+        self._steps_left = 0
+
+    @torch.no_grad()
+    def prefill(self, prompts: torch.Tensor) -> None:
+        """``prompts``: token ids ``[B, T]`` (one length for all sequences)."""
+        dev = self.pool.device
+        b, t = prompts.shape
+        if b != self.batch:
+            raise ValueError(f"BatchedGraphDecoder: {b} prompts for a batch of {self.batch}")
+        self.model.eval()
+        self.pool.reserve(t, batch=b)
+        logits = self.model(prompts.to(dev), kv_cache=self.views)[:, -1]
+        self.tok = logits.argmax(-1).reshape(b, 1).clone()
+        self.pos = torch.full((b,), t, dtype=torch.long, device=dev)
+
+    @torch.no_grad()
+    def begin(self, n_steps: int) -> None:
+        pool, b = self.pool, self.batch
+        if pool.blocks_needed(n_steps, b) > pool._host_free:
+            raise RuntimeError("PagedKVCache: out of blocks")
+        cap = int(pool.host_lens[:b].max()) + n_steps
+        if (cap + pool.block_size - 1) // pool.block_size > pool.max_blocks_per_seq:
+            raise ValueError("BatchedGraphDecoder: sequences would outgrow their block table rows")
+        for view in self.views.values():
+            view.capacity = cap  # one split plan for every step
+        self.ids = torch.empty((n_steps + 1, b), dtype=torch.long, device=pool.device)
+        self.ids[0] = self.tok.reshape(b)
+        self.idx = torch.ones((1,), dtype=torch.long, device=pool.device)
+        self._steps_total = self._steps_left = n_steps
+        self._graph = None
+
+    def _step(self) -> None:
+        self.pool.reserve_device(1, self.batch)
+        logits = self.model(self.tok, kv_cache=self.views, position_ids=self.pos)[:, -1]
+        self.tok.copy_(logits.argmax(-1).reshape(self.batch, 1))
+        self.ids.index_copy_(0, self.idx, self.tok.reshape(1, self.batch))
+        self.pos.add_(1)
+        self.idx.add_(1)
+
+    @torch.no_grad()
+    def step(self, n: int = 1) -> None:
+        dev = self.pool.device
+        for _ in range(n):
+            if self._steps_left <= 0:
+                raise RuntimeError("BatchedGraphDecoder: no decode steps left")
+            if self._graph is None and (not self.use_graph or self._steps_left == self._steps_total):
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(side):
+                    self._step()
+                torch.cuda.current_stream(dev).wait_stream(side)
+                if self.use_graph and self._steps_left > 1:
+                    self._graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(self._graph):  # recorded, not run
+                        self._step()
+            elif self._graph is not None:
+                self._graph.replay()
+            else:
+                self._step()
+            self._steps_left -= 1
+
+    @torch.no_grad()
+    def finish(self) -> list[list[int]]:
+        """Account the steps on the host and return each sequence's ids."""
+        if self._steps_left:
+            raise RuntimeError(f"BatchedGraphDecoder: {self._steps_left} decode steps not run")
+        self._graph = None
+        self.pool.account_host(self._steps_total, self.batch)
+        for view in self.views.values():
+            view.capacity = None
+        self.pool.check()
+        return self.ids.t().tolist()
+
+    @torch.no_grad()
+    def generate(self, prompts: torch.Tensor, n_tokens: int) -> list[list[int]]:
+        self.prefill(prompts)
+        if n_tokens <= 1:
+            return self.tok.reshape(-1, 1)[:, :n_tokens].tolist()
         self.begin(n_tokens - 1)
         self.step(n_tokens - 1)
         return self.finish()

@@ -16,6 +16,8 @@ Block bookkeeping (tables, lengths, free stack, reserve/release) is in
 """
 from __future__ import annotations
 
+from collections.abc import MutableMapping
+
 import torch
 
 from snapmind_b200 import _lib
@@ -157,3 +159,78 @@ class PagedKVPool(BlockPool):
         )  # fmt: skip
         _lib.check(status, "PagedKVPool.decode")
         return out
+
+    def _lens_ladder(self, n: int) -> torch.Tensor:
+        lad = getattr(self, "_ladder", None)
+        if lad is None or lad.numel() < n:
+            lad = torch.arange(1, max(n, 1) + 1, dtype=torch.int32, device=self.device)
+            self._ladder = lad
+        return lad
+
+    def attend_causal(self, layer: int, b: int, q: torch.Tensor, out: torch.Tensor, n_b: int,
+                      scale: float | None = None) -> torch.Tensor:
+        """Causal attention of the newest ``T`` tokens of sequence ``b``
+        (``q``/``out`` ``[Hq, T, D]``, sequence length ``n_b``): query t sees the
+        first ``n_b - T + t + 1`` tokens; one decode-kernel row per query, all
+        on the sequence's table row."""
+        n_q, n_t = q.shape[0], q.shape[1]
+        if n_t == 0:
+            return out
+        scale = self.head_dim ** -0.5 if scale is None else scale
+        lad = self._lens_ladder(n_b)
+        lib = _lib.load()
+        split = lib.snapmind_paged_gqa_decode_split_tokens(n_t, self.n_kv_heads, n_b, self.block_size)
+        ws = self._decode_workspace(n_t, n_q, n_b, split)
+        status = lib.snapmind_paged_gqa_decode(
+            q.data_ptr(), q.stride(1), q.stride(0),
+            self.k[layer].data_ptr(), self.v[layer].data_ptr(), self._dcode,
+            self.block_tables[b].data_ptr(), 0, self.max_blocks_per_seq, lad.data_ptr() + 4 * (n_b - n_t),
+            out.data_ptr(), out.stride(1), out.stride(0),
+            float(scale), n_t, n_q, self.n_kv_heads, self.head_dim, self.block_size, self.num_blocks,
+            n_b, split, 0, ws.data_ptr(), ws.numel(), self.err.data_ptr(), self._stream(),
+        )  # fmt: skip
+        _lib.check(status, "PagedKVPool.attend_causal")
+        return out
+
+    def layer_views(self, batch: int) -> dict[int, "PoolLayerView"]:
+        """One ``kv_cache`` view per layer for sequences ``0 .. batch - 1``."""
+        return {i: PoolLayerView(self, i, batch) for i in range(self.n_layers)}
+
+
+class PoolLayerView(MutableMapping):
+    """The ``kv_cache`` of one layer for a batch of sequences of a
+    :class:`PagedKVPool`, read and written by the ``gqa_paged`` attention plugin.
+
+    The sequences are ragged, so the view holds no dense K/V tensor: ``"k"`` /
+    ``"v"`` read as ``None`` until the layer has stored tokens (a model's prefill
+    test, e.g. ``kv_cache.get("k") is None``) and as an empty placeholder after.
+    The caller grows the sequences (``reserve``) before each forward; the
+    plugin appends the new rows and attends from the pool.  ``capacity``, when
+    set, is the length bound the decode split plan is made for (fixed plans
+    for CUDA-graph replay).
+    """
+
+    KEYS = ("k", "v")
+
+    def __init__(self, pool: PagedKVPool, layer: int, batch: int):
+        self.pool, self.layer, self.batch = pool, layer, batch
+        self.stored = 0
+        self.capacity: int | None = None
+        self._placeholder = torch.empty(0, dtype=pool.dtype, device=pool.device)
+
+    def __getitem__(self, key):
+        if key not in self.KEYS:
+            raise KeyError(key)
+        return None if self.stored == 0 else self._placeholder
+
+    def __setitem__(self, key, value):
+        raise TypeError("PoolLayerView is written by the gqa_paged attention plugin only")
+
+    def __delitem__(self, key):
+        raise TypeError("PoolLayerView entries cannot be deleted")
+
+    def __iter__(self):
+        return iter(self.KEYS)
+
+    def __len__(self):
+        return len(self.KEYS)

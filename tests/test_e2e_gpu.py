@@ -236,3 +236,37 @@ def test_graph_decoder_matches_reference_and_eager(cuda_device, use_graph):
             ke, ve = eager.fetch(layer)
             torch.testing.assert_close(k, ke, rtol=1e-5, atol=1e-6)
             torch.testing.assert_close(v, ve, rtol=1e-5, atol=1e-6)
+
+
+@torch.no_grad()
+@pytest.mark.parametrize("use_graph", [True, False])
+def test_batched_graph_decoder_matches_single_sequences(cuda_device, use_graph):
+    """B prompts decoded together on a PagedKVPool give, per sequence, the ids and
+    cached K/V of decoding that prompt alone (small Llama shape, fp32)."""
+    from snapmind_b200 import PagedGroupedQueryAttention, PagedKVCache, PagedKVPool
+    from snapmind_b200.engine import BatchedGraphDecoder, GraphDecoder
+
+    sh, B, T, n_gen = SMALL, 3, 24, 8
+    model = LlamaHarness(sh, PagedGroupedQueryAttention)
+    init_weights(model, 7)
+    model.to(cuda_device)
+    hd = sh.d_model // sh.n_heads
+    prompts = torch.stack([prompt_ids(sh.vocab_size, T, 100 + i) for i in range(B)])
+    pool = PagedKVPool(sh.n_layers, sh.n_kv_heads, hd, num_blocks=64, max_seqs=B, max_blocks_per_seq=8,
+                       block_size=16, dtype=torch.float32)
+    ids = BatchedGraphDecoder(model, pool, B, use_graph=use_graph).generate(prompts, n_gen)
+    assert list(pool.host_lens[:B]) == [T + n_gen - 1] * B
+    k_all, v_all = pool.gather(B)
+    off = 0
+    for b in range(B):
+        cache = PagedKVCache(sh.max_seq_len, sh.n_layers, sh.n_kv_heads, hd)
+        want = GraphDecoder(model, cache).generate(prompts[b], n_gen)
+        assert ids[b] == want, b
+        n = T + n_gen - 1
+        for layer in range(sh.n_layers):
+            k, v = cache.fetch(layer)
+            got_k = k_all[layer, off: off + k.numel()].reshape(k.shape)
+            got_v = v_all[layer, off: off + v.numel()].reshape(v.shape)
+            torch.testing.assert_close(got_k, k, rtol=1e-5, atol=1e-6)
+            torch.testing.assert_close(got_v, v, rtol=1e-5, atol=1e-6)
+        off += sh.n_kv_heads * n * hd

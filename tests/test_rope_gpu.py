@@ -22,7 +22,7 @@ def _run(q, k, cos_t, sin_t, positions, err):
         q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), q.shape[1],
         k.data_ptr(), k.stride(0), k.stride(1), k.stride(2), k.shape[1],
         _lib.dtype_code(q.dtype), q.shape[0], q.shape[2], q.shape[3], cos_t.data_ptr(), sin_t.data_ptr(),
-        cos_t.shape[0], None if positions is None else positions.data_ptr(), err.data_ptr(), _lib.stream_handle(),
+        cos_t.shape[0], None if positions is None else positions.data_ptr(), 0, err.data_ptr(), _lib.stream_handle(),
     )  # fmt: skip
     _lib.check(rc, "rope")
 
