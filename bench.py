@@ -52,8 +52,11 @@ def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        out = {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+        if "bf16_tflops" in d:
+            out["bf16_tflops"] = float(d["bf16_tflops"])
+        return out
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 def profile_traffic(kernel: str) -> dict | None:
@@ -676,8 +679,10 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
     from snapmind_b200.mla import MLALatentPool
 
     B = MLA_B
-    steps = min(args.steps, 100)
-    warmup = args.warmup
+    # a step is ~0.15 ms: time 1000 of them (after a chunk's worth of warm-up) so that the
+    # timed region is long enough for steady clocks
+    steps = max(args.steps, 1000)
+    warmup = max(args.warmup, MLA_CHUNK)
     ctx_chunks = MLA_CTX // MLA_CHUNK
     width = ctx_chunks + (steps + warmup) // MLA_CHUNK + 2
     nb = B * width
@@ -699,33 +704,108 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
     scale = (128 + 64) ** -0.5
     launches = [0]
 
-    def step():
-        pool.reserve(1, batch=B)
-        pool.append(0, lat_new, rope_new)
-        length = int(pool.host_lens[0])  # every sequence has the same length here
-        launches[0] += 3
-        if length % MLA_CHUNK == 0:  # a chunk just completed: its key joins the index
-            sel.update_keys(0, length // MLA_CHUNK - 1, 1, batch=B)
-            launches[0] += 1
-        idx, _ = sel.select(sel.query(hidden), length // MLA_CHUNK, k=MLA_TOPK)
-        pool.sparse_decode(0, q_lat, q_pe, idx, sink=4, window=1024, scale=scale, n_splits=4)
-        launches[0] += 2
+    n_chunks_dev = torch.full((B,), ctx_chunks, dtype=torch.int32, device=dev)  # complete chunks
 
-    for _ in range(warmup):
-        step()
+    def core():  # one step that completes no chunk: every launch replayable
+        pool.reserve_device(1, B)
+        pool.append(0, lat_new, rope_new)
+        idx, _ = sel.select(sel.query(hidden), n_chunks_dev, k=MLA_TOPK)
+        pool.sparse_decode(0, q_lat, q_pe, idx, sink=4, window=1024, scale=scale, n_splits=4)
+
+    graphs: dict[int, torch.cuda.CUDAGraph] = {}
+
+    def capture(n_core: int) -> None:  # recorded, not run
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for _ in range(n_core):
+                core()
+        graphs[n_core] = gr
+
+    def replay(n_core: int) -> None:  # n_core steps that complete no chunk, as one graph launch
+        if not graphs:  # first: one eager step on a side stream (allocates the workspaces)
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                core()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            pool.account_host(1, B)
+            launches[0] += 4
+            for n in (1, 8):
+                capture(n)
+            n_core -= 1
+            if n_core == 0:
+                return
+            if n_core not in graphs:
+                for _ in range(n_core):
+                    replay(1)
+                return
+        graphs[n_core].replay()
+        pool.account_host(n_core, B)
+        launches[0] += 4 * n_core
+
+    def run_steps(n: int) -> None:
+        done = 0
+        while done < n:
+            length = int(pool.host_lens[0])  # every sequence has the same length here
+            if (length + 1) % MLA_CHUNK == 0:  # this step completes a chunk: its key joins the index
+                pool.reserve(1, batch=B)
+                pool.append(0, lat_new, rope_new)
+                sel.update_keys(0, (length + 1) // MLA_CHUNK - 1, 1, batch=B)
+                n_chunks_dev.add_(1)
+                idx, _ = sel.select(sel.query(hidden), n_chunks_dev, k=MLA_TOPK)
+                pool.sparse_decode(0, q_lat, q_pe, idx, sink=4, window=1024, scale=scale, n_splits=4)
+                launches[0] += 5
+                done += 1
+                continue
+            free = MLA_CHUNK - 1 - (length + 1) % MLA_CHUNK  # later steps before the completing one
+            m = min(n - done, free + 1)
+            while m > 0:
+                c = 8 if m >= 8 else 1
+                replay(c)
+                m -= c
+                done += c
+
+    run_steps(warmup)
     pool.check()
     launches[0] = 0
     barrier(dist)
     torch.cuda.synchronize(dev)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
-    for _ in range(steps):
-        step()
+    run_steps(steps)
     t1.record()
     torch.cuda.synchronize(dev)
     barrier(dist)
     pool.check()
     ms = reduce_max(dist, t0.elapsed_time(t1), dev)
+    # kernel-only times: 20 back-to-back launches captured in a graph, replayed once
+    qsel = sel.query(hidden)
+    idx0, _ = sel.select(qsel, n_chunks_dev, k=MLA_TOPK)
+
+    def graph_us(fn, reps=20):
+        fn()
+        torch.cuda.synchronize(dev)
+        g_ = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_):
+            for _ in range(reps):
+                fn()
+        g_.replay()
+        torch.cuda.synchronize(dev)
+        e0_, e1_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0_.record()
+        g_.replay()
+        e1_.record()
+        torch.cuda.synchronize(dev)
+        return e0_.elapsed_time(e1_) * 1e3 / reps
+
+    select_us = graph_us(lambda: sel.select(qsel, n_chunks_dev, k=MLA_TOPK))
+    sparse_us = graph_us(lambda: pool.sparse_decode(0, q_lat, q_pe, idx0, sink=4, window=1024, scale=scale,
+                                                    n_splits=4))
+    # attended rows per sequence: top-k chunks + the sink chunk + the window chunks (about)
+    att_tokens = B * (MLA_TOPK * MLA_CHUNK + MLA_CHUNK + 1024 + MLA_CHUNK)
+    sparse_bytes = att_tokens * (MLA_RANK + MLA_ROPE) * 2
+    sparse_flops = att_tokens * MLA_HEADS * 2 * ((MLA_RANK + MLA_ROPE) + MLA_RANK)
+    key_bytes = B * (int(pool.host_lens[0]) // MLA_CHUNK) * 128 * 4
     # full latent gather and all-chunk key pooling (HBM-bound)
     length = int(pool.host_lens[0])
     lo = torch.empty((B, length, MLA_RANK), dtype=torch.bfloat16, device=dev)
@@ -757,6 +837,13 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
         "chunk_pool_gbs": round(pool_bytes / (pool_ms * 1e-3) / 1e9, 1),
         "chunk_pool_frac": round(pool_bytes / (pool_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
         "gpu_launches": launches[0],
+        "select_us": round(select_us, 2),
+        "select_key_gbs": round(key_bytes / (select_us * 1e-6) / 1e9, 1),
+        "sparse_attn_us": round(sparse_us, 2),
+        "sparse_attn_gbs": round(sparse_bytes / (sparse_us * 1e-6) / 1e9, 1),
+        "sparse_attn_tflops": round(sparse_flops / (sparse_us * 1e-6) / 1e12, 2),
+        "sparse_attn_tensor_frac": round(sparse_flops / (sparse_us * 1e-6) / 1e12 / pk["bf16_tflops"], 4)
+        if pk.get("bf16_tflops") else None,
     }
     del pool, lo, ro
     torch.cuda.empty_cache()

@@ -1,7 +1,7 @@
 // Tensor-core sparse MLA decode (bf16/f16, kv_lora_rank 512, rope 64,
 // 64-token chunks) for sm_100a.
 //
-// CTA = (split, group of 16 MT heads, sequence), 4 MT warps (MT = 2 when the
+// CTA = (split, group of 16 MT heads, sequence), 8 MT warps (MT = 2 when the
 // heads divide by 32).  Each m-tile of 16 heads is the M dimension of
 // mma.sync m16n8k16 — a dense tile, which is why this kernel uses tensor cores
 // while the paged GQA decode (query group <= 8) is byte-bound anyway.  Per
@@ -10,13 +10,13 @@
 //     to 1168 bytes (ldmatrix of 8 consecutive rows hits 8 distinct bank
 //     groups), double-buffered; rows outside the selection are zero-filled;
 //     the staged tile serves every m-tile of the CTA;
-//   * S = Q K^T: warp (mt, w4) owns tokens [16 w4, 16 w4 + 16) of m-tile mt:
-//     36 k-steps x 2 MMAs on two alternating accumulator chains;
-//   * the tile's row maxima / sums are merged across the 4 warps of an m-tile
+//   * S = Q K^T: warp (mt, wm) owns tokens [8 wm, 8 wm + 8) of m-tile mt:
+//     36 k-steps x 1 MMA on four accumulator chains (k mod 4);
+//   * the tile's row maxima / sums are merged across the 8 warps of an m-tile
 //     in shared memory (online softmax in base 2, scale folded in), P is
 //     staged as bf16;
-//   * O += P V: warp (mt, w4) owns output dims [128 w4, 128 w4 + 128):
-//     4 k-steps x 16 MMAs, V^T fragments via ldmatrix.trans.
+//   * O += P V: warp (mt, wm) owns output dims [64 wm, 64 wm + 64):
+//     4 k-steps x 8 MMAs, V^T fragments via ldmatrix.trans.
 // Splits merge through the last-ticket combine of the paged GQA decode.
 #include "common.cuh"
 #include "paged_decode.cuh"
@@ -78,7 +78,8 @@ __device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
   return (uint32_t)(*reinterpret_cast<uint16_t*>(&a)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&b)) << 16);
 }
 
-constexpr int kMaxWarps = 8;
+constexpr int kWPM = 8;       // warps per 16-head m-tile
+constexpr int kMaxWarps = 16;
 
 struct TcSmem {
   uint32_t sel_bits[kBits / 32];
@@ -108,14 +109,14 @@ __device__ __forceinline__ int chunk_of_rank(const TcSmem& S, int words, int ran
   return lo * 32 + __ffs(word) - 1;
 }
 
-// MT m-tiles of 16 heads per CTA, 4 warps per m-tile: warp = 4 mt + w4.
-// S = Q K^T: warp (mt, w4) scores heads [16 mt, 16 mt + 16) against tokens
-// [16 w4, 16 w4 + 16) of the tile; O += P V: warp (mt, w4) owns those heads x
-// latent dims [128 w4, 128 w4 + 128).  The K/V tile in shared memory serves
-// all m-tiles.
+// MT m-tiles of 16 heads per CTA, kWPM = 8 warps per m-tile: warp = 8 mt + wm.
+// S = Q K^T: warp (mt, wm) scores heads [16 mt, 16 mt + 16) against tokens
+// [8 wm, 8 wm + 8) of the tile; O += P V: warp (mt, wm) owns those heads x
+// latent dims [64 wm, 64 wm + 64).  The K/V tile in shared memory serves
+// all m-tiles; small per-warp accumulators keep 16 warps resident.
 template <typename T, int MT>
-__global__ void __launch_bounds__(128 * MT, 1) sparse_mla_tc_kernel(SparseParams p) {
-  constexpr int kWarps = 4 * MT;
+__global__ void __launch_bounds__(32 * kWPM * MT, 1) sparse_mla_tc_kernel(SparseParams p) {
+  constexpr int kWarps = kWPM * MT;
   constexpr int kThreads = 32 * kWarps;
   constexpr size_t kQBytes = (size_t)16 * MT * kRowBytes;
   constexpr size_t kPBytes = (size_t)16 * MT * kPRowBytes;
@@ -129,7 +130,7 @@ __global__ void __launch_bounds__(128 * MT, 1) sparse_mla_tc_kernel(SparseParams
 
   const int s = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int mt = warp >> 2, w4 = warp & 3;
+  const int mt = warp / kWPM, wm = warp % kWPM;
   const int g = lane >> 2, tig = lane & 3;
   const int bs = kTileRows;
 
@@ -227,15 +228,15 @@ __global__ void __launch_bounds__(128 * MT, 1) sparse_mla_tc_kernel(SparseParams
   const float c2 = p.scale * 1.4426950408889634f;
   float m_run[2] = {-INFINITY, -INFINITY};  // heads g, g+8 of this warp's m-tile
   float l_run[2] = {0.f, 0.f};
-  float o[16][4];
+  float o[8][4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
   // ldmatrix lane addressing
   const int a_row = (lane & 7) + ((lane >> 3) & 1) * 8;  // Q / P rows 0-15 of the m-tile
   const int a_kof = (lane >> 4) * 8;                      // +8 elements for matrices 2,3
-  const int b_tok = (lane & 7) + ((lane >> 4) & 1) * 8;   // K rows (tokens) for B non-trans
-  const int b_kof = ((lane >> 3) & 1) * 8;
+  const int b_tok = lane & 7;                             // K rows (8 tokens) for B non-trans
+  const int b_kof = (lane >> 3) * 8;                      // matrices 0-3: k offsets 0, 8, 16, 24
   const int v_tok = (lane & 7) + ((lane >> 3) & 1) * 8;   // V^T: tokens 0-15 (matrices 0,1 / 2,3)
   const int v_dof = (lane >> 4) * 8;
   const unsigned char* q_rows = q_s + (16 * mt + a_row) * kRowBytes;
@@ -253,43 +254,41 @@ __global__ void __launch_bounds__(128 * MT, 1) sparse_mla_tc_kernel(SparseParams
     __syncthreads();
     const int c = S.tile_chunk[buf];
     const unsigned char* kv = kv_s + buf * kKvBytes;
-    // ---- S = Q K^T for tokens [16 w4, 16 w4 + 16): two accumulator chains (even / odd k)
-    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    float sd[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    const unsigned char* k_rows = kv + (16 * w4 + b_tok) * kRowBytes;
-#pragma unroll 2
-    for (int k = 0; k < kRow / 16; k += 2) {
-      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-      ldsm4(smem_u32(q_rows + (k * 16 + a_kof) * 2), a0, a1, a2, a3);
-      ldsm4(smem_u32(k_rows + (k * 16 + b_kof) * 2), b0, b1, b2, b3);
-      mma<T>(sc[0], a0, a1, a2, a3, b0, b1);
-      mma<T>(sc[1], a0, a1, a2, a3, b2, b3);
-      ldsm4(smem_u32(q_rows + ((k + 1) * 16 + a_kof) * 2), a0, a1, a2, a3);
-      ldsm4(smem_u32(k_rows + ((k + 1) * 16 + b_kof) * 2), b0, b1, b2, b3);
-      mma<T>(sd[0], a0, a1, a2, a3, b0, b1);
-      mma<T>(sd[1], a0, a1, a2, a3, b2, b3);
+    // ---- S = Q K^T for tokens [8 wm, 8 wm + 8): one B load covers two k-steps;
+    //      four accumulator chains (k mod 4)
+    float acc4[4][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc4[c][0] = acc4[c][1] = acc4[c][2] = acc4[c][3] = 0.f;
+    const unsigned char* k_rows = kv + (8 * wm + b_tok) * kRowBytes;
+    for (int k = 0; k < kRow / 16; k += 4) {
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm4(smem_u32(k_rows + ((k + 2 * h2) * 16 + b_kof) * 2), b0, b1, b2, b3);
+        uint32_t a0, a1, a2, a3;
+        ldsm4(smem_u32(q_rows + ((k + 2 * h2) * 16 + a_kof) * 2), a0, a1, a2, a3);
+        mma<T>(acc4[2 * h2], a0, a1, a2, a3, b0, b1);
+        ldsm4(smem_u32(q_rows + ((k + 2 * h2 + 1) * 16 + a_kof) * 2), a0, a1, a2, a3);
+        mma<T>(acc4[2 * h2 + 1], a0, a1, a2, a3, b2, b3);
+      }
     }
+    float sc[4];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sc[nt][e] += sd[nt][e];
-    // validity of this thread's 4 token columns
+    for (int e = 0; e < 4; ++e) sc[e] = (acc4[0][e] + acc4[1][e]) + (acc4[2][e] + acc4[3][e]);
+    // validity of this thread's 2 token columns (rows g and g + 8)
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int r = 16 * w4 + nt * 8 + 2 * tig + e;
-        const int pos = c * bs + r;
-        const bool selected = c >= 0 && ((S.sel_bits[c >> 5] >> (c & 31)) & 1u);
-        const bool valid = c >= 0 && pos < len && (selected || pos < sink || pos >= wstart);
-        if (!valid) {
-          sc[nt][e] = -INFINITY;
-          sc[nt][2 + e] = -INFINITY;
-        }
-        mx[0] = fmaxf(mx[0], sc[nt][e]);
-        mx[1] = fmaxf(mx[1], sc[nt][2 + e]);
+    for (int e = 0; e < 2; ++e) {
+      const int r = 8 * wm + 2 * tig + e;
+      const int pos = c * bs + r;
+      const bool selected = c >= 0 && ((S.sel_bits[c >> 5] >> (c & 31)) & 1u);
+      const bool valid = c >= 0 && pos < len && (selected || pos < sink || pos >= wstart);
+      if (!valid) {
+        sc[e] = -INFINITY;
+        sc[2 + e] = -INFINITY;
       }
+      mx[0] = fmaxf(mx[0], sc[e]);
+      mx[1] = fmaxf(mx[1], sc[2 + e]);
     }
 #pragma unroll
     for (int off = 1; off < 4; off <<= 1) {
@@ -306,21 +305,20 @@ __global__ void __launch_bounds__(128 * MT, 1) sparse_mla_tc_kernel(SparseParams
     for (int hh = 0; hh < 2; ++hh) {
       float tm = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < 4; ++w) tm = fmaxf(tm, S.red_max[4 * mt + w][g + 8 * hh]);
+      for (int w = 0; w < kWPM; ++w) tm = fmaxf(tm, S.red_max[kWPM * mt + w][g + 8 * hh]);
       m_new[hh] = fmaxf(m_run[hh], tm);
       alpha[hh] = (m_run[hh] == -INFINITY) ? 0.f : exp2f((m_run[hh] - m_new[hh]) * c2);
     }
     float ps[2] = {0.f, 0.f};
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
+    {
       float pv[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int hh = e >> 1;
-        pv[e] = (m_new[hh] == -INFINITY) ? 0.f : exp2f((sc[nt][e] - m_new[hh]) * c2);
+        pv[e] = (m_new[hh] == -INFINITY) ? 0.f : exp2f((sc[e] - m_new[hh]) * c2);
         ps[hh] += pv[e];
       }
-      const int col = 16 * w4 + nt * 8 + 2 * tig;
+      const int col = 8 * wm + 2 * tig;
       *reinterpret_cast<uint32_t*>(p_rows + g * kPRowBytes + col * 2) = pack_pair<T>(pv[0], pv[1]);
       *reinterpret_cast<uint32_t*>(p_rows + (g + 8) * kPRowBytes + col * 2) = pack_pair<T>(pv[2], pv[3]);
     }
@@ -338,13 +336,13 @@ __global__ void __launch_bounds__(128 * MT, 1) sparse_mla_tc_kernel(SparseParams
     for (int hh = 0; hh < 2; ++hh) {
       float tsum = 0.f;
 #pragma unroll
-      for (int w = 0; w < 4; ++w) tsum += S.red_sum[4 * mt + w][g + 8 * hh];
+      for (int w = 0; w < kWPM; ++w) tsum += S.red_sum[kWPM * mt + w][g + 8 * hh];
       l_run[hh] = l_run[hh] * alpha[hh] + tsum;
       m_run[hh] = m_new[hh];
     }
-    // ---- O (16 heads x dims [128 w4, 128 w4 + 128)) += P V
+    // ---- O (16 heads x dims [64 wm, 64 wm + 64)) += P V
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
+    for (int nt = 0; nt < 8; ++nt) {
       o[nt][0] *= alpha[0];
       o[nt][1] *= alpha[0];
       o[nt][2] *= alpha[1];
@@ -355,8 +353,8 @@ __global__ void __launch_bounds__(128 * MT, 1) sparse_mla_tc_kernel(SparseParams
       uint32_t a0, a1, a2, a3;
       ldsm4(smem_u32(p_rows + a_row * kPRowBytes + (ks * 16 + a_kof) * 2), a0, a1, a2, a3);
 #pragma unroll
-      for (int np = 0; np < 8; ++np) {
-        const int d0 = 128 * w4 + np * 16;
+      for (int np = 0; np < 4; ++np) {
+        const int d0 = 64 * wm + np * 16;
         uint32_t b0, b1, b2, b3;
         ldsm4t(smem_u32(kv + (ks * 16 + v_tok) * kRowBytes + (d0 + v_dof) * 2), b0, b1, b2, b3);
         mma<T>(o[2 * np], a0, a1, a2, a3, b0, b1);
@@ -371,12 +369,12 @@ __global__ void __launch_bounds__(128 * MT, 1) sparse_mla_tc_kernel(SparseParams
   const DecodeParams& dp = p.dp;
   const bool direct = (p.n_splits == 1);
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
+  for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int hh = e >> 1;
       const int head = 16 * mt + g + 8 * hh;
-      const int d = 128 * w4 + nt * 8 + 2 * tig + (e & 1);
+      const int d = 64 * wm + nt * 8 + 2 * tig + (e & 1);
       if (direct) {
         T* out = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)(h0 + head) * dp.out_stride_head;
         out[d] = Conv<T>::from_f(l_run[hh] > 0.f ? o[nt][e] / l_run[hh] : 0.f);
@@ -424,7 +422,7 @@ int launch_sparse_mla_tc(const SparseParams& p, int dtype, cudaStream_t st) {
   auto go = [&](auto kernel, size_t smem) -> int {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_status(e, "sparse_mla_tc smem attribute");
-    kernel<<<grid, 128 * mt, smem, st>>>(p);
+    kernel<<<grid, 32 * kWPM * mt, smem, st>>>(p);
     return cuda_status(cudaGetLastError(), "sparse_mla_tc launch");
   };
   if (dtype == SNAPMIND_DTYPE_BF16) {
