@@ -351,6 +351,27 @@ SNAPMIND_API int snapmind_paged_gqa_decode(const void *q, int64_t q_stride_seq, 
                               void *stream);
 
 /*
+ * snapmind_paged_gqa_decode over a window of each sequence: sequence b attends
+ * to tokens [seq_starts[b], seq_lens[b]) of its table row (seq_starts: int32,
+ * device, one entry per sequence; a start at or past the length gives a zero
+ * output).  For a sliding window kept as a ring of blocks the start is below
+ * block_size: the blocks before the window are dropped from the table and the
+ * first block's leading tokens are masked.  No reference counterpart as one op:
+ * the reference trims the concatenated K/V to the window
+ * (snapmind/kv_cache/sliding_window.py:31-38, snapmind/models/mistral.py:58-60).
+ */
+SNAPMIND_API int snapmind_paged_gqa_decode_window(const void *q, int64_t q_stride_seq, int64_t q_stride_head,
+                                                 const void *k_pool, const void *v_pool, int dtype,
+                                                 const int32_t *block_tables, int64_t table_stride_seq,
+                                                 int32_t table_width, const int32_t *seq_lens,
+                                                 const int32_t *seq_starts, void *out, int64_t out_stride_seq,
+                                                 int64_t out_stride_head, float scale, int32_t batch,
+                                                 int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
+                                                 int32_t block_size, int32_t num_blocks, int32_t max_seq_len,
+                                                 int32_t split_tokens, int32_t flags, void *workspace,
+                                                 int64_t workspace_bytes, int32_t *err_word, void *stream);
+
+/*
  * The same paged GQA decode for callers that cannot allocate device memory:
  * a host bound through this C ABI with no CUDA allocator of its own (or whose
  * device memory belongs to another allocator it cannot reach), or a serving

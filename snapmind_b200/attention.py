@@ -40,6 +40,7 @@ import torch.nn as nn
 
 from snapmind_b200 import _lib
 from snapmind_b200.kv_cache.paged import PagedKVCache, PagedLayerView
+from snapmind_b200.kv_cache.sliding_window import SlidingLayerView
 from snapmind_b200.paged_pool import PoolLayerView
 from snapmind_b200.registry import ATTENTION
 
@@ -54,6 +55,18 @@ def _is_causal_mask(mask: torch.Tensor, n_q: int, n_k: int) -> bool:
     upper = torch.ones((n_q, n_k), dtype=torch.bool, device=m.device).triu(1)
     ok = torch.where(upper, torch.isneginf(m), m == 0)
     return bool(ok.all())
+
+
+def _is_window_mask(mask: torch.Tensor, n: int, window: int) -> bool:
+    """True if ``mask`` is snapmind/models/mistral.py ``create_sliding_window_mask(n, window)``:
+    row i open on ``[max(0, i - window + 1), i]``, ``-inf`` elsewhere."""
+    if mask.shape[-2:] != (n, n):
+        return False
+    m = mask.reshape(n, n)
+    i = torch.arange(n, device=m.device)[:, None]
+    j = torch.arange(n, device=m.device)[None, :]
+    allowed = (j <= i) & (j >= i - window + 1)
+    return bool(torch.where(allowed, m == 0, torch.isneginf(m)).all())
 
 
 @ATTENTION.register("gqa_paged")
@@ -133,6 +146,8 @@ class PagedGroupedQueryAttention(nn.Module):
     ) -> tuple[torch.Tensor, None]:
         if isinstance(kv_cache, PoolLayerView):
             return self._forward_pool(x, kv_cache, position_ids, mask)
+        if isinstance(kv_cache, SlidingLayerView):
+            return self._forward_window(x, kv_cache, position_ids, mask)
         if x.shape[0] != 1:
             raise ValueError("gqa_paged: the paged cache holds one sequence (batch 1); use a pool view for more")
         q = self._split_heads(self.q_proj(x), self.n_heads)
@@ -221,4 +236,62 @@ class PagedGroupedQueryAttention(nn.Module):
                 pool.attend_causal(layer, b, qd[b], out[b], int(lens[b]))
             out = out.to(x.dtype).transpose(1, 2).reshape(batch, n_new, self.n_heads * self.head_dim)
         view.stored += n_new
+        return self.out_proj(out), None
+
+    def _forward_window(self, x, view: SlidingLayerView, position_ids, mask):
+        """One sequence over a ``"sliding_window"`` cache, with the reference's window
+        semantics (snapmind/models/mistral.py:14-21 and 48-60): a prefill on an
+        empty window takes the sliding-window (or causal) mask, query i seeing
+        rows ``[i - window + 1, i]`` — run in chunks of at most ``window``
+        queries; without a mask every query sees every held token plus the new
+        ones.  The window is trimmed to ``window_size`` afterwards, as the
+        reference's Mistral block does."""
+        cache, layer = view.cache, view.layer_idx
+        if x.shape[0] != 1:
+            raise ValueError("gqa_paged: the sliding-window cache holds one sequence (batch 1)")
+        q = self._split_heads(self.q_proj(x), self.n_heads)
+        k = self._split_heads(self.k_proj(x), self.n_kv_heads)
+        v = self._split_heads(self.v_proj(x), self.n_kv_heads)
+        if cache.n_heads != self.n_kv_heads or cache.head_dim != self.head_dim:
+            raise ValueError("gqa_paged: cache heads / head_dim do not match the layer")
+        if self.pe is not None:
+            tables = self._rope_tables(q)
+            if tables is not None:
+                self._rope(q, k, position_ids, tables, cache._err)
+            else:
+                q, k = self.pe.apply_to_qk(q, k, position_ids)
+        w, n_new, n_old = cache.window_size, x.shape[1], cache.num_tokens(layer)
+        if mask is not None:
+            if n_old:
+                raise ValueError("gqa_paged: a masked prefill needs an empty window")
+            if not (_is_window_mask(mask, n_new, w) or (n_new <= w and _is_causal_mask(mask, n_new, n_new))):
+                raise ValueError("gqa_paged: the mask must be the sliding-window mask of the cache's window")
+            chunk = w
+        else:
+            if n_old + n_new > 2 * w:
+                raise ValueError("gqa_paged: an unmasked step of more than window_size tokens on a full window")
+            chunk = n_new
+        outs = []
+        dev = x.device
+        for c0 in range(0, n_new, chunk):
+            kc, vc = k[:, :, c0:c0 + chunk], v[:, :, c0:c0 + chunk]
+            qc = q[:, :, c0:c0 + chunk]
+            tc = kc.shape[2]
+            cache._append(layer, kc, vc)
+            skip = cache._skip[layer]
+            total = skip + cache.num_tokens(layer)
+            if mask is not None:
+                rows = torch.arange(total - tc, total, dtype=torch.int32, device=dev)
+                lens = rows + 1
+                starts = torch.clamp(rows - w + 1, min=skip)
+            else:
+                lens = torch.full((tc,), total, dtype=torch.int32, device=dev)
+                starts = torch.full((tc,), skip, dtype=torch.int32, device=dev)
+            qd = qc if qc.dtype == cache.dtype else qc.to(cache.dtype)
+            outs.append(cache.attend(layer, qd, lens, starts, scale=self.head_dim ** -0.5))
+            if mask is not None:
+                cache._trim(layer, w)
+        cache._trim(layer, w)
+        out = torch.cat(outs, dim=2) if len(outs) > 1 else outs[0]
+        out = out.to(x.dtype).transpose(1, 2).reshape(1, n_new, self.n_heads * self.head_dim)
         return self.out_proj(out), None

@@ -62,13 +62,14 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
 
   int len = p.seq_lens[b];
   if (len < 0) len = 0;
+  const int skip = p.seq_start ? max(0, p.seq_start[b]) : 0;  // tokens before the window start
   int n_splits = (len + p.split_tokens - 1) / p.split_tokens;
   if (n_splits > p.max_splits) {
     if (s == 0 && threadIdx.x == 0) flag_error(p.err, SNAPMIND_DEVERR_SPLIT);
     n_splits = p.max_splits;
     len = p.max_splits * p.split_tokens;
   }
-  if (len == 0) {
+  if (len <= skip) {
     // softmax over zero keys: the reference's matmul over an empty dim gives 0
     if (s == 0) {
       for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
@@ -115,7 +116,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
   for (int tile = t0 + warp * kTileTok; tile < t1; tile += kGenericWarps * kTileTok) {
     // ---- scores: lane = token
     const int t = tile + lane;
-    bool valid = t < t1;
+    bool valid = t < t1 && t >= skip;
     int64_t row = 0;
     if (valid) {
       const int j = t / p.block_size;
@@ -323,16 +324,15 @@ int64_t snapmind_paged_gqa_decode_workspace_bytes(int32_t batch, int32_t n_q_hea
   return workspace_layout(batch, n_q_heads, n_kv_heads, head_dim, (int)max_splits).total;
 }
 
-int snapmind_paged_gqa_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
-                              const void* k_pool, const void* v_pool, int dtype,
-                              const int32_t* block_tables, int64_t table_stride_seq,
-                              int32_t table_width, const int32_t* seq_lens, void* out,
-                              int64_t out_stride_seq, int64_t out_stride_head, float scale,
-                              int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
-                              int32_t head_dim, int32_t block_size, int32_t num_blocks,
-                              int32_t max_seq_len, int32_t split_tokens, int32_t flags,
-                              void* workspace, int64_t workspace_bytes, int32_t* err_word,
-                              void* stream) {
+}  // extern "C"
+
+static int decode_entry(const void* q, int64_t q_stride_seq, int64_t q_stride_head, const void* k_pool,
+                        const void* v_pool, int dtype, const int32_t* block_tables, int64_t table_stride_seq,
+                        int32_t table_width, const int32_t* seq_lens, const int32_t* seq_starts, void* out,
+                        int64_t out_stride_seq, int64_t out_stride_head, float scale, int32_t batch,
+                        int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+                        int32_t num_blocks, int32_t max_seq_len, int32_t split_tokens, int32_t flags,
+                        void* workspace, int64_t workspace_bytes, int32_t* err_word, void* stream) {
   SNAPMIND_CHECK_ARG(dtype_size(dtype) > 0, "paged_decode: unknown dtype");
   SNAPMIND_CHECK_ARG(batch >= 0 && n_q_heads > 0 && n_kv_heads > 0 && head_dim > 0 &&
                          head_dim <= 256 && block_size > 0 && num_blocks > 0 && table_width >= 0,
@@ -366,6 +366,7 @@ int snapmind_paged_gqa_decode(const void* q, int64_t q_stride_seq, int64_t q_str
   p.table_stride = table_stride_seq;
   p.table_width = table_width;
   p.seq_lens = seq_lens;
+  p.seq_start = seq_starts;
   p.out = out;
   p.out_stride_seq = out_stride_seq;
   p.out_stride_head = out_stride_head;
@@ -396,6 +397,40 @@ int snapmind_paged_gqa_decode(const void* q, int64_t q_stride_seq, int64_t q_str
     case SNAPMIND_DTYPE_BF16: return launch_generic<__nv_bfloat16>(p, grid, st);
     default: return launch_generic<__half>(p, grid, st);
   }
+}
+
+extern "C" {
+
+int snapmind_paged_gqa_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
+                              const void* k_pool, const void* v_pool, int dtype,
+                              const int32_t* block_tables, int64_t table_stride_seq,
+                              int32_t table_width, const int32_t* seq_lens, void* out,
+                              int64_t out_stride_seq, int64_t out_stride_head, float scale,
+                              int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
+                              int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                              int32_t max_seq_len, int32_t split_tokens, int32_t flags,
+                              void* workspace, int64_t workspace_bytes, int32_t* err_word,
+                              void* stream) {
+  return decode_entry(q, q_stride_seq, q_stride_head, k_pool, v_pool, dtype, block_tables, table_stride_seq,
+                      table_width, seq_lens, nullptr, out, out_stride_seq, out_stride_head, scale, batch,
+                      n_q_heads, n_kv_heads, head_dim, block_size, num_blocks, max_seq_len, split_tokens, flags,
+                      workspace, workspace_bytes, err_word, stream);
+}
+
+int snapmind_paged_gqa_decode_window(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
+                                     const void* k_pool, const void* v_pool, int dtype,
+                                     const int32_t* block_tables, int64_t table_stride_seq,
+                                     int32_t table_width, const int32_t* seq_lens, const int32_t* seq_starts,
+                                     void* out, int64_t out_stride_seq, int64_t out_stride_head, float scale,
+                                     int32_t batch, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
+                                     int32_t block_size, int32_t num_blocks, int32_t max_seq_len,
+                                     int32_t split_tokens, int32_t flags, void* workspace,
+                                     int64_t workspace_bytes, int32_t* err_word, void* stream) {
+  SNAPMIND_CHECK_ARG(seq_starts != nullptr, "paged_decode_window: seq_starts is NULL");
+  return decode_entry(q, q_stride_seq, q_stride_head, k_pool, v_pool, dtype, block_tables, table_stride_seq,
+                      table_width, seq_lens, seq_starts, out, out_stride_seq, out_stride_head, scale, batch,
+                      n_q_heads, n_kv_heads, head_dim, block_size, num_blocks, max_seq_len, split_tokens, flags,
+                      workspace, workspace_bytes, err_word, stream);
 }
 
 }  // extern "C"

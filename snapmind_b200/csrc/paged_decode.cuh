@@ -14,6 +14,7 @@ struct DecodeParams {
   int64_t table_stride;
   int32_t table_width;
   const int32_t* seq_lens;
+  const int32_t* seq_start = nullptr;  // per sequence: first attended token (NULL: 0)
   void* out;
   int64_t out_stride_seq, out_stride_head;  // elements
   float scale;

@@ -170,13 +170,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   int len = p.seq_lens[b];
   if (len < 0) len = 0;
+  const int skip = p.seq_start ? max(0, p.seq_start[b]) : 0;  // tokens before the window start
   int n_splits = (len + p.split_tokens - 1) / p.split_tokens;
   if (n_splits > p.max_splits) {
     if (s == 0 && threadIdx.x == 0) flag_error(p.err, SNAPMIND_DEVERR_SPLIT);
     n_splits = p.max_splits;
     len = p.max_splits * p.split_tokens;
   }
-  if (len == 0) {
+  if (len <= skip) {
     if (s == 0) {
       for (int e = threadIdx.x; e < G * kD; e += blockDim.x) {
         const int g = e / kD, d = e - g * kD;
@@ -294,10 +295,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       const int tile_t0 = t0 + i * kTile;
       const int valid = min(16, t1 - (tile_t0 + 16 * warp));  // keys of this warp in the tile
+      const int lead = skip - (tile_t0 + 16 * warp);          // leading keys before the window start
       uint8_t* stage = ring + st * kStageBytes;
       const uint32_t kbase = smem_u32(stage);
       const uint32_t vbase = smem_u32(stage + 2 * kHalfBytes);
-      const bool loaded = valid > 0 && S.table[(tile_t0 - t0 + 16 * warp) / BS] >= 0;
+      // a warp computes only if one of its keys is attended (keeps every score row finite)
+      const bool loaded = valid > 0 && lead < valid && S.table[(tile_t0 - t0 + 16 * warp) / BS] >= 0;
       if (loaded) {
         if (valid < 16) {
           // zero V rows past the sequence end so that zero weights never meet NaN garbage
@@ -318,8 +321,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           mma16816<T>(sc, a0, a1, a2, a3, qf[k][0], qf[k][1]);
         }
         // keys g and g+8 of this warp's 16; heads 2tig, 2tig+1
-        if (g >= valid) sc[0] = sc[1] = -INFINITY;
-        if (g + 8 >= valid) sc[2] = sc[3] = -INFINITY;
+        if (g >= valid || g < lead) sc[0] = sc[1] = -INFINITY;
+        if (g + 8 >= valid || g + 8 < lead) sc[2] = sc[3] = -INFINITY;
         float mt0 = fmaxf(sc[0], sc[2]), mt1 = fmaxf(sc[1], sc[3]);
 #pragma unroll
         for (int off = 4; off < 32; off <<= 1) {

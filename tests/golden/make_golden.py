@@ -572,6 +572,48 @@ def make_indexer(out_npz: Path, out_json: Path):
     out_json.write_text(json.dumps(meta, indent=1))
 
 
+SLIDING_OPS = [  # (op, layer, tokens or keep, seed)
+    ("store", 0, 5, 401), ("store", 1, 3, 402), ("store", 0, 1, 403), ("store", 0, 9, 404),
+    ("store", 1, 20, 405), ("store", 0, 1, 406), ("evict", None, 0, None), ("store", 1, 1, 407),
+    ("evict", None, 6, None), ("store", 0, 2, 408), ("store", 0, 30, 409), ("store", 1, 12, 410),
+    ("reset", None, None, None), ("store", 0, 4, 411),
+]
+SLIDING_CFG = {"n_layers": 2, "n_heads": 2, "head_dim": 8, "window_size": 12}
+
+
+def sliding_inputs(op, cfg):
+    _, layer, n, seed = op
+    shape = (1, cfg["n_heads"], n, cfg["head_dim"])
+    return randn(seed, shape), randn(seed + 1000, shape)
+
+
+def make_sliding(out: Path):
+    """The reference SlidingWindowKVCache driven by SLIDING_OPS: after each op,
+    the shape and digest of every layer's fetched K and V and memory_usage()."""
+    import torch
+    from snapmind.kv_cache.sliding_window import SlidingWindowKVCache
+
+    cfg = SLIDING_CFG
+    cache = SlidingWindowKVCache(max_seq_len=64, n_layers=cfg["n_layers"], n_heads=cfg["n_heads"],
+                                 head_dim=cfg["head_dim"], window_size=cfg["window_size"])
+    steps = []
+    for op in SLIDING_OPS:
+        kind, layer, n, _ = op
+        if kind == "store":
+            k, v = sliding_inputs(op, cfg)
+            cache.store(layer, torch.from_numpy(k), torch.from_numpy(v), 0)
+        elif kind == "evict":
+            cache.evict(n)
+        else:
+            cache.reset()
+        rec = {"memory_usage": cache.memory_usage(), "layers": []}
+        for i in range(cfg["n_layers"]):
+            k, v = cache.fetch(i)
+            rec["layers"].append({"shape": list(k.shape), "k": digest(k.numpy()), "v": digest(v.numpy())})
+        steps.append(rec)
+    out.write_text(json.dumps({"config": cfg, "steps": steps}, indent=1))
+
+
 E2E_CASES = [
     # (name, shape name, weight seed, prompt seed, prompt length, generated ids, cache sample per layer)
     ("small", "SMALL", 7, 11, 24, 8, None),
@@ -654,14 +696,14 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SNAPMIND_REFERENCE", "/root/reference"))
     ap.add_argument("--only", nargs="*", default=None,
-                    help="fixtures to regenerate: paged, gqa, tiered, mla, indexer, e2e (default: all)")
+                    help="fixtures to regenerate: paged, gqa, tiered, mla, indexer, e2e, sliding (default: all)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     sys.path.insert(0, str(HERE.parent))
     import torch
 
     torch.set_num_threads(4)
-    want = set(args.only) if args.only else {"paged", "gqa", "tiered", "mla", "indexer", "e2e"}
+    want = set(args.only) if args.only else {"paged", "gqa", "tiered", "mla", "indexer", "e2e", "sliding"}
     if "paged" in want:
         make_paged_ops(HERE / "paged_ops.json")
         make_paged_batched(HERE / "paged_batched.json")
@@ -675,6 +717,8 @@ def main():
         make_indexer(HERE / "indexer.npz", HERE / "indexer.json")
     if "e2e" in want:
         make_e2e(HERE / "e2e_llama.npz", HERE / "e2e_llama.json")
+    if "sliding" in want:
+        make_sliding(HERE / "sliding_window.json")
     print("golden vectors written to", HERE)
 
 
