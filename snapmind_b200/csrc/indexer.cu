@@ -486,6 +486,112 @@ __global__ void __launch_bounds__(256) indexer_project_kernel(PoolParams p, cons
   }
 }
 
+// Tensor-core form of the projection for bf16 projection matrices: each fp32
+// mean is split into two bf16 terms (hi = bf16(x), lo = bf16(x - hi): their sum
+// is x to about 2^-18 relative), both multiplied by the bf16 matrix with
+// mma.sync m16n8k16 and accumulated in fp32.  CTA = 64 chunks x 128 outputs,
+// 4 warps of 16 chunks; 32 columns per step, staged in shared memory with
+// 80-byte rows (ldmatrix of 8 consecutive rows hits 8 bank groups), the next
+// step's operands loaded into registers while the current one is multiplied.
+constexpr int kTcItems = 64, kTcOut = 128, kTcK = 32, kTcRow = kTcK + 8;
+
+__device__ __forceinline__ uint32_t idx_smem_u32(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+__device__ __forceinline__ void idx_ldsm4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(a));
+}
+__device__ __forceinline__ void idx_mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(128) indexer_project_tc_kernel(PoolParams p, const float* means, int64_t items) {
+  __shared__ __align__(16) __nv_bfloat16 Ah[kTcItems][kTcRow];
+  __shared__ __align__(16) __nv_bfloat16 Al[kTcItems][kTcRow];
+  __shared__ __align__(16) __nv_bfloat16 Bs[kTcOut][kTcRow];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  const int W = p.width, O = p.out_dim;
+  const int64_t item0 = (int64_t)blockIdx.x * kTcItems;
+  const int o0 = blockIdx.y * kTcOut;
+  const __nv_bfloat16* P = reinterpret_cast<const __nv_bfloat16*>(p.proj);
+  // loaders: A rows of 16 floats (two threads per chunk row), B rows of 32 bf16 (one thread per output)
+  const int a_r = tid >> 1, a_c = (tid & 1) * 16;
+  const int64_t a_item = item0 + a_r;
+  const bool a_ok = a_item < items;
+  const int b_o = o0 + tid;
+  const bool b_ok = b_o < O;
+  const float* a_src = means + (a_ok ? a_item : 0) * W + a_c;
+  const __nv_bfloat16* b_src = P + (int64_t)(b_ok ? b_o : 0) * W;
+  float4 a_reg[4];
+  uint4 b_reg[4];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      a_reg[j] = a_ok ? *reinterpret_cast<const float4*>(a_src + k0 + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      b_reg[j] = b_ok ? *reinterpret_cast<const uint4*>(b_src + k0 + 8 * j) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  float acc[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  const int a_row = (lane & 7) + ((lane >> 3) & 1) * 8, a_kof = (lane >> 4) * 8;
+  const int b_row = (lane & 7) + ((lane >> 4) & 1) * 8, b_kof = ((lane >> 3) & 1) * 8;
+  fetch(0);
+  for (int k0 = 0; k0 < W; k0 += kTcK) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float x[4] = {a_reg[j].x, a_reg[j].y, a_reg[j].z, a_reg[j].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat16 hi = __float2bfloat16_rn(x[e]);
+        Ah[a_r][a_c + 4 * j + e] = hi;
+        Al[a_r][a_c + 4 * j + e] = __float2bfloat16_rn(x[e] - __bfloat162float(hi));
+      }
+      *reinterpret_cast<uint4*>(&Bs[tid][8 * j]) = b_reg[j];
+    }
+    __syncthreads();
+    if (k0 + kTcK < W) fetch(k0 + kTcK);
+#pragma unroll
+    for (int ks = 0; ks < kTcK / 16; ++ks) {
+      uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+      idx_ldsm4(idx_smem_u32(&Ah[16 * warp + a_row][ks * 16 + a_kof]), h0, h1, h2, h3);
+      idx_ldsm4(idx_smem_u32(&Al[16 * warp + a_row][ks * 16 + a_kof]), l0, l1, l2, l3);
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        uint32_t b0, b1, b2, b3;
+        idx_ldsm4(idx_smem_u32(&Bs[16 * np + b_row][ks * 16 + b_kof]), b0, b1, b2, b3);
+        idx_mma_bf16(acc[2 * np], h0, h1, h2, h3, b0, b1);
+        idx_mma_bf16(acc[2 * np], l0, l1, l2, l3, b0, b1);
+        idx_mma_bf16(acc[2 * np + 1], h0, h1, h2, h3, b2, b3);
+        idx_mma_bf16(acc[2 * np + 1], l0, l1, l2, l3, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int64_t item = item0 + 16 * warp + g + 8 * hr;
+    if (item >= items) continue;
+    const int b = (int)(item / p.chunk_count);
+    const int c = p.chunk_begin + (int)(item - (int64_t)b * p.chunk_count);
+    float* out = p.out + ((int64_t)b * p.max_chunks + c) * O;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const int o = o0 + nt * 8 + 2 * tig;
+      if (o < O) out[o] = acc[nt][2 * hr];
+      if (o + 1 < O) out[o + 1] = acc[nt][2 * hr + 1];
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // reference score: one warp per chunk
 // ---------------------------------------------------------------------------
@@ -813,6 +919,13 @@ int snapmind_indexer_pool_chunks(const void* pool, int dtype, int64_t row_width,
              : dtype == SNAPMIND_DTYPE_BF16 ? mean_go(indexer_mean_kernel<__nv_bfloat16>)
                                             : mean_go(indexer_mean_kernel<__half>);
     if (rc != SNAPMIND_OK) return rc;
+    const bool tc = pd == SNAPMIND_DTYPE_BF16 && width % kTcK == 0 && (reinterpret_cast<uintptr_t>(proj) & 15) == 0;
+    if (tc) {
+      dim3 tgrid((unsigned)((items + kTcItems - 1) / kTcItems), (unsigned)((out_dim + kTcOut - 1) / kTcOut));
+      SNAPMIND_CHECK_ARG(tgrid.y <= 65535, "indexer_pool_chunks: out_dim too large");
+      indexer_project_tc_kernel<<<tgrid, 128, 0, st>>>(p, means, items);
+      return cuda_status(cudaGetLastError(), "indexer_project_tc launch");
+    }
     dim3 pgrid((unsigned)((items + kProjTile - 1) / kProjTile), (unsigned)((out_dim + kProjTile - 1) / kProjTile));
     SNAPMIND_CHECK_ARG(pgrid.y <= 65535, "indexer_pool_chunks: out_dim too large");
     auto proj_go = [&](auto kernel) -> int {

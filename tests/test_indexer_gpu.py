@@ -146,7 +146,8 @@ def test_chunk_keys_bulk_two_kernel_path(cuda_device):
             want = wk @ rows[c * bs:(c + 1) * bs].astype(np.float64).mean(axis=0)
             np.testing.assert_allclose(two_np[b, c], want, rtol=1e-4, atol=1e-4)
         assert not two_np[b, n_chunks:].any()
-    np.testing.assert_allclose(two_np, fused_np, rtol=1e-5, atol=1e-6)
+    # the bulk path projects on tensor cores with the means split into two bf16 terms
+    np.testing.assert_allclose(two_np, fused_np, rtol=1e-4, atol=1e-5)
 
 
 @pytest.mark.parametrize("sliced", [False, True])
