@@ -52,7 +52,7 @@ constexpr int generic_smem_floats(int head_dim) {
 }
 
 template <typename T, int NI, int GMAX>
-__global__ void __launch_bounds__(kGenericWarps * 32)
+__global__ void __launch_bounds__(kGenericWarps * 32, (GMAX <= 8 && NI <= 2) ? 2 : 1)
     paged_decode_generic_kernel(DecodeParams p) {
   const int s = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -135,15 +135,24 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
     if (valid) {
       const T* kr = kpool + row;
       if (vec) {
-        for (int d = 0; d < D; d += 4) {
-          const float4 kv = load4_as_f(kr + d);
+        // kKv vector loads per round are issued before any of them is used
+        constexpr int kKv = GMAX >= 32 ? 4 : 8;
+        for (int d0 = 0; d0 < D; d0 += 4 * kKv) {
+          float4 kv[kKv];
 #pragma unroll
-          for (int g = 0; g < GMAX; ++g) {
-            const float4 qv = *reinterpret_cast<const float4*>(q_s + g * DP + d);
-            sc[g] = fmaf(qv.x, kv.x, sc[g]);
-            sc[g] = fmaf(qv.y, kv.y, sc[g]);
-            sc[g] = fmaf(qv.z, kv.z, sc[g]);
-            sc[g] = fmaf(qv.w, kv.w, sc[g]);
+          for (int j = 0; j < kKv; ++j)
+            kv[j] = d0 + 4 * j < D ? load4_as_f(kr + d0 + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int j = 0; j < kKv; ++j) {
+            if (d0 + 4 * j >= D) break;
+#pragma unroll
+            for (int g = 0; g < GMAX; ++g) {
+              const float4 qv = *reinterpret_cast<const float4*>(q_s + g * DP + d0 + 4 * j);
+              sc[g] = fmaf(qv.x, kv[j].x, sc[g]);
+              sc[g] = fmaf(qv.y, kv[j].y, sc[g]);
+              sc[g] = fmaf(qv.z, kv[j].z, sc[g]);
+              sc[g] = fmaf(qv.w, kv[j].w, sc[g]);
+            }
           }
         }
       } else {
@@ -179,7 +188,8 @@ __global__ void __launch_bounds__(kGenericWarps * 32)
     __syncwarp();
     // ---- P V: lane = dims
     const unsigned vmask = __ballot_sync(0xffffffffu, valid);
-#pragma unroll 4
+    constexpr int kPvUnroll = (NI <= 2 && GMAX < 32) ? 8 : 4;  // value rows in flight
+#pragma unroll kPvUnroll
     for (int jt = 0; jt < kTileTok; ++jt) {
       const int64_t rj = __shfl_sync(0xffffffffu, row, jt);
       if (!((vmask >> jt) & 1u)) continue;
