@@ -200,6 +200,12 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
                 "warmup": warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": {"workload": r["workload"]},
                 args.only: r}
+    if args.only == "head_shard":
+        r = run_head_shard(args, dev, dist, world)
+        return {"metric": METRIC, "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": steps,
+                "warmup": warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": {"workload": r["workload"]},
+                "roofline": r["roofline"], "head_shard": r}
     if args.only == "append_gather":
         ag = run_append_gather(args, dev, seed, dist, world)
         return {"metric": METRIC, "value": ag["value"], "unit": ag["unit"], "n_gpus": world, "steps": steps,
@@ -638,6 +644,10 @@ def run_tiered(args, dev, seed, dist, world) -> dict:
     copy_ms = c0.elapsed_time(c1) / 10
     chunk_bytes = pool.chunk_host_bytes
     exposed = max(0.0, (ms_with - ms_without) / steps)
+    # decode attention reads every resident K/V row of every layer once per step
+    resident = float(pool.table_lens.float().sum().item())
+    attn_bytes = resident * TIER_L * 2 * H * D * 2
+    pk = peaks()
     res = {
         "value": round(B * world * steps / (ms_with * 1e-3), 1),
         "unit": "tok/s",
@@ -654,6 +664,16 @@ def run_tiered(args, dev, seed, dist, world) -> dict:
         "copy_ms_per_step_alone": round(copy_ms, 4),
         "overlap": round(1.0 - min(1.0, exposed / copy_ms), 4) if copy_ms > 0 else None,
         "resident_tokens_per_seq": int(pool.table_lens.float().mean().item()),
+        "roofline": {
+            "kernel": "paged_gqa_decode over resident slots (whole step, without re-fetch)",
+            "bound": "hbm",
+            "achieved": round(attn_bytes / (ms_without / steps * 1e-3) / 1e9, 1),
+            "peak": pk["hbm_gbs"],
+            "peak_source": pk["source"],
+            "unit": "GB/s",
+            "frac": round(attn_bytes / (ms_without / steps * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+            "algorithmic_bytes_per_step": int(attn_bytes),
+        },
         "h2d_bytes_measured": int(h2d0),
         "gpu_launches_per_step": 3 + TIER_L,
     }
@@ -939,6 +959,109 @@ def run_append_gather(args, dev, seed, dist, world) -> dict:
     return res
 
 
+def run_head_shard(args, dev, dist, world) -> dict:
+    """KV-head-sharded decode: every rank serves the same batch with H/N kv heads.
+
+    Three timings per layer call over the same shards: the local decode alone,
+    the decode + NCCL all-gather of the head slices (+ reorder), and the decode
+    whose epilogue stores the rows into every rank's buffer over NVLink + the
+    bounded epoch wait.  Whole-job throughput counts each sequence's token once
+    (all ranks serve the same sequences)."""
+    import torch
+
+    from snapmind_b200 import PagedKVPool
+    from snapmind_b200.head_shard import HeadShardedDecode, PeerHeadShardedDecode, head_range, shard_query
+
+    if world < 2 or H % world:
+        raise SystemExit("head_shard needs 2, 4 or 8 ranks")
+    rank = dist.get_rank()
+    seed = 4321  # the same sequences on every rank
+    B = args.batch
+    lens = seeded_lengths(seed, B, *DECODE_CTX)
+    nb, width, tables, free = shuffled_tables(seed, lens, 0)
+    lo, hi = head_range(H, world, rank)
+    pool = PagedKVPool(L, hi - lo, D, nb, max_seqs=B, max_blocks_per_seq=width, block_size=BS,
+                       dtype=torch.bfloat16, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed + rank)
+    pool.k.normal_(generator=g)
+    pool.v.normal_(generator=g)
+    pool.set_state(tables, lens, free)
+    q_all = torch.randn((L, B, HQ, D), device=dev, generator=torch.Generator(device=dev).manual_seed(seed))
+    q_all = q_all.to(torch.bfloat16)
+    out = torch.empty((L, B, HQ, D), device=dev, dtype=torch.bfloat16)
+    local = torch.empty((B, HQ // world, D), device=dev, dtype=torch.bfloat16)
+    max_len = int(lens.max())
+    nccl = HeadShardedDecode(pool, HQ, world, rank)
+    fused = PeerHeadShardedDecode(pool, HQ, world, rank, max_batch=B)
+    steps, warmup = args.steps, max(args.warmup, 3)
+
+    def step_local():
+        for layer in range(L):
+            pool.decode(layer, shard_query(q_all[layer], H, world, rank), out=local, max_seq_len=max_len)
+
+    def step_nccl():
+        for layer in range(L):
+            nccl.decode(layer, q_all[layer], out=out[layer], max_seq_len=max_len)
+
+    def step_fused():
+        for layer in range(L):
+            fused.decode(layer, q_all[layer], out=out[layer], max_seq_len=max_len)
+
+    def timed(fn) -> float:
+        for _ in range(warmup):
+            fn()
+        barrier(dist)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(steps):
+            fn()
+        t1.record()
+        torch.cuda.synchronize()
+        barrier(dist)
+        return reduce_max(dist, t0.elapsed_time(t1) / steps, dev)
+
+    ms_local = timed(step_local)
+    ms_nccl = timed(step_nccl)
+    ref = out.clone()
+    ms_fused = timed(step_fused)
+    fused.check()
+    pool.check()
+    same = bool(torch.equal(out, ref))
+    fused.close()
+    kv_bytes = float(lens.sum()) * (hi - lo) * D * ELEM * 2 * L  # this rank's K/V rows per step
+    pk = peaks()
+    res = {
+        "workload": f"head-sharded decode, {B} seqs x ctx {DECODE_CTX[0]}-{DECODE_CTX[1]}, {L} layers, "
+                    f"Hq {HQ} / H {H} over {world} ranks ({(hi - lo)} kv heads each), D {D}, bf16",
+        "value": round(B * 1e3 / ms_fused, 1),
+        "unit": "tok/s",
+        "ms_per_step": round(ms_fused, 4),
+        "ms_per_step_local_decode_only": round(ms_local, 4),
+        "ms_per_step_nccl_all_gather": round(ms_nccl, 4),
+        "ms_per_step_fused_peer_stores": round(ms_fused, 4),
+        "exposed_exchange_us_per_layer": {
+            "nccl": round((ms_nccl - ms_local) * 1e3 / L, 2),
+            "fused": round((ms_fused - ms_local) * 1e3 / L, 2),
+        },
+        "fused_equals_nccl": same,
+        "exchange_bytes_per_layer_per_rank": B * (HQ // world) * D * ELEM * (world - 1),
+        "roofline": {
+            "kernel": "paged_gqa_decode (peer stores) per rank, whole step",
+            "bound": "hbm",
+            "achieved": round(kv_bytes / (ms_fused * 1e-3) / 1e9, 1),
+            "peak": pk["hbm_gbs"],
+            "peak_source": pk["source"],
+            "unit": "GB/s",
+            "frac": round(kv_bytes / (ms_fused * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+        },
+        "gpu_launches_per_step": {"local": L, "nccl": 3 * L, "fused": 2 * L},
+    }
+    del pool
+    torch.cuda.empty_cache()
+    return res
+
+
 def barrier(dist):
     if dist is not None:
         dist.barrier()
@@ -1107,7 +1230,7 @@ def main():
     ap.add_argument("--batch", type=int, default=DECODE_BATCH, help="decode sequences per GPU")
     ap.add_argument("--ag-batch", type=int, default=AG_BATCH, help="append/gather sequences per GPU")
     ap.add_argument("--layers", type=int, default=L)
-    ap.add_argument("--only", choices=["all", "decode", "append_gather", "tiered", "mla", "e2e_llama"], default="all")
+    ap.add_argument("--only", choices=["all", "decode", "append_gather", "tiered", "mla", "e2e_llama", "head_shard"], default="all")
     ap.add_argument("--tiered-batch", type=int, default=TIER_B)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup

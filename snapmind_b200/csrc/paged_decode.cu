@@ -74,10 +74,9 @@ __global__ void __launch_bounds__(kGenericWarps * 32, (GMAX <= 8 && NI <= 2) ? 2
     if (s == 0) {
       for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
         const int g = e / D, d = e - g * D;
-        T* o = reinterpret_cast<T*>(p.out) + (int64_t)b * p.out_stride_seq +
-               (int64_t)(kvh * G + g) * p.out_stride_head;
-        o[d] = Conv<T>::from_f(0.f);
+        store_out<T>(p, b, kvh * G + g, d, 0.f);
       }
+      output_done(p);
     }
     return;
   }
@@ -249,9 +248,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32, (GMAX <= 8 && NI <= 2) ? 2
       A += sm_acc[(w * GMAX + g) * D + d] * f;
     }
     if (direct) {
-      T* o = reinterpret_cast<T*>(p.out) + (int64_t)b * p.out_stride_seq +
-             (int64_t)(kvh * G + g) * p.out_stride_head;
-      o[d] = Conv<T>::from_f(A / L);
+      store_out<T>(p, b, kvh * G + g, d, A / L);
     } else {
       float* part = part_base + ((int64_t)g * p.max_splits + s) * (D + 2);
       part[2 + d] = A;
@@ -261,7 +258,10 @@ __global__ void __launch_bounds__(kGenericWarps * 32, (GMAX <= 8 && NI <= 2) ? 2
       }
     }
   }
-  if (direct) return;
+  if (direct) {
+    output_done(p);
+    return;
+  }
 
   // ---- last-ticket merge of the split partials --------------------------------
   __threadfence();
@@ -275,6 +275,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32, (GMAX <= 8 && NI <= 2) ? 2
   __threadfence();
   combine_splits<T>(p, b, kvh, n_splits, sm);
   if (threadIdx.x == 0) p.counters[b * p.n_kv_heads + kvh] = 0;
+  output_done(p);
 }
 
 template <typename T, int NI>
@@ -342,7 +343,8 @@ static int decode_entry(const void* q, int64_t q_stride_seq, int64_t q_stride_he
                         int64_t out_stride_seq, int64_t out_stride_head, float scale, int32_t batch,
                         int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
                         int32_t num_blocks, int32_t max_seq_len, int32_t split_tokens, int32_t flags,
-                        void* workspace, int64_t workspace_bytes, int32_t* err_word, void* stream) {
+                        void* workspace, int64_t workspace_bytes, int32_t* err_word, void* stream,
+                        const PeerArgs* peers = nullptr) {
   SNAPMIND_CHECK_ARG(dtype_size(dtype) > 0, "paged_decode: unknown dtype");
   SNAPMIND_CHECK_ARG(batch >= 0 && n_q_heads > 0 && n_kv_heads > 0 && head_dim > 0 &&
                          head_dim <= 256 && block_size > 0 && num_blocks > 0 && table_width >= 0,
@@ -350,8 +352,14 @@ static int decode_entry(const void* q, int64_t q_stride_seq, int64_t q_stride_he
   SNAPMIND_CHECK_ARG(n_q_heads % n_kv_heads == 0,
                      "paged_decode: n_q_heads (%d) must be a multiple of n_kv_heads (%d)",
                      n_q_heads, n_kv_heads);
+  if (peers) {
+    SNAPMIND_CHECK_ARG(batch > 0, "paged_decode_peers: batch must be positive (every rank signals)");
+    SNAPMIND_CHECK_ARG(peers->out && peers->flags && peers->n >= 1 && peers->rank >= 0 &&
+                           peers->rank < peers->n && peers->epoch > 0 && peers->head_offset >= 0,
+                       "paged_decode_peers: bad peer arguments");
+  }
   if (batch == 0) return SNAPMIND_OK;
-  SNAPMIND_CHECK_ARG(q && k_pool && v_pool && block_tables && seq_lens && out,
+  SNAPMIND_CHECK_ARG(q && k_pool && v_pool && block_tables && seq_lens && (out || peers),
                      "paged_decode: null pointer");
   if (max_seq_len <= 0) max_seq_len = table_width * block_size;
   if (split_tokens <= 0)
@@ -393,6 +401,16 @@ static int decode_entry(const void* q, int64_t q_stride_seq, int64_t q_stride_he
   p.counters = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + ws.counters_off);
   p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + ws.partials_off);
   p.err = err_word;
+  if (peers) {
+    p.peer_out = peers->out;
+    p.n_peers = peers->n;
+    p.head_offset = peers->head_offset;
+    p.peer_flags = peers->flags;
+    p.rank = peers->rank;
+    p.epoch = peers->epoch;
+    p.done_counter = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + ws.done_off);
+    p.done_target = batch * n_kv_heads;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   if (!(flags & SNAPMIND_DECODE_FORCE_GENERIC)) {
@@ -441,6 +459,24 @@ int snapmind_paged_gqa_decode_window(const void* q, int64_t q_stride_seq, int64_
                       table_width, seq_lens, seq_starts, out, out_stride_seq, out_stride_head, scale, batch,
                       n_q_heads, n_kv_heads, head_dim, block_size, num_blocks, max_seq_len, split_tokens, flags,
                       workspace, workspace_bytes, err_word, stream);
+}
+
+
+int snapmind_paged_gqa_decode_peers(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
+                                    const void* k_pool, const void* v_pool, int dtype,
+                                    const int32_t* block_tables, int64_t table_stride_seq, int32_t table_width,
+                                    const int32_t* seq_lens, const int32_t* seq_starts, void* const* peer_out,
+                                    int32_t n_peers, int32_t head_offset, int64_t out_stride_seq,
+                                    int64_t out_stride_head, int32_t* const* peer_flags, int32_t rank,
+                                    int32_t epoch, float scale, int32_t batch, int32_t n_q_heads,
+                                    int32_t n_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                                    int32_t max_seq_len, int32_t split_tokens, int32_t flags, void* workspace,
+                                    int64_t workspace_bytes, int32_t* err_word, void* stream) {
+  const PeerArgs peers{peer_out, n_peers, head_offset, peer_flags, rank, epoch};
+  return decode_entry(q, q_stride_seq, q_stride_head, k_pool, v_pool, dtype, block_tables, table_stride_seq,
+                      table_width, seq_lens, seq_starts, nullptr, out_stride_seq, out_stride_head, scale, batch,
+                      n_q_heads, n_kv_heads, head_dim, block_size, num_blocks, max_seq_len, split_tokens, flags,
+                      workspace, workspace_bytes, err_word, stream, &peers);
 }
 
 }  // extern "C"

@@ -181,10 +181,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (s == 0) {
       for (int e = threadIdx.x; e < G * kD; e += blockDim.x) {
         const int g = e / kD, d = e - g * kD;
-        T* o = reinterpret_cast<T*>(p.out) + (int64_t)b * p.out_stride_seq +
-               (int64_t)(kvh * G + g) * p.out_stride_head;
-        o[d] = Conv<T>::from_f(0.f);
+        store_out<T>(p, b, kvh * G + g, d, 0.f);
       }
+      output_done(p);
     }
     return;
   }
@@ -430,9 +429,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       A += mo[(w * 8 + h) * kD + d] * f;
     }
     if (direct) {
-      T* out = reinterpret_cast<T*>(p.out) + (int64_t)b * p.out_stride_seq +
-               (int64_t)(kvh * G + h) * p.out_stride_head;
-      out[d] = Conv<T>::from_f(A / L);
+      store_out<T>(p, b, kvh * G + h, d, A / L);
     } else {
       float* part = part_base + ((int64_t)h * p.max_splits + s) * (kD + 2);
       part[2 + d] = A;
@@ -442,7 +439,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
   }
-  if (direct) return;
+  if (direct) {
+    output_done(p);
+    return;
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -454,6 +454,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __threadfence();
   combine_splits<T>(p, b, kvh, n_splits, mo);
   if (threadIdx.x == 0) p.counters[b * p.n_kv_heads + kvh] = 0;
+  output_done(p);
 }
 
 // ---------------------------------------------------------------------------

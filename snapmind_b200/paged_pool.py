@@ -128,15 +128,19 @@ class PagedKVPool(BlockPool):
 
     def decode(self, layer: int, q: torch.Tensor, out: torch.Tensor | None = None, scale: float | None = None,
                batch: int | None = None, split_tokens: int = 0, force_generic: bool = False,
-               max_seq_len: int | None = None) -> torch.Tensor:
-        """Paged GQA decode attention of ``q`` ``[B, Hq, D]`` against layer ``layer``."""
+               max_seq_len: int | None = None, peers=None) -> torch.Tensor | None:
+        """Paged GQA decode attention of ``q`` ``[B, Hq, D]`` against layer ``layer``.
+
+        ``peers`` (a ``head_shard.PeerTargets``) sends the output rows to the
+        output buffers of every rank of a head-sharded decode instead of ``out``
+        and returns None."""
         batch = q.shape[0] if batch is None else batch
         n_q = q.shape[1]
         if q.dtype != self.dtype:
             raise TypeError(f"q dtype {q.dtype} != pool dtype {self.dtype}")
         if q.stride(-1) != 1:
             q = q.contiguous()
-        if out is None:
+        if out is None and peers is None:
             out = torch.empty((batch, n_q, self.head_dim), dtype=self.dtype, device=self.device)
         scale = self.head_dim ** -0.5 if scale is None else scale
         if max_seq_len is None:
@@ -147,6 +151,20 @@ class PagedKVPool(BlockPool):
             batch, self.n_kv_heads, max_len, self.block_size
         )
         ws = self._decode_workspace(batch, n_q, max_len, split)
+        if peers is not None:
+            status = lib.snapmind_paged_gqa_decode_peers(
+                q.data_ptr(), q.stride(0), q.stride(1),
+                self.k[layer].data_ptr(), self.v[layer].data_ptr(), self._dcode,
+                self.block_tables.data_ptr(), self.max_blocks_per_seq, self.max_blocks_per_seq,
+                self.seq_lens.data_ptr(), None,
+                peers.out_ptrs.data_ptr(), peers.n, peers.head_offset, peers.out_stride_seq, peers.out_stride_head,
+                peers.flag_ptrs.data_ptr(), peers.rank, peers.epoch,
+                float(scale), batch, n_q, self.n_kv_heads, self.head_dim, self.block_size, self.num_blocks,
+                max_len, split, _lib.DECODE_FORCE_GENERIC if force_generic else 0,
+                ws.data_ptr(), ws.numel(), self.err.data_ptr(), self._stream(),
+            )  # fmt: skip
+            _lib.check(status, "PagedKVPool.decode (peers)")
+            return None
         status = lib.snapmind_paged_gqa_decode(
             q.data_ptr(), q.stride(0), q.stride(1),
             self.k[layer].data_ptr(), self.v[layer].data_ptr(), self._dcode,

@@ -1,4 +1,6 @@
-"""KV-head-sharded paged decode on 2 GPUs over NCCL (skipped with fewer GPUs)."""
+"""KV-head-sharded paged decode on 2 GPUs (skipped with fewer GPUs): the NCCL
+all-gather version, and the version whose decode kernel stores the rows into
+every rank's buffer over NVLink (CUDA IPC peer mappings, no multicast)."""
 import os
 import socket
 
@@ -24,7 +26,7 @@ def _worker(rank, world, port, results):
 
     from oracle import bf16, gqa
     from snapmind_b200 import PagedKVPool
-    from snapmind_b200.head_shard import HeadShardedDecode, head_range
+    from snapmind_b200.head_shard import HeadShardedDecode, PeerHeadShardedDecode, head_range
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -61,7 +63,20 @@ def _worker(rank, world, port, results):
         pool.check()
         want = np.stack([gqa.gqa_attention(q[b][None, :, None], k[b][None, :, : lens[b]], v[b][None, :, : lens[b]],
                                            D ** -0.5)[0, :, 0] for b in range(B)])
-        results[rank] = float(np.abs(out.float().cpu().numpy() - want).max())
+        err = float(np.abs(out.float().cpu().numpy() - want).max())
+        # the fused version: several epochs (both receive buffers), each equal to the NCCL version
+        pdec = PeerHeadShardedDecode(pool, Hq, world, rank)
+        same = True
+        for _ in range(5):
+            qe = torch.from_numpy(bf16.round_to_bf16(rng.standard_normal((B, Hq, D)).astype(np.float32)))
+            qe = qe.cuda().to(torch.bfloat16)
+            ref = dec.decode(0, qe)
+            got = pdec.decode(0, qe).clone()
+            torch.cuda.synchronize()
+            pdec.check()
+            same = same and bool(torch.equal(got, ref))
+        pdec.close()
+        results[rank] = (err, same)
     finally:
         dist.destroy_process_group()
 
@@ -73,4 +88,5 @@ def test_head_sharded_decode_two_gpus(cuda_device):
 
     results = mp.Manager().dict()
     mp.spawn(_worker, args=(2, _free_port(), results), nprocs=2, join=True)
-    assert results[0] < 2e-2 and results[1] < 2e-2, dict(results)
+    assert results[0][0] < 2e-2 and results[1][0] < 2e-2, dict(results)
+    assert results[0][1] and results[1][1], dict(results)
