@@ -376,18 +376,16 @@ SNAPMIND_API int snapmind_paged_gqa_decode_window(const void *q, int64_t q_strid
  * holds kv heads [head_offset / group, ...) of every sequence and its query
  * heads start at global head `head_offset`.  Instead of one local output, the
  * kernel stores every finished output row into the output buffer of each of
- * the n_peers ranks (peer_out: device array of n_peers device pointers, in
- * rank order, this rank's own buffer included; peers are reached by plain
- * NVLink stores through CUDA IPC mappings), at the global head offset, with
- * out_stride_seq / out_stride_head of the full [batch][heads][head_dim]
- * buffer.  When all of its outputs are stored, the call writes `epoch` (> 0,
- * growing from call to call) into element `rank` of every rank's flag array
- * (peer_flags: device array of n_peers pointers to int32[n_peers]).
- * snapmind_peer_wait then waits for all ranks.  seq_starts may be NULL (whole
- * sequences) or as in snapmind_paged_gqa_decode_window.  batch must be
- * positive.  The workspace is that of snapmind_paged_gqa_decode; it also holds
- * the call's counter of finished outputs.  No reference counterpart: snapmind
- * runs on one device; this replaces the all-gather of the per-rank head slices.
+ * the n_peers ranks (peer_out: device array of n_peers 16-byte-aligned device
+ * pointers, in rank order, this rank's own buffer included; peers are reached
+ * by plain 16-byte NVLink stores through CUDA IPC mappings), at the global
+ * head offset, with out_stride_seq / out_stride_head of the full
+ * [batch][heads][head_dim] buffer (head_dim and both strides multiples of 16
+ * bytes).  seq_starts may be NULL (whole sequences) or as in
+ * snapmind_paged_gqa_decode_window.  The workspace is that of
+ * snapmind_paged_gqa_decode.  Follow it on the same stream with
+ * snapmind_peer_sync (SIGNAL | WAIT).  No reference counterpart: snapmind runs
+ * on one device; this replaces the all-gather of the per-rank head slices.
  */
 SNAPMIND_API int snapmind_paged_gqa_decode_peers(const void *q, int64_t q_stride_seq, int64_t q_stride_head,
                                                 const void *k_pool, const void *v_pool, int dtype,
@@ -395,21 +393,26 @@ SNAPMIND_API int snapmind_paged_gqa_decode_peers(const void *q, int64_t q_stride
                                                 int32_t table_width, const int32_t *seq_lens,
                                                 const int32_t *seq_starts, void *const *peer_out,
                                                 int32_t n_peers, int32_t head_offset, int64_t out_stride_seq,
-                                                int64_t out_stride_head, int32_t *const *peer_flags,
-                                                int32_t rank, int32_t epoch, float scale, int32_t batch,
+                                                int64_t out_stride_head, float scale, int32_t batch,
                                                 int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
                                                 int32_t block_size, int32_t num_blocks, int32_t max_seq_len,
                                                 int32_t split_tokens, int32_t flags, void *workspace,
                                                 int64_t workspace_bytes, int32_t *err_word, void *stream);
 
 /*
- * Enqueue on `stream` a wait until flags[r] >= epoch for every r < n_peers
- * (this rank's own flag array, written by the ranks' decode calls).  The wait
- * gives up after 2 s and then ORs SNAPMIND_DEVERR_TIMEOUT into *err_word.
- * Work enqueued after it on the stream sees every rank's output rows.
+ * One warp on `stream`.  SNAPMIND_PEER_SIGNAL: after a system-scope fence
+ * (the peer stores of the work before it on the stream are complete), write
+ * `epoch` (> 0, growing from call to call) into element `rank` of every rank's
+ * flag array (peer_flags: device array of n_peers pointers to int32[n_peers]).
+ * SNAPMIND_PEER_WAIT: wait until flags[r] >= epoch for every r < n_peers
+ * (this rank's own flag array); the wait gives up after 2 s and then ORs
+ * SNAPMIND_DEVERR_TIMEOUT into *err_word.  Work enqueued after it on the
+ * stream sees every rank's output rows.
  */
-SNAPMIND_API int snapmind_peer_wait(const int32_t *flags, int32_t n_peers, int32_t epoch, int32_t *err_word,
-                                    void *stream);
+#define SNAPMIND_PEER_SIGNAL 1
+#define SNAPMIND_PEER_WAIT 2
+SNAPMIND_API int snapmind_peer_sync(int32_t *const *peer_flags, const int32_t *flags, int32_t n_peers,
+                                    int32_t rank, int32_t epoch, int32_t what, int32_t *err_word, void *stream);
 
 /*
  * CUDA IPC for the peer buffers.  snapmind_ipc_export writes the

@@ -113,10 +113,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "snapmind_paged_gqa_decode_peers": (
         _int,
-        [_p, _i64, _i64, _p, _p, _int, _p, _i64, _i32, _p, _p, _p, _i32, _i32, _i64, _i64, _p, _i32, _i32,
+        [_p, _i64, _i64, _p, _p, _int, _p, _i64, _i32, _p, _p, _p, _i32, _i32, _i64, _i64,
          _f32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _p, _i64, _p, _p],
     ),
-    "snapmind_peer_wait": (_int, [_p, _i32, _i32, _p, _p]),
+    "snapmind_peer_sync": (_int, [_p, _p, _i32, _i32, _i32, _i32, _p, _p]),
     "snapmind_ipc_export": (_int, [_p, _p, ctypes.POINTER(_i64)]),
     "snapmind_ipc_open": (_int, [_p, _i64, ctypes.POINTER(_p)]),
     "snapmind_ipc_close": (_int, [_p, _i64]),
@@ -129,6 +129,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
 
 NOALLOC_DECODE_SCRATCH_BYTES = 16 << 20
 IPC_HANDLE_BYTES = 64
+PEER_SIGNAL = 1
+PEER_WAIT = 2
 
 _lib: ctypes.CDLL | None = None
 

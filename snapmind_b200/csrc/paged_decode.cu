@@ -72,11 +72,14 @@ __global__ void __launch_bounds__(kGenericWarps * 32, (GMAX <= 8 && NI <= 2) ? 2
   if (len <= skip) {
     // softmax over zero keys: the reference's matmul over an empty dim gives 0
     if (s == 0) {
-      for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
-        const int g = e / D, d = e - g * D;
-        store_out<T>(p, b, kvh * G + g, d, 0.f);
+      if (p.n_peers > 0) {
+        emit_peer_rows<T>(p, b, kvh * G, G, D, [](int, int) { return 0.f; });
+      } else {
+        for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+          const int g = e / D, d = e - g * D;
+          store_out<T>(p, b, kvh * G + g, d, 0.f);
+        }
       }
-      output_done(p);
     }
     return;
   }
@@ -233,6 +236,23 @@ __global__ void __launch_bounds__(kGenericWarps * 32, (GMAX <= 8 && NI <= 2) ? 2
   __syncthreads();
 
   const bool direct = (n_splits == 1);
+  if (direct && p.n_peers > 0) {
+    emit_peer_rows<T>(p, b, kvh * G, G, D, [&](int g, int d) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kGenericWarps; ++w) M = fmaxf(M, sm_m[w * GMAX + g]);
+      float L = 0.f, A = 0.f;
+#pragma unroll
+      for (int w = 0; w < kGenericWarps; ++w) {
+        const float mw = sm_m[w * GMAX + g];
+        const float f = (mw == -INFINITY) ? 0.f : expf(mw - M);
+        L += sm_l[w * GMAX + g] * f;
+        A += sm_acc[(w * GMAX + g) * D + d] * f;
+      }
+      return A / L;
+    });
+    return;
+  }
   float* part_base = p.partials + ((int64_t)b * p.n_q_heads + kvh * G) * p.max_splits * (D + 2);
   for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
     const int g = e / D, d = e - g * D;
@@ -258,10 +278,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32, (GMAX <= 8 && NI <= 2) ? 2
       }
     }
   }
-  if (direct) {
-    output_done(p);
-    return;
-  }
+  if (direct) return;
 
   // ---- last-ticket merge of the split partials --------------------------------
   __threadfence();
@@ -275,7 +292,6 @@ __global__ void __launch_bounds__(kGenericWarps * 32, (GMAX <= 8 && NI <= 2) ? 2
   __threadfence();
   combine_splits<T>(p, b, kvh, n_splits, sm);
   if (threadIdx.x == 0) p.counters[b * p.n_kv_heads + kvh] = 0;
-  output_done(p);
 }
 
 template <typename T, int NI>
@@ -353,10 +369,11 @@ static int decode_entry(const void* q, int64_t q_stride_seq, int64_t q_stride_he
                      "paged_decode: n_q_heads (%d) must be a multiple of n_kv_heads (%d)",
                      n_q_heads, n_kv_heads);
   if (peers) {
-    SNAPMIND_CHECK_ARG(batch > 0, "paged_decode_peers: batch must be positive (every rank signals)");
-    SNAPMIND_CHECK_ARG(peers->out && peers->flags && peers->n >= 1 && peers->rank >= 0 &&
-                           peers->rank < peers->n && peers->epoch > 0 && peers->head_offset >= 0,
+    const int vec = 16 / dtype_size(dtype);  // elements per 16-byte peer store
+    SNAPMIND_CHECK_ARG(peers->out && peers->n >= 1 && peers->head_offset >= 0,
                        "paged_decode_peers: bad peer arguments");
+    SNAPMIND_CHECK_ARG(head_dim % vec == 0 && out_stride_seq % vec == 0 && out_stride_head % vec == 0,
+                       "paged_decode_peers: head_dim and output strides must be multiples of 16 bytes");
   }
   if (batch == 0) return SNAPMIND_OK;
   SNAPMIND_CHECK_ARG(q && k_pool && v_pool && block_tables && seq_lens && (out || peers),
@@ -405,11 +422,6 @@ static int decode_entry(const void* q, int64_t q_stride_seq, int64_t q_stride_he
     p.peer_out = peers->out;
     p.n_peers = peers->n;
     p.head_offset = peers->head_offset;
-    p.peer_flags = peers->flags;
-    p.rank = peers->rank;
-    p.epoch = peers->epoch;
-    p.done_counter = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + ws.done_off);
-    p.done_target = batch * n_kv_heads;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
@@ -467,12 +479,11 @@ int snapmind_paged_gqa_decode_peers(const void* q, int64_t q_stride_seq, int64_t
                                     const int32_t* block_tables, int64_t table_stride_seq, int32_t table_width,
                                     const int32_t* seq_lens, const int32_t* seq_starts, void* const* peer_out,
                                     int32_t n_peers, int32_t head_offset, int64_t out_stride_seq,
-                                    int64_t out_stride_head, int32_t* const* peer_flags, int32_t rank,
-                                    int32_t epoch, float scale, int32_t batch, int32_t n_q_heads,
+                                    int64_t out_stride_head, float scale, int32_t batch, int32_t n_q_heads,
                                     int32_t n_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
                                     int32_t max_seq_len, int32_t split_tokens, int32_t flags, void* workspace,
                                     int64_t workspace_bytes, int32_t* err_word, void* stream) {
-  const PeerArgs peers{peer_out, n_peers, head_offset, peer_flags, rank, epoch};
+  const PeerArgs peers{peer_out, n_peers, head_offset};
   return decode_entry(q, q_stride_seq, q_stride_head, k_pool, v_pool, dtype, block_tables, table_stride_seq,
                       table_width, seq_lens, seq_starts, nullptr, out_stride_seq, out_stride_head, scale, batch,
                       n_q_heads, n_kv_heads, head_dim, block_size, num_blocks, max_seq_len, split_tokens, flags,

@@ -27,65 +27,58 @@ struct DecodeParams {
   // n_peers = 0: the local `out` only
   void* const* peer_out = nullptr;       // [n_peers] output bases, rank order (own buffer included)
   int32_t n_peers = 0, head_offset = 0;  // q heads of this launch start at head_offset globally
-  int32_t* const* peer_flags = nullptr;  // [n_peers] flag arrays; flags[r] = last epoch rank r finished
-  int32_t rank = 0, epoch = 0;
-  int32_t* done_counter = nullptr;       // zero between calls
-  int32_t done_target = 0;               // output events per call: batch x n_kv_heads
 };
 
 // Destinations of a decode whose outputs go straight to several GPUs.
 struct PeerArgs {
-  void* const* out;      // device array [n]: output base on each rank
+  void* const* out;  // device array [n]: output base on each rank (16-byte aligned)
   int32_t n, head_offset;
-  int32_t* const* flags;  // device array [n]: flag array on each rank
-  int32_t rank, epoch;
 };
 
-// One output element of (sequence b, q head `head` of this launch): to `out`,
-// or to every GPU's output buffer at the global head.
+// One output element of (sequence b, q head `head` of this launch) to `out`.
 template <typename T>
 __device__ __forceinline__ void store_out(const DecodeParams& p, int b, int head, int d, float v) {
-  const T x = Conv<T>::from_f(v);
-  const int64_t off = (int64_t)b * p.out_stride_seq + d;
-  if (p.n_peers == 0) {
-    reinterpret_cast<T*>(p.out)[off + (int64_t)head * p.out_stride_head] = x;
-    return;
-  }
-  const int64_t hoff = (int64_t)(head + p.head_offset) * p.out_stride_head;
-  for (int r = 0; r < p.n_peers; ++r) reinterpret_cast<T*>(p.peer_out[r])[off + hoff] = x;
+  reinterpret_cast<T*>(p.out)[(int64_t)b * p.out_stride_seq + (int64_t)head * p.out_stride_head + d] =
+      Conv<T>::from_f(v);
 }
 
-__device__ __forceinline__ void st_release_sys(int32_t* ptr, int32_t v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
-}
+__device__ __forceinline__ uint32_t bits16(__nv_bfloat16 x) { return __bfloat16_as_ushort(x); }
+__device__ __forceinline__ uint32_t bits16(__half x) { return __half_as_ushort(x); }
 
-// Called by every thread of a CTA after its output writes for one (sequence,
-// kv head); the last of the call's done_target events publishes the epoch to
-// every GPU's flag array (after a system-scope fence).
-__device__ __forceinline__ void output_done(const DecodeParams& p) {
-  if (p.n_peers == 0) return;
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int t = atomicAdd(p.done_counter, 1);
-    if (t == p.done_target - 1) {
-      *p.done_counter = 0;
-      __threadfence_system();
-      for (int r = 0; r < p.n_peers; ++r) st_release_sys(p.peer_flags[r] + p.rank, p.epoch);
+// The output rows of heads [head0, head0 + G) of sequence b, value(g, d) each,
+// stored into every GPU's output buffer at the global head: 16-byte stores
+// (whole vectors cross NVLink), every peer in turn.  head_dim and the output
+// strides are multiples of 16 bytes (checked by the host).
+template <typename T, typename F>
+__device__ __forceinline__ void emit_peer_rows(const DecodeParams& p, int b, int head0, int G, int D, F value) {
+  constexpr int V = 16 / sizeof(T);
+  const int per_row = D / V;
+  for (int e = threadIdx.x; e < G * per_row; e += blockDim.x) {
+    const int g = e / per_row, d0 = (e - g * per_row) * V;
+    uint32_t w[4];
+    if constexpr (sizeof(T) == 4) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) w[j] = __float_as_uint(value(g, d0 + j));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        w[j] = bits16(Conv<T>::from_f(value(g, d0 + 2 * j))) | (bits16(Conv<T>::from_f(value(g, d0 + 2 * j + 1))) << 16);
     }
+    const uint4 v = make_uint4(w[0], w[1], w[2], w[3]);
+    const int64_t off = (int64_t)b * p.out_stride_seq + (int64_t)(head0 + g + p.head_offset) * p.out_stride_head + d0;
+    for (int r = 0; r < p.n_peers; ++r) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.peer_out[r]) + off) = v;
   }
 }
 
 struct WorkspaceLayout {
-  int64_t counters_off, done_off, partials_off, total;
+  int64_t counters_off, partials_off, total;
 };
 
 inline WorkspaceLayout workspace_layout(int batch, int n_q_heads, int n_kv_heads, int head_dim,
                                         int max_splits) {
   WorkspaceLayout w;
   w.counters_off = 0;
-  w.done_off = (int64_t)batch * n_kv_heads * sizeof(int32_t);  // one counter of finished outputs
-  const int64_t counters = w.done_off + (int64_t)sizeof(int32_t);
+  const int64_t counters = (int64_t)batch * n_kv_heads * sizeof(int32_t);
   w.partials_off = (counters + 255) / 256 * 256;
   w.total = w.partials_off +
             (int64_t)batch * n_q_heads * max_splits * (head_dim + 2) * (int64_t)sizeof(float);
@@ -146,14 +139,21 @@ __device__ void combine_splits(const DecodeParams& p, int b, int kvh, int n_spli
     }
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
-    const int g = e / D, d = e - g * D;
+  auto value = [&](int g, int d) {
     const float* pg = base + (int64_t)g * p.max_splits * pstride;
     const float M = s_M[g];
     float A = 0.f;
     for (int s = 0; s < n_splits; ++s)
       A += __ldcg(pg + s * pstride + 2 + d) * expf(__ldcg(pg + s * pstride) - M);
-    store_out<T>(p, b, kvh * G + g, d, A / s_L[g]);
+    return A / s_L[g];
+  };
+  if (p.n_peers > 0) {
+    emit_peer_rows<T>(p, b, kvh * G, G, D, value);
+    return;
+  }
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int g = e / D, d = e - g * D;
+    store_out<T>(p, b, kvh * G + g, d, value(g, d));
   }
 }
 

@@ -179,11 +179,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   if (len <= skip) {
     if (s == 0) {
-      for (int e = threadIdx.x; e < G * kD; e += blockDim.x) {
-        const int g = e / kD, d = e - g * kD;
-        store_out<T>(p, b, kvh * G + g, d, 0.f);
+      if (p.n_peers > 0) {
+        emit_peer_rows<T>(p, b, kvh * G, G, kD, [](int, int) { return 0.f; });
+      } else {
+        for (int e = threadIdx.x; e < G * kD; e += blockDim.x) {
+          const int g = e / kD, d = e - g * kD;
+          store_out<T>(p, b, kvh * G + g, d, 0.f);
+        }
       }
-      output_done(p);
     }
     return;
   }
@@ -414,6 +417,23 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   // ---- merge the 4 consumer warps
   const bool direct = (n_splits == 1);
+  if (direct && p.n_peers > 0) {
+    emit_peer_rows<T>(p, b, kvh * G, G, kD, [&](int h, int d) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, mm[w * 8 + h]);
+      float L = 0.f, A = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumers; ++w) {
+        const float mw = mm[w * 8 + h];
+        const float f = (mw == -INFINITY) ? 0.f : expf(mw - M);
+        L += ml[w * 8 + h] * f;
+        A += mo[(w * 8 + h) * kD + d] * f;
+      }
+      return A / L;
+    });
+    return;
+  }
   float* part_base = p.partials + ((int64_t)b * p.n_q_heads + kvh * G) * p.max_splits * (kD + 2);
   for (int e = threadIdx.x; e < G * kD; e += blockDim.x) {
     const int h = e / kD, d = e - h * kD;
@@ -439,10 +459,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
   }
-  if (direct) {
-    output_done(p);
-    return;
-  }
+  if (direct) return;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -454,7 +471,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   __threadfence();
   combine_splits<T>(p, b, kvh, n_splits, mo);
   if (threadIdx.x == 0) p.counters[b * p.n_kv_heads + kvh] = 0;
-  output_done(p);
 }
 
 // ---------------------------------------------------------------------------

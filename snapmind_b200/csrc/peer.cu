@@ -1,11 +1,12 @@
 // Peer memory for the KV-head-sharded decode: the decode kernel of every rank
 // stores its finished output rows straight into every rank's output buffer
-// (NVLink peer stores through CUDA IPC mappings) and publishes an epoch into
-// every rank's flag array; a one-warp kernel then waits, bounded, until every
-// rank's epoch has arrived.  No reference counterpart: snapmind runs on one
-// device.  This replaces an all-gather of the per-rank head slices.
+// (NVLink peer stores through CUDA IPC mappings).  After it, on the same
+// stream, one warp publishes the call's epoch into every rank's flag array and
+// waits, bounded, until every rank's epoch has arrived.  No reference
+// counterpart: snapmind runs on one device.  This replaces an all-gather of the
+// per-rank head slices.
 //
-// Only plain loads and stores reach peer memory: no multicast, no TMA.
+// Only plain loads and stores reach peer memory; no TMA touches it.
 #include <cuda.h>
 #include <string.h>
 
@@ -31,9 +32,22 @@ __device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* ptr) {
   return v;
 }
 
-// Lane r waits for flags[r] to reach `epoch` (epochs only grow; the signed
-// difference tolerates wrap-around).
-__global__ void peer_wait_kernel(const int32_t* flags, int n, int32_t epoch, int32_t* err) {
+__device__ __forceinline__ void st_release_sys(int32_t* ptr, int32_t v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+// SIGNAL: lane r writes `epoch` into element `rank` of rank r's flag array.
+// The decode before this kernel on the stream has completed; the system-scope
+// fence orders its peer stores before the flags.  WAIT: lane r waits for
+// flags[r] to reach `epoch` (epochs only grow; the signed difference tolerates
+// wrap-around).
+__global__ void peer_sync_kernel(int32_t* const* peer_flags, const int32_t* flags, int n, int rank, int32_t epoch,
+                                 int what, int32_t* err) {
+  if (what & SNAPMIND_PEER_SIGNAL) {
+    __threadfence_system();
+    for (int r = threadIdx.x; r < n; r += blockDim.x) st_release_sys(peer_flags[r] + rank, epoch);
+  }
+  if (!(what & SNAPMIND_PEER_WAIT)) return;
   const unsigned long long t0 = global_ns();
   for (int r = threadIdx.x; r < n; r += blockDim.x) {
     while ((int32_t)(ld_acquire_sys(flags + r) - epoch) < 0) {
@@ -71,10 +85,17 @@ using namespace snapmind;
 
 extern "C" {
 
-int snapmind_peer_wait(const int32_t* flags, int32_t n_peers, int32_t epoch, int32_t* err_word, void* stream) {
-  SNAPMIND_CHECK_ARG(flags != nullptr && n_peers >= 1 && n_peers <= 1024, "peer_wait: bad arguments");
-  peer_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, n_peers, epoch, err_word);
-  return cuda_status(cudaGetLastError(), "peer_wait launch");
+int snapmind_peer_sync(int32_t* const* peer_flags, const int32_t* flags, int32_t n_peers, int32_t rank,
+                       int32_t epoch, int32_t what, int32_t* err_word, void* stream) {
+  SNAPMIND_CHECK_ARG(n_peers >= 1 && n_peers <= 1024 && rank >= 0 && rank < n_peers && epoch > 0 &&
+                         (what & ~(SNAPMIND_PEER_SIGNAL | SNAPMIND_PEER_WAIT)) == 0,
+                     "peer_sync: bad arguments");
+  SNAPMIND_CHECK_ARG(!(what & SNAPMIND_PEER_SIGNAL) || peer_flags != nullptr, "peer_sync: peer_flags is NULL");
+  SNAPMIND_CHECK_ARG(!(what & SNAPMIND_PEER_WAIT) || flags != nullptr, "peer_sync: flags is NULL");
+  if (what == 0) return SNAPMIND_OK;
+  peer_sync_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(peer_flags, flags, n_peers, rank, epoch, what,
+                                                                    err_word);
+  return cuda_status(cudaGetLastError(), "peer_sync launch");
 }
 
 int snapmind_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out) {

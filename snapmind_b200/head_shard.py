@@ -13,11 +13,11 @@ reorder of the gathered ``[N, B, Hq/N, D]`` into ``[B, Hq, D]``.
 
 ``PeerHeadShardedDecode`` fuses the exchange into the decode kernel: its
 epilogue stores every finished output row into every rank's ``[B, Hq, D]``
-buffer at the row's global head (plain NVLink stores through CUDA IPC
-mappings), the last CTA publishes the call's epoch into every rank's flag
-array, and a one-warp kernel waits (bounded) for all ranks' epochs.  No
-collective launch, no gathered copy, no reorder: the rows land in place while
-other CTAs are still attending.
+buffer at the row's global head (16-byte NVLink stores through CUDA IPC
+mappings), so the rows land in place while other CTAs are still attending.
+One warp after it publishes the call's epoch into every rank's flag array and
+waits (bounded) for all ranks' epochs.  No collective launch, no gathered
+copy, no reorder.
 """
 from __future__ import annotations
 
@@ -82,13 +82,10 @@ class PeerTargets:
     """Destinations of one head-sharded decode call (``PagedKVPool.decode(peers=...)``)."""
 
     out_ptrs: torch.Tensor   # int64 [n] device: each rank's output base for this call
-    flag_ptrs: torch.Tensor  # int64 [n] device: each rank's flag array
     n: int
-    rank: int
     head_offset: int         # global index of this rank's first query head
     out_stride_seq: int      # elements
     out_stride_head: int
-    epoch: int
 
 
 # allocations opened in this process: handle bytes -> [base pointer, users]
@@ -181,13 +178,14 @@ class PeerHeadShardedDecode(HeadShardedDecode):
         self.epoch += 1
         par = self.epoch & 1
         q_local = shard_query(q, self.n_kv_total, self.world, self.rank)
-        targets = PeerTargets(self._out_ptrs[par], self._flag_ptrs, self.world, self.rank, self.head_offset,
-                              self.n_q_heads * self.head_dim, self.head_dim, self.epoch)
+        targets = PeerTargets(self._out_ptrs[par], self.world, self.head_offset, self.n_q_heads * self.head_dim,
+                              self.head_dim)
         self.pool.decode(layer, q_local, peers=targets, **kw)
         _lib.check(
-            _lib.load().snapmind_peer_wait(self._flags.data_ptr(), self.world, self.epoch, self.err.data_ptr(),
+            _lib.load().snapmind_peer_sync(self._flag_ptrs.data_ptr(), self._flags.data_ptr(), self.world, self.rank,
+                                           self.epoch, _lib.PEER_SIGNAL | _lib.PEER_WAIT, self.err.data_ptr(),
                                            self.pool._stream()),
-            "snapmind_peer_wait",
+            "snapmind_peer_sync",
         )
         n = b * self.n_q_heads * self.head_dim
         view = self._buf[par * self._out_bytes:].view(self.dtype)[:n].view(b, self.n_q_heads, self.head_dim)

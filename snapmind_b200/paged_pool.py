@@ -158,7 +158,6 @@ class PagedKVPool(BlockPool):
                 self.block_tables.data_ptr(), self.max_blocks_per_seq, self.max_blocks_per_seq,
                 self.seq_lens.data_ptr(), None,
                 peers.out_ptrs.data_ptr(), peers.n, peers.head_offset, peers.out_stride_seq, peers.out_stride_head,
-                peers.flag_ptrs.data_ptr(), peers.rank, peers.epoch,
                 float(scale), batch, n_q, self.n_kv_heads, self.head_dim, self.block_size, self.num_blocks,
                 max_len, split, _lib.DECODE_FORCE_GENERIC if force_generic else 0,
                 ws.data_ptr(), ws.numel(), self.err.data_ptr(), self._stream(),

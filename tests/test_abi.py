@@ -52,14 +52,17 @@ def test_host_side_argument_errors_need_no_gpu():
     rc = l.snapmind_paged_gqa_decode(None, 0, 0, None, None, 1, None, 0, 0, None, None, 0, 0, 1.0,
                                      1, 6, 4, 128, 16, 1, 0, 0, 0, None, 0, None, None)
     assert rc == lib.ERR_BAD_ARGUMENT and "multiple" in lib.last_error()
-    # the peer decode: every rank must signal, so an empty batch is refused; so is a rank outside the peers
-    peers_args = lambda batch, n_peers, rank, epoch: l.snapmind_paged_gqa_decode_peers(
-        None, 0, 0, None, None, 1, None, 0, 0, None, None, 8, n_peers, 0, 0, 0, 8, rank, epoch, 1.0,
-        batch, 8, 8, 128, 16, 1, 0, 0, 0, None, 0, None, None)
-    assert peers_args(0, 2, 0, 1) == lib.ERR_BAD_ARGUMENT and "batch" in lib.last_error()
-    assert peers_args(1, 2, 2, 1) == lib.ERR_BAD_ARGUMENT and "peer" in lib.last_error()
-    assert peers_args(1, 2, 0, 0) == lib.ERR_BAD_ARGUMENT and "peer" in lib.last_error()
-    assert l.snapmind_peer_wait(None, 2, 1, None, None) == lib.ERR_BAD_ARGUMENT
+    # the peer decode: whole 16-byte vectors per peer store, at least one peer
+    peers_args = lambda n_peers, stride_head: l.snapmind_paged_gqa_decode_peers(
+        None, 0, 0, None, None, 1, None, 0, 0, None, None, 8, n_peers, 0, 8 * 128, stride_head, 1.0,
+        1, 8, 8, 128, 16, 1, 0, 0, 0, None, 0, None, None)
+    assert peers_args(0, 128) == lib.ERR_BAD_ARGUMENT and "peer" in lib.last_error()
+    assert peers_args(2, 100) == lib.ERR_BAD_ARGUMENT and "16 bytes" in lib.last_error()
+    # the flag sync: rank inside the peers, a positive epoch, the arrays the mode needs
+    assert l.snapmind_peer_sync(None, None, 2, 2, 1, lib.PEER_WAIT, None, None) == lib.ERR_BAD_ARGUMENT
+    assert l.snapmind_peer_sync(None, None, 2, 0, 0, lib.PEER_WAIT, None, None) == lib.ERR_BAD_ARGUMENT
+    assert l.snapmind_peer_sync(None, None, 2, 0, 1, lib.PEER_SIGNAL, None, None) == lib.ERR_BAD_ARGUMENT
+    assert l.snapmind_peer_sync(None, None, 2, 0, 1, lib.PEER_WAIT, None, None) == lib.ERR_BAD_ARGUMENT
     off = ctypes.c_int64(0)
     assert l.snapmind_ipc_export(None, None, ctypes.byref(off)) == lib.ERR_BAD_ARGUMENT
 
@@ -67,6 +70,6 @@ def test_host_side_argument_errors_need_no_gpu():
 def test_workspace_size_formula():
     l = lib.load()
     n = l.snapmind_paged_gqa_decode_workspace_bytes(128, 32, 8, 128, 8192, 512)
-    counters = (128 * 8 * 4 + 4 + 255) // 256 * 256  # tickets + the finished-output counter
+    counters = (128 * 8 * 4 + 255) // 256 * 256
     assert n == counters + 128 * 32 * 16 * 130 * 4
     assert l.snapmind_paged_gqa_decode_split_tokens(128, 8, 8192, 16) % 64 == 0

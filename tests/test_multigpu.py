@@ -1,6 +1,6 @@
 """KV-head-sharded paged decode on 2 GPUs (skipped with fewer GPUs): the NCCL
 all-gather version, and the version whose decode kernel stores the rows into
-every rank's buffer over NVLink (CUDA IPC peer mappings, no multicast)."""
+every rank's buffer over NVLink (plain stores through CUDA IPC peer mappings)."""
 import os
 import socket
 

@@ -1,10 +1,11 @@
 """The head-sharded decode with output rows stored into every rank's buffer
-(snapmind_paged_gqa_decode_peers + snapmind_peer_wait), on one GPU.
+(snapmind_paged_gqa_decode_peers + snapmind_peer_sync), on one GPU.
 
 The ranks are emulated in one process: each "rank" has its own pool (its kv
-heads), receive buffers and flag array, all on cuda:0; the decodes of all
-ranks are launched one after another on one stream and the waits come after
-all of them, so no kernel ever waits for one that has not already finished.
+heads), receive buffers and flag array, all on cuda:0; the decodes and
+signals of all ranks are launched one after another on one stream and the
+waits come after all of them, so no kernel ever waits for one that has not
+already finished.
 Checked: every rank's buffer equals the concatenated local decodes bit for
 bit and the oracle within the bf16/fp32 tolerances, over several epochs and
 both buffer parities; a wait on a flag that nothing sets gives up and reports.
@@ -89,10 +90,13 @@ def test_peer_decode_emulated_ranks(cuda_device, dtype, world):
             lo, hi = head_range(H, world, r)
             q_r = qd[:, lo * group: hi * group]
             local.append(pools[r].decode(0, q_r))
-            t = PeerTargets(out_ptrs[par], flag_ptrs, world, r, lo * group, Hq * D, D, epoch)
+            t = PeerTargets(out_ptrs[par], world, lo * group, Hq * D, D)
             assert pools[r].decode(0, q_r, peers=t) is None
+            lib.check(l.snapmind_peer_sync(flag_ptrs.data_ptr(), None, world, r, epoch, lib.PEER_SIGNAL,
+                                           errs.data_ptr(), stream), "signal")
         for r in range(world):
-            lib.check(l.snapmind_peer_wait(flags[r].data_ptr(), world, epoch, errs.data_ptr(), stream), "wait")
+            lib.check(l.snapmind_peer_sync(None, flags[r].data_ptr(), world, r, epoch, lib.PEER_WAIT,
+                                           errs.data_ptr(), stream), "wait")
         torch.cuda.synchronize()
         for p in pools:
             p.check()
@@ -119,7 +123,7 @@ def test_peer_wait_gives_up_on_a_flag_nobody_sets(cuda_device):
     err = torch.zeros(1, dtype=torch.int32, device=cuda_device)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    lib.check(lib.load().snapmind_peer_wait(flags.data_ptr(), 2, 5, err.data_ptr(),
+    lib.check(lib.load().snapmind_peer_sync(None, flags.data_ptr(), 2, 0, 5, lib.PEER_WAIT, err.data_ptr(),
                                             torch.cuda.current_stream().cuda_stream), "wait")
     torch.cuda.synchronize()
     dt = time.perf_counter() - t0
@@ -130,7 +134,7 @@ def test_peer_wait_gives_up_on_a_flag_nobody_sets(cuda_device):
     # an arrived epoch (or a later one) passes at once
     err.zero_()
     flags[1] = 6
-    lib.check(lib.load().snapmind_peer_wait(flags.data_ptr(), 2, 5, err.data_ptr(),
+    lib.check(lib.load().snapmind_peer_sync(None, flags.data_ptr(), 2, 0, 5, lib.PEER_WAIT, err.data_ptr(),
                                             torch.cuda.current_stream().cuda_stream), "wait")
     torch.cuda.synchronize()
     assert int(err.item()) == 0
