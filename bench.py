@@ -730,9 +730,15 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
         pool.reserve_device(1, B)
         pool.append(0, lat_new, rope_new)
         idx, _ = sel.select(sel.query(hidden), n_chunks_dev, k=MLA_TOPK)
-        pool.sparse_decode(0, q_lat, q_pe, idx, sink=4, window=1024, scale=scale, n_splits=4)
+        pool.sparse_decode(0, q_lat, q_pe, idx, sink=4, window=1024, scale=scale)
 
     graphs: dict[int, torch.cuda.CUDAGraph] = {}
+
+    # kernels per step: reserve, append, top-k, sparse attention (+ the split merge when it splits)
+    from snapmind_b200 import _lib as slib
+
+    n_spl = slib.load().snapmind_sparse_mla_default_splits(B, MLA_HEADS, MLA_RANK, MLA_ROPE, MLA_CHUNK, 1)
+    per_core = 4 + (1 if n_spl > 1 else 0)
 
     def capture(n_core: int) -> None:  # recorded, not run
         gr = torch.cuda.CUDAGraph()
@@ -749,7 +755,7 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
                 core()
             torch.cuda.current_stream(dev).wait_stream(side)
             pool.account_host(1, B)
-            launches[0] += 4
+            launches[0] += per_core
             for n in (1, 8):
                 capture(n)
             n_core -= 1
@@ -761,7 +767,7 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
                 return
         graphs[n_core].replay()
         pool.account_host(n_core, B)
-        launches[0] += 4 * n_core
+        launches[0] += per_core * n_core
 
     def run_steps(n: int) -> None:
         done = 0
@@ -773,8 +779,8 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
                 sel.update_keys(0, (length + 1) // MLA_CHUNK - 1, 1, batch=B)
                 n_chunks_dev.add_(1)
                 idx, _ = sel.select(sel.query(hidden), n_chunks_dev, k=MLA_TOPK)
-                pool.sparse_decode(0, q_lat, q_pe, idx, sink=4, window=1024, scale=scale, n_splits=4)
-                launches[0] += 5
+                pool.sparse_decode(0, q_lat, q_pe, idx, sink=4, window=1024, scale=scale)
+                launches[0] += per_core + 1
                 done += 1
                 continue
             free = MLA_CHUNK - 1 - (length + 1) % MLA_CHUNK  # later steps before the completing one
@@ -819,8 +825,7 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
         return e0_.elapsed_time(e1_) * 1e3 / reps
 
     select_us = graph_us(lambda: sel.select(qsel, n_chunks_dev, k=MLA_TOPK))
-    sparse_us = graph_us(lambda: pool.sparse_decode(0, q_lat, q_pe, idx0, sink=4, window=1024, scale=scale,
-                                                    n_splits=4))
+    sparse_us = graph_us(lambda: pool.sparse_decode(0, q_lat, q_pe, idx0, sink=4, window=1024, scale=scale))
     # attended rows per sequence: top-k chunks + the sink chunk + the window chunks (about)
     att_tokens = B * (MLA_TOPK * MLA_CHUNK + MLA_CHUNK + 1024 + MLA_CHUNK)
     sparse_bytes = att_tokens * (MLA_RANK + MLA_ROPE) * 2

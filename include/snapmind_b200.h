@@ -308,6 +308,15 @@ SNAPMIND_API int64_t snapmind_indexer_topk_workspace_bytes(int32_t batch, int32_
  * n_heads is a multiple of 16; splits > 1 need a zero-filled workspace of
  * snapmind_sparse_mla_workspace_bytes(...) bytes.
  */
+/*
+ * Split count the sparse MLA kernels run best with for this batch (CTAs per
+ * sequence along the attended positions): the tcgen05 kernel (128 heads,
+ * kv_lora_rank 512, rope 64, block 64, bf16/f16) fills the SMs with
+ * (split, output half) CTAs; the other shapes with (split, 32-head group) CTAs.
+ * No reference counterpart (the reference has no GPU path).
+ */
+SNAPMIND_API int32_t snapmind_sparse_mla_default_splits(int32_t batch, int32_t n_heads, int32_t kv_lora_rank,
+                                                       int32_t rope_dim, int32_t block_size, int32_t dtype);
 SNAPMIND_API int64_t snapmind_sparse_mla_workspace_bytes(int32_t batch, int32_t n_heads, int32_t kv_lora_rank,
                                                          int32_t n_splits);
 SNAPMIND_API int snapmind_sparse_mla_decode(const void *q_lat, const void *q_pe, int dtype, const void *latent_pool,

@@ -93,6 +93,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _p, _int, _p, _i32, _i32, _i32, _i32, _f32, _f32, _i32, _p, _p, _p, _p, _i64, _p],
     ),
     "snapmind_indexer_topk_workspace_bytes": (_i64, [_i32, _i32, _i32]),
+    "snapmind_sparse_mla_default_splits": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "snapmind_sparse_mla_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32]),
     "snapmind_sparse_mla_decode": (
         _int,

@@ -253,6 +253,17 @@ using namespace snapmind;
 
 extern "C" {
 
+int32_t snapmind_sparse_mla_default_splits(int32_t batch, int32_t n_heads, int32_t kv_lora_rank, int32_t rope_dim,
+                                           int32_t block_size, int32_t dtype) {
+  if (batch <= 0 || n_heads <= 0) return 1;
+  if ((dtype == SNAPMIND_DTYPE_BF16 || dtype == SNAPMIND_DTYPE_F16) && n_heads == 128 && kv_lora_rank == 512 &&
+      rope_dim == 64 && block_size == 64)
+    return sparse_mla_umma_splits(batch);  // (split, output half) CTAs fill the SMs once
+  const int groups = (n_heads + 31) / 32;
+  const int per_seq = num_sms() / (groups * batch);
+  return per_seq < 1 ? 1 : (per_seq > 64 ? 64 : per_seq);
+}
+
 int64_t snapmind_sparse_mla_workspace_bytes(int32_t batch, int32_t n_heads, int32_t kv_lora_rank, int32_t n_splits) {
   if (batch <= 0 || n_heads <= 0 || kv_lora_rank <= 0 || n_splits <= 0) return 0;
   const int groups = (n_heads + kHeadsPerCta - 1) / kHeadsPerCta;
@@ -331,6 +342,7 @@ int snapmind_sparse_mla_decode(const void* q_lat, const void* q_pe, int dtype, c
                       (size_t)block_size * (kv_lora_rank + rope_dim) * esz + 16;
   SNAPMIND_CHECK_ARG(smem <= 227 * 1024, "sparse_mla_decode: shared memory %zu exceeds the limit", smem);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (sparse_mla_umma_supported(p, dtype)) return launch_sparse_mla_umma(p, dtype, st);
   if (sparse_mla_tc_supported(p, dtype)) return launch_sparse_mla_tc(p, dtype, st);
   dim3 grid(n_splits, groups, batch);
   auto go = [&](auto kernel) -> int {

@@ -21,7 +21,12 @@ struct SparseParams {
   DecodeParams dp;  // output, partials and tickets in the paged-decode layout (group = 16 heads)
 };
 
-// Tensor-core path (sparse_mla_tc.cu): bf16/f16, R = 512, P = 64, block 64.
+// tcgen05 path (sparse_mla_umma.cu): bf16/f16, 128 heads, R = 512, P = 64, block 64.
+bool sparse_mla_umma_supported(const SparseParams& p, int dtype);
+int launch_sparse_mla_umma(const SparseParams& p, int dtype, cudaStream_t stream);
+int sparse_mla_umma_splits(int batch);
+
+// mma.sync path (sparse_mla_tc.cu): bf16/f16, heads a multiple of 16, R = 512, P = 64, block 64.
 bool sparse_mla_tc_supported(const SparseParams& p, int dtype);
 int launch_sparse_mla_tc(const SparseParams& p, int dtype, cudaStream_t stream);
 

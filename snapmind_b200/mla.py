@@ -118,7 +118,7 @@ class MLALatentPool(BlockPool):
 
 
     def sparse_decode(self, layer: int, q_lat: torch.Tensor, q_pe: torch.Tensor, selected: torch.Tensor | None,
-                      sink: int = 4, window: int = 1024, scale: float | None = None, n_splits: int = 4,
+                      sink: int = 4, window: int = 1024, scale: float | None = None, n_splits: int | None = None,
                       out: torch.Tensor | None = None, batch: int | None = None) -> torch.Tensor:
         """Sparse MLA decode attention of one query token per sequence.
 
@@ -126,7 +126,8 @@ class MLALatentPool(BlockPool):
         key up-projection), ``q_pe`` ``[B, H, rope_dim]``, ``selected`` int32
         ``[B, k]`` chunk ids (block ids of the sequence, -1 unused).  Attends over
         positions < sink, >= len - window and the selected chunks; returns the
-        latent output ``[B, H, kv_lora_rank]``.
+        latent output ``[B, H, kv_lora_rank]``.  ``n_splits`` (CTAs per
+        sequence and head group) defaults to the kernel's choice for the batch.
         """
         batch = q_lat.shape[0] if batch is None else batch
         H = q_lat.shape[1]
@@ -138,6 +139,9 @@ class MLALatentPool(BlockPool):
             out = torch.empty((batch, H, self.kv_lora_rank), dtype=self.dtype, device=self.device)
         k = 0 if selected is None else selected.shape[1]
         lib = _lib.load()
+        if n_splits is None:
+            n_splits = lib.snapmind_sparse_mla_default_splits(batch, H, self.kv_lora_rank, self.rope_dim,
+                                                              self.block_size, self._dcode)
         need = lib.snapmind_sparse_mla_workspace_bytes(batch, H, self.kv_lora_rank, n_splits)
         ws = getattr(self, "_sparse_ws", None)
         if ws is None or ws.numel() < need:

@@ -213,9 +213,10 @@ def test_topk_sliced_equals_single_cta(cuda_device, k, n_chunks):
     assert int(ws[: 4 * B].count_nonzero()) == 0  # tickets reset
 
 
+@pytest.mark.parametrize("H", [32, 128])  # mma.sync kernel (32 heads), tcgen05 kernel (128 heads)
 @pytest.mark.parametrize("sink,window,n_splits", [(4, 1024, 4), (0, 0, 1), (4, 200, 3), (70, 5000, 2)])
-def test_sparse_mla_decode_matches_oracle(cuda_device, sink, window, n_splits):
-    B, H, R, P, bs, k = 4, 32, 512, 64, 64, 8
+def test_sparse_mla_decode_matches_oracle(cuda_device, sink, window, n_splits, H):
+    B, R, P, bs, k = 4, 512, 64, 64, 8
     lens = [64 * 30 + 5, 700, 64 * 20, 1]
     pool, lat, rope, tables = _latent_pool(B, lens, bs=bs, seed=11)
     rng = np.random.RandomState(3)
@@ -273,3 +274,57 @@ def test_sparse_mla_decode_cuda_core_path(cuda_device, R, P, dt):
         want = omla.sparse_mla_decode(q_lat[b], q_pe[b], _seq_rows(lat, tables, b, lens[b], bs),
                                       _seq_rows(rope, tables, b, lens[b], bs), pos, scale)
         np.testing.assert_allclose(got[b], want, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("n_splits", [1, 3, None])
+def test_sparse_mla_tcgen05_rising_scores_and_poisoned_slots(cuda_device, n_splits):
+    """128 heads (tcgen05 kernel): scores that rise by ~40 in log2 units along the
+    sequence for half of the heads (the reference maximum is raised and the
+    output rescaled in TMEM several times) and fall for the other half (no
+    rescale after the first tile), with NaN in every pool slot that holds no
+    token (rows past each sequence's end and the spare blocks)."""
+    B, H, R, P, bs = 2, 128, 512, 64, 64
+    lens = [64 * 31 + 17, 64 * 12]
+    pool, lat, rope, tables = _latent_pool(B, lens, bs=bs, seed=41)
+    u = np.random.RandomState(5).standard_normal(R)
+    u /= np.linalg.norm(u)
+    nb = lat.shape[0]
+    scale = (128 + 64) ** -0.5
+    slope = 0.02 / (scale * 1.4426950408889634)  # q . k grows by 0.02 log2 units per position
+    for b in range(B):
+        for j, blk in enumerate(tables[b][: (lens[b] + bs - 1) // bs]):
+            t = j * bs + np.arange(bs)
+            lat[blk] = bf16.round_to_bf16(0.1 * lat[blk] + np.outer(slope * t, u).astype(np.float32))
+    poison = np.zeros((nb, bs), bool)
+    used = set()
+    for b in range(B):
+        nbk = (lens[b] + bs - 1) // bs
+        used.update(int(x) for x in tables[b][:nbk])
+        if lens[b] % bs:
+            poison[tables[b][nbk - 1], lens[b] % bs:] = True
+    for blk in range(nb):
+        if blk not in used:
+            poison[blk] = True
+    lat_dev = lat.copy()
+    rope_dev = rope.copy()
+    lat_dev[poison] = np.nan
+    rope_dev[poison] = np.nan
+    pool.latent[0, :, 0].copy_(torch.from_numpy(lat_dev).to(torch.bfloat16))
+    pool.rope[0, :, 0].copy_(torch.from_numpy(rope_dev).to(torch.bfloat16))
+    sign = np.where(np.arange(H) % 2 == 0, 1.0, -1.0)[:, None]
+    q_lat = bf16.round_to_bf16((sign * u[None, :] + 0.01 * randn(51, (B, H, R))).astype(np.float32))
+    q_pe = bf16.round_to_bf16(randn(52, (B, H, P)) * 0.05)
+    selected = np.array([[3, 9, 20, -1], [0, 5, 7, 11]], np.int32)
+    kw = {} if n_splits is None else {"n_splits": n_splits}
+    out = pool.sparse_decode(0, torch.from_numpy(q_lat).cuda().to(torch.bfloat16),
+                             torch.from_numpy(q_pe).cuda().to(torch.bfloat16), torch.from_numpy(selected).cuda(),
+                             sink=4, window=300, scale=scale, **kw)
+    pool.check()
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    for b in range(B):
+        sel_b = [int(c) for c in selected[b] if 0 <= c < (lens[b] + bs - 1) // bs]
+        pos = omla.sparse_positions(lens[b], sel_b, bs, 4, 300)
+        want = omla.sparse_mla_decode(q_lat[b], q_pe[b], _seq_rows(lat, tables, b, lens[b], bs),
+                                      _seq_rows(rope, tables, b, lens[b], bs), pos, scale)
+        np.testing.assert_allclose(got[b], want, rtol=2e-2, atol=2e-2)
