@@ -6,13 +6,14 @@
 // [n x 576] (latent 512 | rope 64), output [128 x 512] over the first 512
 // columns of the same rows.  The 128 heads are exactly the M = 128 of one
 // tcgen05.mma, so:
-//   CTA = (split s, output half dh, sequence b), 4 warps (thread = head row).
+//   CTA = (split s, output half dh, sequence b), 6 warps: warps 0-3 softmax
+//   (thread = head row = TMEM lane), warp 4 TMA producer, warp 5 MMA issuer.
 //   Shared memory (1024-aligned, 128-byte swizzle, written by TMA):
 //     Q: 9 k-blocks x [128 rows x 64] = 144 KB, resident;
 //     2 stages of 32 attended rows: 9 k-blocks x [32 rows x 64] = 36 KB each;
 //     P: [128 x 32] bf16, 64-byte swizzle, written by the softmax threads.
 //   TMEM (512 columns): O [128 x 256] f32 at column 0 (this CTA's half of the
-//     512 output dims), S [128 x 32] f32 at column 256.
+//     512 output dims), two S buffers [128 x 32] f32 at columns 256 and 288.
 //   Per tile of 32 tokens (half a block):
 //     S = Q K^T: 36 MMAs (M 128, N 32, K 16), K-major operands;
 //     softmax: each thread loads its row of S from TMEM, masks the tokens
@@ -21,8 +22,12 @@
 //       writes P = exp2(s - m) as bf16 into shared memory;
 //     O += P V: 2 MMAs (M 128, N 256, K 16), V = the tile's latent columns
 //       [256 dh, 256 dh + 256) read MN-major from the same staged rows.
-//   One thread issues TMA loads and MMAs; completion is tracked by mbarriers
-//   (tcgen05.commit), every wait is bounded (about a second), and TMEM is
+//   Pipeline: the producer refills a stage once O += P V of its previous tile
+//   has completed; the MMA warp issues S of tile t (into S buffer t & 1)
+//   before O += P V of tile t - 1, so the tensor core computes the next
+//   scores while the softmax warps work on the current ones.  Handshakes are
+//   mbarriers (tcgen05.commit for the tensor core), every wait is bounded
+//   (about a second) and ends early once another role gave up, and TMEM is
 //   released on every path.
 // Splits write fp32 partials (max, sum, unnormalised output) in the layout of
 // the paged GQA decode; a second kernel merges them over all (sequence, head)
@@ -51,7 +56,9 @@ constexpr int kKB = (kR + kP) / 64;                     // 9 k-blocks of 64 elem
 constexpr int kBs = 64;                                 // block (chunk) size
 constexpr int kTok = 32;                                // tokens per tile
 constexpr int kDH = kR / 2;                             // output dims per CTA
-constexpr int kThreads = 128;
+constexpr int kSoftmaxThreads = 128;                    // warps 0-3: one head row per thread
+constexpr int kProducerWarp = 4, kMmaWarp = 5;
+constexpr int kThreads = 192;
 constexpr uint32_t kQBlock = kH * 128;                  // one k-block of Q: 16 KB
 constexpr uint32_t kQBytes = kKB * kQBlock;             // 144 KB
 constexpr uint32_t kTBlock = kTok * 128;                // one k-block of a tile: 4 KB
@@ -63,10 +70,15 @@ constexpr uint32_t kTmemCols = 512, kColO = 0, kColS = 256;
 constexpr float kRescale = 8.f;                         // log2 headroom of the reference maximum
 
 struct Ctrl {
-  uint64_t full[kStages];
+  uint64_t full[kStages];    // producer -> MMA, softmax: tile staged
+  uint64_t empty[kStages];   // MMA commit after O += P V: stage free
+  uint64_t s_full[2];        // MMA commit after S = Q K^T: S buffer ready
+  uint64_t s_empty[2];       // softmax threads: S buffer read
   uint64_t q_full;
-  uint64_t mma;
+  uint64_t p_full;           // softmax threads: P written (and O rescaled)
+  uint64_t o_done;           // MMA commit after O += P V
   uint32_t tmem_base;
+  int32_t abort;
   int32_t count;
   int32_t tile_phys[kStages];
   int32_t tile_chunk[kStages];
@@ -100,6 +112,22 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Waits of the pipeline roles: bounded, and cut short once another role gave up.
+__device__ __forceinline__ bool role_wait(const Ctrl& C, uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*reinterpret_cast<const volatile int32_t*>(&C.abort)) return false;
+    if (clock64() - t0 > kWaitTicks) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void give_up(Ctrl& C, int32_t* err) {
+  atomicExch(&C.abort, 1);
+  flag_error(err, SNAPMIND_DEVERR_TIMEOUT);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     sparse_mla_umma_kernel(const __grid_constant__ CUtensorMap qlat_map, const __grid_constant__ CUtensorMap qpe_map,
@@ -118,14 +146,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = idesc_f16(kBf16, kH, kTok, false, false);
   constexpr uint32_t kIdescPV = idesc_f16(kBf16, kH, kDH, false, true);
+  const DecodeParams& dp = p.dp;
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) mbar_init(smem_u32(&C.full[i]), 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(smem_u32(&C.full[i]), 1);
+      mbar_init(smem_u32(&C.empty[i]), 1);
+      mbar_init(smem_u32(&C.s_full[i]), 1);
+      mbar_init(smem_u32(&C.s_empty[i]), kSoftmaxThreads);
+    }
     mbar_init(smem_u32(&C.q_full), 1);
-    mbar_init(smem_u32(&C.mma), 1);
+    mbar_init(smem_u32(&C.p_full), kSoftmaxThreads);
+    mbar_init(smem_u32(&C.o_done), 1);
+    C.abort = 0;
     mbar_init_fence();
   }
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(&C.tmem_base), kTmemCols);
     tmem_relinquish();
   }
@@ -135,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (len < 0) len = 0;
   int n_chunks = (len + kBs - 1) / kBs;
   if (n_chunks > kBits) {
-    if (tid == 0 && s == 0 && dh == 0) flag_error(p.dp.err, SNAPMIND_DEVERR_TABLE);
+    if (tid == 0 && s == 0 && dh == 0) flag_error(dp.err, SNAPMIND_DEVERR_TABLE);
     n_chunks = kBits;
     len = kBits * kBs;
   }
@@ -180,312 +216,308 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = C.tmem_base;
-  const uint32_t t_row = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's TMEM lanes
   const int count = C.count;
-  const DecodeParams& dp = p.dp;
-  const int head = tid;
 
   // tiles of this split: tile u = half (u & 1) of the (u >> 1)-th attended chunk
   const int total = 2 * count;
   const int per = (total + p.n_splits - 1) / max(p.n_splits, 1);
   const int u_lo = min(total, s * per), u_hi = min(total, u_lo + per);
   const int n_tiles = u_hi - u_lo;
+  const bool direct = (p.n_splits == 1);
 
-  auto issue_tile = [&](int t) {  // thread 0
-    const int st = t % kStages;
-    const int u = u_lo + t;
-    const int c = chunk_of_rank(C, words, u >> 1);
-    int32_t phys = c < p.table_width ? p.tables[(int64_t)b * p.table_stride + c] : -1;
-    if (phys >= p.num_blocks) phys = -1;
-    C.tile_phys[st] = phys;
-    C.tile_chunk[st] = c;
-    const uint32_t bar = smem_u32(&C.full[st]);
-    if (phys < 0) {
-      flag_error(dp.err, SNAPMIND_DEVERR_BLOCK_ID);
-      mbar_arrive(bar);
-      return;
-    }
-    mbar_arrive_expect_tx(bar, kTileBytes);
-    uint8_t* stage = kv_s + st * kTileBytes;
-    const int y = phys * kBs + (u & 1) * kTok;
+  if (n_tiles > 0) {
+    if (warp == kProducerWarp) {
+      // ---------------------------------------------------------------- TMA producer
+      if (lane == 0) {
+        const uint32_t qb = smem_u32(&C.q_full);
+        mbar_arrive_expect_tx(qb, kQBytes);
 #pragma unroll
-    for (int kb = 0; kb < kKB - 1; ++kb) tma_load_2d(smem_u32(stage + kb * kTBlock), &lat_map, kb * 64, y, bar);
-    tma_load_2d(smem_u32(stage + (kKB - 1) * kTBlock), &rope_map, 0, y, bar);
-  };
-
-  bool aborted = false;
-  int issued = 0, consumed = 0;
-  bool mma_pending = false, q_pending = false;
-  uint32_t mma_phase = 0;
-  float m_ref = -INFINITY, l_run = 0.f;  // this thread's head row, log2 units of score * scale
-  const float c2 = p.scale * 1.4426950408889634f;
-
-  if (count > 0 && n_tiles > 0) {
-    if (tid == 0) {
-      const uint32_t qb = smem_u32(&C.q_full);
-      mbar_arrive_expect_tx(qb, kQBytes);
+        for (int kb = 0; kb < kKB - 1; ++kb)
+          tma_load_2d(smem_u32(q_s + kb * kQBlock), &qlat_map, kb * 64, b * kH, qb);
+        tma_load_2d(smem_u32(q_s + (kKB - 1) * kQBlock), &qpe_map, 0, b * kH, qb);
+        int issued = 0;
+        for (int t = 0; t < n_tiles; ++t) {
+          const int st = t % kStages;
+          if (t >= kStages && !role_wait(C, smem_u32(&C.empty[st]), ((t / kStages) - 1) & 1)) {
+            give_up(C, dp.err);
+            break;
+          }
+          const int u = u_lo + t;
+          const int c = chunk_of_rank(C, words, u >> 1);
+          int32_t phys = c < p.table_width ? p.tables[(int64_t)b * p.table_stride + c] : -1;
+          if (phys >= p.num_blocks) phys = -1;
+          C.tile_phys[st] = phys;
+          C.tile_chunk[st] = c;
+          const uint32_t bar = smem_u32(&C.full[st]);
+          if (phys < 0) {
+            flag_error(dp.err, SNAPMIND_DEVERR_BLOCK_ID);
+            mbar_arrive(bar);
+          } else {
+            mbar_arrive_expect_tx(bar, kTileBytes);
+            uint8_t* stage = kv_s + st * kTileBytes;
+            const int y = phys * kBs + (u & 1) * kTok;
 #pragma unroll
-      for (int kb = 0; kb < kKB - 1; ++kb) tma_load_2d(smem_u32(q_s + kb * kQBlock), &qlat_map, kb * 64, b * kH, qb);
-      tma_load_2d(smem_u32(q_s + (kKB - 1) * kQBlock), &qpe_map, 0, b * kH, qb);
-      for (int t = 0; t < min(kStages, n_tiles); ++t) issue_tile(t);
-    }
-    issued = min(kStages, n_tiles);
-    q_pending = true;
-
-    for (int t = 0; t < n_tiles; ++t) {
-      const int st = t % kStages;
-      uint8_t* stage = kv_s + st * kTileBytes;
-      bool ok = true;
-      if (t == 0) {
-        ok = mbar_wait(smem_u32(&C.q_full), 0);
-        if (ok) q_pending = false;
-      }
-      ok = ok && mbar_wait(smem_u32(&C.full[st]), (t / kStages) & 1);
-      if (__syncthreads_or(!ok)) {
-        aborted = true;
-        break;
-      }
-      consumed = t + 1;
-      const int phys = C.tile_phys[st], c = C.tile_chunk[st];
-      const int pos0 = c * kBs + (t + u_lo) % 2 * kTok;
-      // rows holding no token (past the end, or an unloaded tile): zero this CTA's V columns
-      const int good = phys < 0 ? 0 : max(0, min(kTok, len - pos0));
-      if (good < kTok) {
-        const int rows = kTok - good;
-        for (int e = tid; e < 4 * rows * 8; e += kThreads) {
-          const int kb = dh * 4 + e / (rows * 8);
-          const int r = good + (e / 8) % rows;
-          *reinterpret_cast<uint4*>(stage + kb * kTBlock + r * 128 + (e & 7) * 16) = make_uint4(0, 0, 0, 0);
+            for (int kb = 0; kb < kKB - 1; ++kb)
+              tma_load_2d(smem_u32(stage + kb * kTBlock), &lat_map, kb * 64, y, bar);
+            tma_load_2d(smem_u32(stage + (kKB - 1) * kTBlock), &rope_map, 0, y, bar);
+          }
+          issued = t + 1;
         }
-        fence_proxy_async_smem();
+        // before the shared memory is released: every copy issued has landed (bounded)
+        for (int t = max(0, issued - kStages); t < issued; ++t)
+          mbar_wait(smem_u32(&C.full[t % kStages]), (t / kStages) & 1);
+        mbar_wait(smem_u32(&C.q_full), 0);
       }
-      const bool selected = phys >= 0 && ((C.sel_bits[c >> 5] >> (c & 31)) & 1u);
-      __syncthreads();
-
-      // ---- S = Q K^T
-      if (tid == 0) {
-        tc_fence_after();
-#pragma unroll 1
-        for (int kb = 0; kb < kKB; ++kb) {
+    } else if (warp == kMmaWarp) {
+      // ---------------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        bool ok = role_wait(C, smem_u32(&C.q_full), 0);
+        uint32_t last_bar = 0, last_parity = 0;  // the latest commit: covers every MMA issued
+        auto issue_pv = [&](int t) {  // O += P V of tile t
+          const uint8_t* stage = kv_s + (t % kStages) * kTileBytes;
+          tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = smem_desc(smem_u32(q_s + kb * kQBlock + kk * 32), 16, 1024, kSwizzle128B);
-            const uint64_t bd = smem_desc(smem_u32(stage + kb * kTBlock + kk * 32), 16, 1024, kSwizzle128B);
-            umma_f16(tmem + kColS, ad, bd, kIdescS, (kb | kk) != 0);
+          for (int ks = 0; ks < kTok / 16; ++ks) {
+            const uint64_t ad = smem_desc(smem_u32(p_s + ks * 32), 16, 512, kSwizzle64B);
+            const uint64_t bd =
+                smem_desc(smem_u32(stage + dh * 4 * kTBlock + ks * 16 * 128), kTBlock, 1024, kSwizzle128B);
+            umma_f16(tmem + kColO, ad, bd, kIdescPV, (t > 0 || ks > 0) ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&C.empty[t % kStages]));
+          umma_commit(smem_u32(&C.o_done));
+          last_bar = smem_u32(&C.o_done);
+          last_parity = t & 1;
+        };
+        for (int t = 0; ok && t < n_tiles; ++t) {
+          const int st = t % kStages, sb = t & 1;
+          ok = role_wait(C, smem_u32(&C.full[st]), (t / kStages) & 1) &&
+               (t < 2 || role_wait(C, smem_u32(&C.s_empty[sb]), ((t >> 1) - 1) & 1));
+          if (!ok) break;
+          // S = Q K^T into S buffer sb
+          const uint8_t* stage = kv_s + st * kTileBytes;
+          tc_fence_after();
+#pragma unroll 1
+          for (int kb = 0; kb < kKB; ++kb) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = smem_desc(smem_u32(q_s + kb * kQBlock + kk * 32), 16, 1024, kSwizzle128B);
+              const uint64_t bd = smem_desc(smem_u32(stage + kb * kTBlock + kk * 32), 16, 1024, kSwizzle128B);
+              umma_f16(tmem + kColS + sb * kTok, ad, bd, kIdescS, (kb | kk) != 0);
+            }
+          }
+          umma_commit(smem_u32(&C.s_full[sb]));
+          last_bar = smem_u32(&C.s_full[sb]);
+          last_parity = (t >> 1) & 1;
+          // O += P V of the previous tile, once its P is written
+          if (t >= 1) {
+            ok = role_wait(C, smem_u32(&C.p_full), (t - 1) & 1);
+            if (!ok) break;
+            issue_pv(t - 1);
           }
         }
-        umma_commit(smem_u32(&C.mma));
+        if (ok) {
+          ok = role_wait(C, smem_u32(&C.p_full), (n_tiles - 1) & 1);
+          if (ok) issue_pv(n_tiles - 1);
+        }
+        if (!ok) {
+          give_up(C, dp.err);
+          if (last_bar) mbar_wait(last_bar, last_parity);  // MMAs in flight finish (bounded) before TMEM goes
+        }
       }
-      mma_pending = true;
-      ok = mbar_wait(smem_u32(&C.mma), mma_phase);
-      if (__syncthreads_or(!ok)) {
-        aborted = true;
-        break;
-      }
-      mma_phase ^= 1;
-      mma_pending = false;
-      tc_fence_after();
-      // S(t) done, and with it O += P V of tile t - 1: its stage and P are free
-      if (tid == 0 && t + 1 < n_tiles && t + 1 >= kStages) {
-        issue_tile(t + 1);
-      }
-      if (t + 1 < n_tiles && t + 1 >= kStages) issued = t + 2;
-
-      // ---- softmax of this thread's row
-      float sv[kTok];
-      tmem_ld32(t_row + kColS, sv);
-      tmem_wait_ld();
-      float mt = -INFINITY;
+    } else {
+      // ---------------------------------------------------------------- softmax warps 0-3
+      const int head = tid;  // TMEM lane = head row
+      const uint32_t t_row = tmem + ((uint32_t)(warp * 32) << 16);
+      const float c2 = p.scale * 1.4426950408889634f;
+      float m_ref = -INFINITY, l_run = 0.f;  // log2 units of score * scale
+      bool ok = true;
+      for (int t = 0; t < n_tiles; ++t) {
+        const int st = t % kStages, sb = t & 1;
+        ok = role_wait(C, smem_u32(&C.full[st]), (t / kStages) & 1) &&
+             role_wait(C, smem_u32(&C.s_full[sb]), (t >> 1) & 1);
+        if (__any_sync(0xffffffffu, !ok)) {
+          ok = false;
+          break;
+        }
+        const int phys = C.tile_phys[st], c = C.tile_chunk[st];
+        const int pos0 = c * kBs + ((t + u_lo) & 1) * kTok;
+        const int good = phys < 0 ? 0 : max(0, min(kTok, len - pos0));  // rows holding a token
+        const bool selected = phys >= 0 && ((C.sel_bits[c >> 5] >> (c & 31)) & 1u);
+        tc_fence_after();
+        float sv[kTok];
+        tmem_ld32(t_row + kColS + sb * kTok, sv);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(smem_u32(&C.s_empty[sb]));
+        float mt = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < kTok; ++j) {
-        const int pos = pos0 + j;
-        const bool valid = j < good && (selected || pos < sink || pos >= wstart);
-        sv[j] = valid ? sv[j] * c2 : -INFINITY;
-        mt = fmaxf(mt, sv[j]);
+        for (int j = 0; j < kTok; ++j) {
+          const int pos = pos0 + j;
+          const bool valid = j < good && (selected || pos < sink || pos >= wstart);
+          sv[j] = valid ? sv[j] * c2 : -INFINITY;
+          mt = fmaxf(mt, sv[j]);
+        }
+        // O += P V of tile t - 1 has finished: P is free and O holds it
+        if (t >= 1) {
+          ok = role_wait(C, smem_u32(&C.o_done), (t - 1) & 1);
+          if (__any_sync(0xffffffffu, !ok)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        const bool raise = mt > m_ref + kRescale;
+        const float m_new = raise ? mt : m_ref;
+        if (__any_sync(0xffffffffu, raise && m_ref != -INFINITY)) {
+          // O rows of this warp at the old reference maximum: rescale in TMEM
+          const float alpha = (raise && m_ref != -INFINITY) ? exp2f(m_ref - m_new) : 1.f;
+#pragma unroll 1
+          for (int cc = 0; cc < kDH; cc += 32) {
+            float o[32];
+            tmem_ld32(t_row + kColO + cc, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] *= alpha;
+            tmem_st32(t_row + kColO + cc, o);
+          }
+          tmem_wait_st();
+          l_run *= alpha;
+        }
+        m_ref = m_new;
+        uint32_t pk[kTok / 2];
+        float psum = 0.f;
+#pragma unroll
+        for (int j = 0; j < kTok / 2; ++j) {
+          const float p0 = m_ref == -INFINITY ? 0.f : exp2f(sv[2 * j] - m_ref);
+          const float p1 = m_ref == -INFINITY ? 0.f : exp2f(sv[2 * j + 1] - m_ref);
+          psum += p0 + p1;
+          pk[j] = pack2<T>(p0, p1);
+        }
+        l_run += psum;
+        {  // row `head` of P: 64 bytes, 64-byte swizzle (chunk c of row r at c ^ ((r >> 1) & 3))
+          uint8_t* prow = p_s + (head >> 3) * 512 + (head & 7) * 64;
+          const int sw = (head >> 1) & 3;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4)
+            *reinterpret_cast<uint4*>(prow + ((c4 ^ sw) << 4)) =
+                make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]);
+        }
+        if (good < kTok) {  // rows holding no token: zero this CTA's V columns (S of the tile is done)
+          uint8_t* stage = kv_s + st * kTileBytes;
+          const int rows = kTok - good;
+          for (int e = tid; e < 4 * rows * 8; e += kSoftmaxThreads) {
+            const int kb = dh * 4 + e / (rows * 8);
+            const int r = good + (e / 8) % rows;
+            *reinterpret_cast<uint4*>(stage + kb * kTBlock + r * 128 + (e & 7) * 16) = make_uint4(0, 0, 0, 0);
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(smem_u32(&C.p_full));
       }
-      const bool raise = mt > m_ref + kRescale;
-      const float m_new = raise ? mt : m_ref;
-      if (__any_sync(0xffffffffu, raise && m_ref != -INFINITY)) {
-        // O rows of this warp at the old reference maximum: rescale in TMEM
-        const float alpha = (raise && m_ref != -INFINITY) ? exp2f(m_ref - m_new) : 1.f;
+      if (ok) {
+        ok = role_wait(C, smem_u32(&C.o_done), (n_tiles - 1) & 1);
+        ok = !__any_sync(0xffffffffu, !ok);
+      }
+      if (!ok) {
+        give_up(C, dp.err);
+      } else {
+        // ---- epilogue: this thread's row of O (256 columns)
+        tc_fence_after();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        float* part = dp.partials + (((int64_t)b * dp.n_q_heads + head) * dp.max_splits + s) * (kR + 2);
+        T* orow = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq +
+                  (int64_t)head * dp.out_stride_head + dh * kDH;
 #pragma unroll 1
         for (int cc = 0; cc < kDH; cc += 32) {
           float o[32];
           tmem_ld32(t_row + kColO + cc, o);
           tmem_wait_ld();
+          if (direct) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] *= alpha;
-          tmem_st32(t_row + kColO + cc, o);
+            for (int j = 0; j < 32; j += 8)
+              *reinterpret_cast<uint4*>(orow + cc + j) =
+                  make_uint4(pack2<T>(o[j] * inv, o[j + 1] * inv), pack2<T>(o[j + 2] * inv, o[j + 3] * inv),
+                             pack2<T>(o[j + 4] * inv, o[j + 5] * inv), pack2<T>(o[j + 6] * inv, o[j + 7] * inv));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j += 2)
+              *reinterpret_cast<float2*>(part + 2 + dh * kDH + cc + j) = make_float2(o[j], o[j + 1]);
+          }
         }
-        tmem_wait_st();
-        l_run *= alpha;
-      }
-      m_ref = m_new;
-      uint32_t pk[kTok / 2];
-      float psum = 0.f;
-#pragma unroll
-      for (int j = 0; j < kTok / 2; ++j) {
-        const float p0 = m_ref == -INFINITY ? 0.f : exp2f(sv[2 * j] - m_ref);
-        const float p1 = m_ref == -INFINITY ? 0.f : exp2f(sv[2 * j + 1] - m_ref);
-        psum += p0 + p1;
-        pk[j] = pack2<T>(p0, p1);
-      }
-      l_run += psum;
-      // row `head` of P: 64 bytes, 64-byte swizzle (16-byte chunk c of row r at chunk c ^ ((r >> 1) & 3))
-      {
-        uint8_t* prow = p_s + (head >> 3) * 512 + (head & 7) * 64;
-        const int sw = (head >> 1) & 3;
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4)
-          *reinterpret_cast<uint4*>(prow + ((c4 ^ sw) << 4)) =
-              make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncthreads();
-
-      // ---- O += P V
-      if (tid == 0) {
-        tc_fence_after();
-#pragma unroll
-        for (int ks = 0; ks < kTok / 16; ++ks) {
-          const uint64_t ad = smem_desc(smem_u32(p_s + ks * 32), 16, 512, kSwizzle64B);
-          const uint64_t bd =
-              smem_desc(smem_u32(stage + dh * 4 * kTBlock + ks * 16 * 128), kTBlock, 1024, kSwizzle128B);
-          umma_f16(tmem + kColO, ad, bd, kIdescPV, (t > 0 || ks > 0) ? 1u : 0u);
+        if (!direct && dh == 0) {
+          part[0] = m_ref == -INFINITY ? -INFINITY : m_ref * 0.6931471805599453f;  // natural-log units
+          part[1] = l_run;
         }
-        if (t + 1 == n_tiles) umma_commit(smem_u32(&C.mma));
       }
     }
-    if (!aborted) {
-      mma_pending = true;
-      const bool ok = mbar_wait(smem_u32(&C.mma), mma_phase);
-      if (__syncthreads_or(!ok)) aborted = true;
-      else mma_pending = false;
-      tc_fence_after();
-    }
-  }
-
-  if (aborted) {
-    if (tid == 0) {
-      flag_error(dp.err, SNAPMIND_DEVERR_TIMEOUT);
-      // wait (bounded) for what is still in flight before the memory is released
-      if (q_pending) mbar_wait(smem_u32(&C.q_full), 0);
-      for (int i = consumed; i < issued; ++i) mbar_wait(smem_u32(&C.full[i % kStages]), (i / kStages) & 1);
-      if (mma_pending) mbar_wait(smem_u32(&C.mma), mma_phase);
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-      tc_fence_after();
-      tmem_dealloc(tmem, kTmemCols);
-    }
-    return;
-  }
-
-  const bool direct = (p.n_splits == 1);
-  if (count == 0) {
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-      tc_fence_after();
-      tmem_dealloc(tmem, kTmemCols);
-    }
-    if (s == 0 && direct) {
+  } else if (tid < kSoftmaxThreads) {
+    // no tile in this split: an empty partial (or a zero output when nothing is attended)
+    const int head = tid;
+    if (direct) {
       T* o = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)head * dp.out_stride_head +
              dh * kDH;
       for (int d = 0; d < kDH; d += 8) *reinterpret_cast<uint4*>(o + d) = make_uint4(0, 0, 0, 0);
-    }
-    if (!direct) {  // empty partials: the merge reads every split
+    } else if (dh == 0) {
       float* part = dp.partials + (((int64_t)b * dp.n_q_heads + head) * dp.max_splits + s) * (kR + 2);
-      if (dh == 0) {
-        part[0] = -INFINITY;
-        part[1] = 0.f;
-      }
-      for (int d = 0; d < kDH; ++d) part[2 + dh * kDH + d] = 0.f;
+      part[0] = -INFINITY;
+      part[1] = 0.f;
     }
-    return;
   }
 
-  // ---- epilogue: this thread's row of O (256 columns)
-  const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-  float* part = dp.partials + (((int64_t)b * dp.n_q_heads + head) * dp.max_splits + s) * (kR + 2);
-  T* orow = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)head * dp.out_stride_head +
-            dh * kDH;
-#pragma unroll 1
-  for (int cc = 0; cc < kDH; cc += 32) {
-    float o[32];
-    if (n_tiles > 0) {
-      tmem_ld32(t_row + kColO + cc, o);
-      tmem_wait_ld();
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) o[j] = 0.f;
-    }
-    if (direct) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        const uint4 v = make_uint4(pack2<T>(o[j] * inv, o[j + 1] * inv), pack2<T>(o[j + 2] * inv, o[j + 3] * inv),
-                                   pack2<T>(o[j + 4] * inv, o[j + 5] * inv), pack2<T>(o[j + 6] * inv, o[j + 7] * inv));
-        *reinterpret_cast<uint4*>(orow + cc + j) = v;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; j += 2)
-        *reinterpret_cast<float2*>(part + 2 + dh * kDH + cc + j) = make_float2(o[j], o[j + 1]);
-    }
-  }
-  if (!direct && dh == 0) {
-    part[0] = m_ref == -INFINITY ? -INFINITY : m_ref * 0.6931471805599453f;  // natural-log units
-    part[1] = l_run;
-  }
+  // ---- every role is done with shared memory and TMEM
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
 }
 
-// Merge of the split partials: one CTA per (sequence, 8 heads), 16-byte output stores.
+// Merge of the split partials: one warp per (sequence, head, 128 output dims);
+// lanes read the splits' (max, sum) pairs in parallel, then every lane
+// accumulates 4 dims over all splits with independent loads.
 template <typename T>
 __global__ void __launch_bounds__(256) sparse_mla_merge_kernel(DecodeParams dp, int n_splits) {
-  const int b = blockIdx.y;
-  const int hl = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.x * 8 + hl;
+  const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int q4 = w & 3, h = (w >> 2) % kH, b = (w >> 2) / kH;
+  if (b >= dp.batch) return;
   const int64_t pstride = kR + 2;
   const float* pg = dp.partials + ((int64_t)b * dp.n_q_heads + h) * dp.max_splits * pstride;
-  float M = -INFINITY;
-  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, __ldcg(pg + s * pstride));
-  float L = 0.f;
-  for (int s = 0; s < n_splits; ++s) {
-    const float m = __ldcg(pg + s * pstride);
-    if (m != -INFINITY) L += __ldcg(pg + s * pstride + 1) * expf(m - M);
+  float m_l[2], l_l[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int sp = lane + 32 * i;
+    m_l[i] = sp < n_splits ? __ldcg(pg + sp * pstride) : -INFINITY;
+    l_l[i] = sp < n_splits ? __ldcg(pg + sp * pstride + 1) : 0.f;
   }
+  float M = fmaxf(m_l[0], m_l[1]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float f_l[2], L = 0.f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    f_l[i] = m_l[i] == -INFINITY ? 0.f : expf(m_l[i] - M);
+    L += l_l[i] * f_l[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  // lane covers dims [16 lane, 16 lane + 16)
-  float acc[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-  for (int s = 0; s < n_splits; ++s) {
-    const float m = __ldcg(pg + s * pstride);
-    if (m == -INFINITY) continue;
-    const float f = expf(m - M);
-    const float* a = pg + s * pstride + 2 + 16 * lane;
-#pragma unroll
-    for (int j = 0; j < 16; j += 2) {
-      const float2 v = __ldcg(reinterpret_cast<const float2*>(a + j));
-      acc[j] += v.x * f;
-      acc[j + 1] += v.y * f;
-    }
+  const int d = q4 * 128 + lane * 4;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int sp = 0; sp < n_splits; ++sp) {
+    const float f = __shfl_sync(0xffffffffu, sp < 32 ? f_l[0] : f_l[1], sp & 31);
+    if (f == 0.f) continue;
+    const float2 a = __ldcg(reinterpret_cast<const float2*>(pg + sp * pstride + 2 + d));
+    const float2 c = __ldcg(reinterpret_cast<const float2*>(pg + sp * pstride + 4 + d));
+    acc[0] += a.x * f;
+    acc[1] += a.y * f;
+    acc[2] += c.x * f;
+    acc[3] += c.y * f;
   }
-  T* o = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)h * dp.out_stride_head + 16 * lane;
-#pragma unroll
-  for (int j = 0; j < 16; j += 8) {
-    *reinterpret_cast<uint4*>(o + j) =
-        make_uint4(pack2<T>(acc[j] * inv, acc[j + 1] * inv), pack2<T>(acc[j + 2] * inv, acc[j + 3] * inv),
-                   pack2<T>(acc[j + 4] * inv, acc[j + 5] * inv), pack2<T>(acc[j + 6] * inv, acc[j + 7] * inv));
-  }
+  T* o = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)h * dp.out_stride_head + d;
+  *reinterpret_cast<uint2*>(o) = make_uint2(pack2<T>(acc[0] * inv, acc[1] * inv), pack2<T>(acc[2] * inv, acc[3] * inv));
 }
 
 }  // namespace
@@ -523,7 +555,7 @@ int launch_sparse_mla_umma(const SparseParams& p, int dtype, cudaStream_t st) {
     kernel<<<dim3(p.n_splits, 2, p.batch), kThreads, kSmemBytes, st>>>(qlat, qpe, lat, rope, p);
     int rc = cuda_status(cudaGetLastError(), "sparse_mla_umma launch");
     if (rc != SNAPMIND_OK || p.n_splits == 1) return rc;
-    merge<<<dim3(kH / 8, p.batch), 256, 0, st>>>(p.dp, p.n_splits);
+    merge<<<dim3(p.batch * kH * 4 / 8), 256, 0, st>>>(p.dp, p.n_splits);
     return cuda_status(cudaGetLastError(), "sparse_mla_merge launch");
   };
   return bf16 ? go(sparse_mla_umma_kernel<__nv_bfloat16>, sparse_mla_merge_kernel<__nv_bfloat16>)
