@@ -102,6 +102,13 @@ __device__ __forceinline__ int chunk_of_rank(const Ctrl& C, int words, int rank)
   return lo * 32 + __ffs(word) - 1;
 }
 
+// 2^x by the hardware approximation (MUFU.EX2); -inf -> 0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float hi);
 template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -342,20 +349,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int phys = C.tile_phys[st], c = C.tile_chunk[st];
         const int pos0 = c * kBs + ((t + u_lo) & 1) * kTok;
         const int good = phys < 0 ? 0 : max(0, min(kTok, len - pos0));  // rows holding a token
-        const bool selected = phys >= 0 && ((C.sel_bits[c >> 5] >> (c & 31)) & 1u);
+        // attended tokens of the tile as a bit mask: [0, good) for a selected chunk,
+        // else [0, min(good, sink - pos0)) and [max(0, wstart - pos0), good)
+        uint32_t vmask;
+        {
+          const uint32_t below_good = good >= 32 ? 0xffffffffu : ((1u << good) - 1u);
+          const bool selected = phys >= 0 && ((C.sel_bits[c >> 5] >> (c & 31)) & 1u);
+          if (selected) {
+            vmask = below_good;
+          } else {
+            const int a = max(0, min(32, sink - pos0));
+            const int w = max(0, min(32, wstart - pos0));
+            const uint32_t sink_bits = a >= 32 ? 0xffffffffu : ((1u << a) - 1u);
+            const uint32_t win_bits = w >= 32 ? 0u : ~((1u << w) - 1u);
+            vmask = (sink_bits | win_bits) & below_good;
+          }
+        }
         tc_fence_after();
         float sv[kTok];
         tmem_ld32(t_row + kColS + sb * kTok, sv);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(smem_u32(&C.s_empty[sb]));
-        float mt = -INFINITY;
+        // masked row maximum (raw scores; scale > 0), as a tree
+        float mx[kTok / 2];
 #pragma unroll
-        for (int j = 0; j < kTok; ++j) {
-          const int pos = pos0 + j;
-          const bool valid = j < good && (selected || pos < sink || pos >= wstart);
-          sv[j] = valid ? sv[j] * c2 : -INFINITY;
-          mt = fmaxf(mt, sv[j]);
+        for (int j = 0; j < kTok / 2; ++j)
+          mx[j] = fmaxf((vmask >> (2 * j)) & 1u ? sv[2 * j] : -INFINITY,
+                        (vmask >> (2 * j + 1)) & 1u ? sv[2 * j + 1] : -INFINITY);
+#pragma unroll
+        for (int w = kTok / 4; w >= 1; w >>= 1)
+#pragma unroll
+          for (int j = 0; j < w; ++j) mx[j] = fmaxf(mx[j], mx[j + w]);
+        const float mt = mx[0] * c2;
+        const bool raise = mt > m_ref + kRescale;
+        const float m_old = m_ref;
+        m_ref = raise ? mt : m_ref;
+        // P = 2^(s c2 - m) for attended tokens, 0 elsewhere
+        uint32_t pk[kTok / 2];
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < kTok / 2; ++j) {
+          const float e0 = ex2_approx(fmaf(sv[2 * j], c2, -m_ref));
+          const float e1 = ex2_approx(fmaf(sv[2 * j + 1], c2, -m_ref));
+          const float p0 = (vmask >> (2 * j)) & 1u ? e0 : 0.f;
+          const float p1 = (vmask >> (2 * j + 1)) & 1u ? e1 : 0.f;
+          ps[j & 3] += p0 + p1;
+          pk[j] = pack2<T>(p0, p1);
         }
         // O += P V of tile t - 1 has finished: P is free and O holds it
         if (t >= 1) {
@@ -366,11 +406,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
         }
-        const bool raise = mt > m_ref + kRescale;
-        const float m_new = raise ? mt : m_ref;
-        if (__any_sync(0xffffffffu, raise && m_ref != -INFINITY)) {
+        if (__any_sync(0xffffffffu, raise && m_old != -INFINITY)) {
           // O rows of this warp at the old reference maximum: rescale in TMEM
-          const float alpha = (raise && m_ref != -INFINITY) ? exp2f(m_ref - m_new) : 1.f;
+          const float alpha = (raise && m_old != -INFINITY) ? exp2f(m_old - m_ref) : 1.f;
 #pragma unroll 1
           for (int cc = 0; cc < kDH; cc += 32) {
             float o[32];
@@ -383,17 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
           l_run *= alpha;
         }
-        m_ref = m_new;
-        uint32_t pk[kTok / 2];
-        float psum = 0.f;
-#pragma unroll
-        for (int j = 0; j < kTok / 2; ++j) {
-          const float p0 = m_ref == -INFINITY ? 0.f : exp2f(sv[2 * j] - m_ref);
-          const float p1 = m_ref == -INFINITY ? 0.f : exp2f(sv[2 * j + 1] - m_ref);
-          psum += p0 + p1;
-          pk[j] = pack2<T>(p0, p1);
-        }
-        l_run += psum;
+        l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
         {  // row `head` of P: 64 bytes, 64-byte swizzle (chunk c of row r at c ^ ((r >> 1) & 3))
           uint8_t* prow = p_s + (head >> 3) * 512 + (head & 7) * 64;
           const int sw = (head >> 1) & 3;
@@ -505,16 +533,18 @@ __global__ void __launch_bounds__(256) sparse_mla_merge_kernel(DecodeParams dp, 
   const float inv = L > 0.f ? 1.f / L : 0.f;
   const int d = q4 * 128 + lane * 4;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
+  // splits without attended tokens (factor 0) may hold stale values: select, never multiply
+#pragma unroll 8
   for (int sp = 0; sp < n_splits; ++sp) {
     const float f = __shfl_sync(0xffffffffu, sp < 32 ? f_l[0] : f_l[1], sp & 31);
-    if (f == 0.f) continue;
     const float2 a = __ldcg(reinterpret_cast<const float2*>(pg + sp * pstride + 2 + d));
     const float2 c = __ldcg(reinterpret_cast<const float2*>(pg + sp * pstride + 4 + d));
-    acc[0] += a.x * f;
-    acc[1] += a.y * f;
-    acc[2] += c.x * f;
-    acc[3] += c.y * f;
+    if (f != 0.f) {
+      acc[0] = fmaf(a.x, f, acc[0]);
+      acc[1] = fmaf(a.y, f, acc[1]);
+      acc[2] = fmaf(c.x, f, acc[2]);
+      acc[3] = fmaf(c.y, f, acc[3]);
+    }
   }
   T* o = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)h * dp.out_stride_head + d;
   *reinterpret_cast<uint2*>(o) = make_uint2(pack2<T>(acc[0] * inv, acc[1] * inv), pack2<T>(acc[2] * inv, acc[3] * inv));
