@@ -23,9 +23,11 @@
 //     O += P V: 2 MMAs (M 128, N 256, K 16), V = the tile's latent columns
 //       [256 dh, 256 dh + 256) read MN-major from the same staged rows.
 //   Pipeline: the producer refills a stage once O += P V of its previous tile
-//   has completed; the MMA warp issues S of tile t (into S buffer t & 1)
-//   before O += P V of tile t - 1, so the tensor core computes the next
-//   scores while the softmax warps work on the current ones.  Handshakes are
+//   has completed; the MMA warp issues, whichever is ready first, O += P V of
+//   the oldest tile whose P is written (it frees a stage) or S of the next
+//   staged tile (into S buffer t & 1, at most two ahead), so the tensor core
+//   computes the next scores while the softmax warps work on the current
+//   ones and no load waits behind a later tile's data.  Handshakes are
 //   mbarriers (tcgen05.commit for the tensor core), every wait is bounded
 //   (about a second) and ends early once another role gave up, and TMEM is
 //   released on every path.
@@ -295,13 +297,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           last_bar = smem_u32(&C.o_done);
           last_parity = t & 1;
         };
-        for (int t = 0; ok && t < n_tiles; ++t) {
-          const int st = t % kStages, sb = t & 1;
-          ok = role_wait(C, smem_u32(&C.full[st]), (t / kStages) & 1) &&
-               (t < 2 || role_wait(C, smem_u32(&C.s_empty[sb]), ((t >> 1) - 1) & 1));
-          if (!ok) break;
-          // S = Q K^T into S buffer sb
-          const uint8_t* stage = kv_s + st * kTileBytes;
+        auto issue_s = [&](int t) {  // S = Q K^T of tile t into S buffer t & 1
+          const int sb = t & 1;
+          const uint8_t* stage = kv_s + (t % kStages) * kTileBytes;
           tc_fence_after();
 #pragma unroll 1
           for (int kb = 0; kb < kKB; ++kb) {
@@ -315,16 +313,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(smem_u32(&C.s_full[sb]));
           last_bar = smem_u32(&C.s_full[sb]);
           last_parity = (t >> 1) & 1;
-          // O += P V of the previous tile, once its P is written
-          if (t >= 1) {
-            ok = role_wait(C, smem_u32(&C.p_full), (t - 1) & 1);
-            if (!ok) break;
-            issue_pv(t - 1);
+        };
+        // Issue whichever is ready: O += P V of the oldest tile whose P is written
+        // (it frees a stage for the producer), else S of the next staged tile (at
+        // most two S buffers ahead of O += P V).
+        int ns = 0, np = 0;
+        long long idle_since = clock64();
+        while (ok && np < n_tiles) {
+          bool progressed = false;
+          if (np < ns && mbar_try_wait(smem_u32(&C.p_full), np & 1)) {
+            issue_pv(np++);
+            progressed = true;
+          } else if (ns < n_tiles && ns <= np + 1 &&
+                     mbar_try_wait(smem_u32(&C.full[ns % kStages]), (ns / kStages) & 1) &&
+                     (ns < 2 || mbar_try_wait(smem_u32(&C.s_empty[ns & 1]), ((ns >> 1) - 1) & 1))) {
+            issue_s(ns++);
+            progressed = true;
           }
-        }
-        if (ok) {
-          ok = role_wait(C, smem_u32(&C.p_full), (n_tiles - 1) & 1);
-          if (ok) issue_pv(n_tiles - 1);
+          if (progressed) {
+            idle_since = clock64();
+          } else if (*reinterpret_cast<const volatile int32_t*>(&C.abort) || clock64() - idle_since > kWaitTicks) {
+            ok = false;
+          }
         }
         if (!ok) {
           give_up(C, dp.err);
