@@ -6,32 +6,31 @@
 // [n x 576] (latent 512 | rope 64), output [128 x 512] over the first 512
 // columns of the same rows.  The 128 heads are exactly the M = 128 of one
 // tcgen05.mma, so:
-//   CTA = (split s, output quarter dq, sequence b), 6 warps: warps 0-3 softmax
+//   CTA = (split s, output half dh, sequence b), 6 warps: warps 0-3 softmax
 //   (thread = head row = TMEM lane), warp 4 TMA producer, warp 5 MMA issuer.
-//   TMEM (512 columns): the latent part of Q as bf16 pairs (256 columns, the
-//     A operand of the score MMAs: read from TMEM, not re-read from shared
-//     memory by every MMA), O [128 x 128] f32 (this CTA's quarter of the
-//     output dims), two S buffers [128 x 32] f32.
-//   Shared memory (1024-aligned, 128-byte swizzle, written by TMA): the rope
-//     part of Q [128 x 64]; 5 stages of 32 attended rows, 9 k-blocks x
-//     [32 rows x 64] = 36 KB each; P [128 x 32] bf16 (64-byte swizzle).
+//   Shared memory (1024-aligned, 128-byte swizzle, written by TMA):
+//     Q: 9 k-blocks x [128 rows x 64] = 144 KB, resident;
+//     2 stages of 32 attended rows: 9 k-blocks x [32 rows x 64] = 36 KB each;
+//     P: [128 x 32] bf16, 64-byte swizzle, written by the softmax threads.
+//   TMEM (512 columns): O [128 x 256] f32 at column 0 (this CTA's half of the
+//     512 output dims), two S buffers [128 x 32] f32 at columns 256 and 288.
 //   Per tile of 32 tokens (half a block):
-//     S = Q K^T: 32 MMAs with A in TMEM (latent) + 4 with A in shared memory
-//       (rope), M 128, N 32, K 16;
+//     S = Q K^T: 36 MMAs (M 128, N 32, K 16), K-major operands;
 //     softmax: each thread loads its row of S from TMEM, masks the tokens
 //       outside the selection, keeps a reference maximum that is raised only
 //       when a score exceeds it by 2^8 (then O's row is rescaled in TMEM), and
 //       writes P = exp2(s - m) as bf16 into shared memory;
-//     O += P V: 2 MMAs (M 128, N 128, K 16), V = the tile's latent columns
-//       [128 dq, 128 dq + 128) read MN-major from the same staged rows.
+//     O += P V: 2 MMAs (M 128, N 256, K 16), V = the tile's latent columns
+//       [256 dh, 256 dh + 256) read MN-major from the same staged rows.
 //   Pipeline: the producer refills a stage once O += P V of its previous tile
 //   has completed; the MMA warp issues, whichever is ready first, O += P V of
 //   the oldest tile whose P is written (it frees a stage) or S of the next
 //   staged tile (into S buffer t & 1, at most two ahead), so the tensor core
 //   computes the next scores while the softmax warps work on the current
-//   ones.  Handshakes are mbarriers (tcgen05.commit for the tensor core), every
-//   wait is bounded (about a second) and ends early once another role gave
-//   up, and TMEM is released on every path.
+//   ones and no load waits behind a later tile's data.  Handshakes are
+//   mbarriers (tcgen05.commit for the tensor core), every wait is bounded
+//   (about a second) and ends early once another role gave up, and TMEM is
+//   released on every path.
 // Splits write fp32 partials (max, sum, unnormalised output) in the layout of
 // the paged GQA decode; a second kernel merges them over all (sequence, head)
 // rows in parallel.
@@ -58,19 +57,18 @@ constexpr int kR = 512, kP = 64;
 constexpr int kKB = (kR + kP) / 64;                     // 9 k-blocks of 64 elements
 constexpr int kBs = 64;                                 // block (chunk) size
 constexpr int kTok = 32;                                // tokens per tile
-constexpr int kParts = 4;                               // output dims split over CTAs
-constexpr int kDQ = kR / kParts;                        // output dims per CTA: 128
+constexpr int kDH = kR / 2;                             // output dims per CTA
 constexpr int kSoftmaxThreads = 128;                    // warps 0-3: one head row per thread
 constexpr int kProducerWarp = 4, kMmaWarp = 5;
 constexpr int kThreads = 192;
-constexpr uint32_t kQpeBytes = kH * 128;                // rope part of Q: [128 rows x 64], 16 KB
+constexpr uint32_t kQBlock = kH * 128;                  // one k-block of Q: 16 KB
+constexpr uint32_t kQBytes = kKB * kQBlock;             // 144 KB
 constexpr uint32_t kTBlock = kTok * 128;                // one k-block of a tile: 4 KB
 constexpr uint32_t kTileBytes = kKB * kTBlock;          // 36 KB
 constexpr uint32_t kPBytes = kH * kTok * 2;             // 8 KB
-constexpr int kStages = 5;
+constexpr int kStages = 2;
 constexpr int kBits = 4096;                             // chunks per sequence (bitmaps)
-// TMEM columns: Q latent part (bf16 pairs), O (f32), two S buffers (f32)
-constexpr uint32_t kTmemCols = 512, kColQ = 0, kColO = kR / 2, kColS = kColO + kDQ;
+constexpr uint32_t kTmemCols = 512, kColO = 0, kColS = 256;
 constexpr float kRescale = 8.f;                         // log2 headroom of the reference maximum
 
 struct Ctrl {
@@ -78,8 +76,7 @@ struct Ctrl {
   uint64_t empty[kStages];   // MMA commit after O += P V: stage free
   uint64_t s_full[2];        // MMA commit after S = Q K^T: S buffer ready
   uint64_t s_empty[2];       // softmax threads: S buffer read
-  uint64_t q_full;           // producer: rope part of Q staged
-  uint64_t qt_full;          // softmax threads: latent part of Q stored in TMEM
+  uint64_t q_full;
   uint64_t p_full;           // softmax threads: P written (and O rescaled)
   uint64_t o_done;           // MMA commit after O += P V
   uint32_t tmem_base;
@@ -92,7 +89,7 @@ struct Ctrl {
   int32_t word_pre[kBits / 32 + 1];
 };
 
-constexpr size_t kSmemBytes = 1024 + kQpeBytes + kStages * kTileBytes + kPBytes + sizeof(Ctrl);
+constexpr size_t kSmemBytes = 1024 + kQBytes + kStages * kTileBytes + kPBytes + sizeof(Ctrl);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 __device__ __forceinline__ int chunk_of_rank(const Ctrl& C, int words, int rank) {
@@ -142,21 +139,22 @@ __device__ __forceinline__ void give_up(Ctrl& C, int32_t* err) {
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
-    sparse_mla_umma_kernel(const __grid_constant__ CUtensorMap qpe_map, const __grid_constant__ CUtensorMap lat_map,
-                           const __grid_constant__ CUtensorMap rope_map, SparseParams p) {
+    sparse_mla_umma_kernel(const __grid_constant__ CUtensorMap qlat_map, const __grid_constant__ CUtensorMap qpe_map,
+                           const __grid_constant__ CUtensorMap lat_map, const __grid_constant__ CUtensorMap rope_map,
+                           SparseParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* qpe_s = base;
-  uint8_t* kv_s = qpe_s + kQpeBytes;
+  uint8_t* q_s = base;
+  uint8_t* kv_s = q_s + kQBytes;
   uint8_t* p_s = kv_s + kStages * kTileBytes;
   Ctrl& C = *reinterpret_cast<Ctrl*>(p_s + kPBytes);
 
-  const int s = blockIdx.x, dq = blockIdx.y, b = blockIdx.z;
+  const int s = blockIdx.x, dh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = idesc_f16(kBf16, kH, kTok, false, false);
-  constexpr uint32_t kIdescPV = idesc_f16(kBf16, kH, kDQ, false, true);
+  constexpr uint32_t kIdescPV = idesc_f16(kBf16, kH, kDH, false, true);
   const DecodeParams& dp = p.dp;
 
   if (tid == 0) {
@@ -167,7 +165,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&C.s_empty[i]), kSoftmaxThreads);
     }
     mbar_init(smem_u32(&C.q_full), 1);
-    mbar_init(smem_u32(&C.qt_full), kSoftmaxThreads);
     mbar_init(smem_u32(&C.p_full), kSoftmaxThreads);
     mbar_init(smem_u32(&C.o_done), 1);
     C.abort = 0;
@@ -183,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (len < 0) len = 0;
   int n_chunks = (len + kBs - 1) / kBs;
   if (n_chunks > kBits) {
-    if (tid == 0 && s == 0 && dq == 0) flag_error(dp.err, SNAPMIND_DEVERR_TABLE);
+    if (tid == 0 && s == 0 && dh == 0) flag_error(dp.err, SNAPMIND_DEVERR_TABLE);
     n_chunks = kBits;
     len = kBits * kBs;
   }
@@ -242,9 +239,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------------------------------------------------------- TMA producer
       if (lane == 0) {
         const uint32_t qb = smem_u32(&C.q_full);
-        mbar_arrive_expect_tx(qb, kQpeBytes);
-        tma_load_2d(smem_u32(qpe_s), &qpe_map, 0, b * kH, qb);
-        // block of tile t (resolved before its stage frees up)
+        mbar_arrive_expect_tx(qb, kQBytes);
+#pragma unroll
+        for (int kb = 0; kb < kKB - 1; ++kb)
+          tma_load_2d(smem_u32(q_s + kb * kQBlock), &qlat_map, kb * 64, b * kH, qb);
+        tma_load_2d(smem_u32(q_s + (kKB - 1) * kQBlock), &qpe_map, 0, b * kH, qb);
+        // block of tile t, resolved before its stage frees up
         auto locate = [&](int t, int& c, int32_t& phys) {
           c = chunk_of_rank(C, words, (u_lo + t) >> 1);
           phys = c < p.table_width ? p.tables[(int64_t)b * p.table_stride + c] : -1;
@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kMmaWarp) {
       // ---------------------------------------------------------------- MMA issuer
       if (lane == 0) {
-        bool ok = role_wait(C, smem_u32(&C.q_full), 0) && role_wait(C, smem_u32(&C.qt_full), 0);
+        bool ok = role_wait(C, smem_u32(&C.q_full), 0);
         uint32_t last_bar = 0, last_parity = 0;  // the latest commit: covers every MMA issued
         auto issue_pv = [&](int t) {  // O += P V of tile t
           const uint8_t* stage = kv_s + (t % kStages) * kTileBytes;
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int ks = 0; ks < kTok / 16; ++ks) {
             const uint64_t ad = smem_desc(smem_u32(p_s + ks * 32), 16, 512, kSwizzle64B);
             const uint64_t bd =
-                smem_desc(smem_u32(stage + dq * 2 * kTBlock + ks * 16 * 128), kTBlock, 1024, kSwizzle128B);
+                smem_desc(smem_u32(stage + dh * 4 * kTBlock + ks * 16 * 128), kTBlock, 1024, kSwizzle128B);
             umma_f16(tmem + kColO, ad, bd, kIdescPV, (t > 0 || ks > 0) ? 1u : 0u);
           }
           umma_commit(smem_u32(&C.empty[t % kStages]));
@@ -305,46 +305,47 @@ __global__ void __launch_bounds__(kThreads, 1)
           last_bar = smem_u32(&C.o_done);
           last_parity = t & 1;
         };
-        auto issue_s = [&](int t) {  // S = Q K^T of tile t into S buffer t & 1
+        // S = Q K^T of tile t into S buffer t & 1, one k-block (4 MMAs) per call
+        auto issue_s_block = [&](int t, int kb) {
           const int sb = t & 1;
           const uint8_t* stage = kv_s + (t % kStages) * kTileBytes;
-          const uint32_t d = tmem + kColS + sb * kTok;
-          tc_fence_after();
-          // latent dims: A = Q from TMEM (8 columns per K step of 16)
-#pragma unroll 1
-          for (int kb = 0; kb < kKB - 1; ++kb) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t bd = smem_desc(smem_u32(stage + kb * kTBlock + kk * 32), 16, 1024, kSwizzle128B);
-              umma_f16_ts(d, tmem + kColQ + kb * 32 + kk * 8, bd, kIdescS, (kb | kk) != 0);
-            }
-          }
-          // rope dims: A = the rope part of Q from shared memory
+          if (kb == 0) tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = smem_desc(smem_u32(qpe_s + kk * 32), 16, 1024, kSwizzle128B);
-            const uint64_t bd =
-                smem_desc(smem_u32(stage + (kKB - 1) * kTBlock + kk * 32), 16, 1024, kSwizzle128B);
-            umma_f16(d, ad, bd, kIdescS, 1u);
+            const uint64_t ad = smem_desc(smem_u32(q_s + kb * kQBlock + kk * 32), 16, 1024, kSwizzle128B);
+            const uint64_t bd = smem_desc(smem_u32(stage + kb * kTBlock + kk * 32), 16, 1024, kSwizzle128B);
+            umma_f16(tmem + kColS + sb * kTok, ad, bd, kIdescS, (kb | kk) != 0);
           }
-          umma_commit(smem_u32(&C.s_full[sb]));
-          last_bar = smem_u32(&C.s_full[sb]);
-          last_parity = (t >> 1) & 1;
+          if (kb == kKB - 1) {
+            umma_commit(smem_u32(&C.s_full[sb]));
+            last_bar = smem_u32(&C.s_full[sb]);
+            last_parity = (t >> 1) & 1;
+          }
         };
         // Issue whichever is ready: O += P V of the oldest tile whose P is written
-        // (it frees a stage for the producer), else S of the next staged tile (at
-        // most two S buffers ahead of O += P V).
-        int ns = 0, np = 0;
+        // (it frees a stage for the producer), else the next k-block of the score
+        // MMAs in progress, else start S of the next staged tile (at most two S
+        // buffers ahead of O += P V).  Issuing S a k-block at a time keeps a
+        // ready O += P V from queueing behind a whole tile of score MMAs.
+        int ns = 0, s_kb = 0, np = 0;  // ns: tile whose S is being issued (s_kb k-blocks done)
         long long idle_since = clock64();
         while (ok && np < n_tiles) {
           bool progressed = false;
           if (np < ns && mbar_try_wait(smem_u32(&C.p_full), np & 1)) {
             issue_pv(np++);
             progressed = true;
+          } else if (s_kb > 0) {
+            issue_s_block(ns, s_kb);
+            if (++s_kb == kKB) {
+              s_kb = 0;
+              ++ns;
+            }
+            progressed = true;
           } else if (ns < n_tiles && ns <= np + 1 &&
                      mbar_try_wait(smem_u32(&C.full[ns % kStages]), (ns / kStages) & 1) &&
                      (ns < 2 || mbar_try_wait(smem_u32(&C.s_empty[ns & 1]), ((ns >> 1) - 1) & 1))) {
-            issue_s(ns++);
+            issue_s_block(ns, 0);
+            s_kb = 1;
             progressed = true;
           }
           if (progressed) {
@@ -365,26 +366,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float c2 = p.scale * 1.4426950408889634f;
       float m_ref = -INFINITY, l_run = 0.f;  // log2 units of score * scale
       bool ok = true;
-      {  // this head's latent query row into its TMEM lane: 512 elements = 256 columns
-        const uint4* qrow = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.q_lat) +
-                                                           ((int64_t)b * kH + head) * kR);
-#pragma unroll 1
-        for (int j = 0; j < kR / 64; ++j) {
-          uint32_t w[32];
-#pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            const uint4 x = __ldg(qrow + j * 8 + v);
-            w[4 * v] = x.x;
-            w[4 * v + 1] = x.y;
-            w[4 * v + 2] = x.z;
-            w[4 * v + 3] = x.w;
-          }
-          tmem_st32u(t_row + kColQ + 32 * j, w);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(smem_u32(&C.qt_full));
-      }
       for (int t = 0; t < n_tiles; ++t) {
         const int st = t % kStages, sb = t & 1;
         ok = role_wait(C, smem_u32(&C.full[st]), (t / kStages) & 1) &&
@@ -457,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // O rows of this warp at the old reference maximum: rescale in TMEM
           const float alpha = (raise && m_old != -INFINITY) ? exp2f(m_old - m_ref) : 1.f;
 #pragma unroll 1
-          for (int cc = 0; cc < kDQ; cc += 32) {
+          for (int cc = 0; cc < kDH; cc += 32) {
             float o[32];
             tmem_ld32(t_row + kColO + cc, o);
             tmem_wait_ld();
@@ -480,8 +461,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (good < kTok) {  // rows holding no token: zero this CTA's V columns (S of the tile is done)
           uint8_t* stage = kv_s + st * kTileBytes;
           const int rows = kTok - good;
-          for (int e = tid; e < 2 * rows * 8; e += kSoftmaxThreads) {
-            const int kb = dq * 2 + e / (rows * 8);
+          for (int e = tid; e < 4 * rows * 8; e += kSoftmaxThreads) {
+            const int kb = dh * 4 + e / (rows * 8);
             const int r = good + (e / 8) % rows;
             *reinterpret_cast<uint4*>(stage + kb * kTBlock + r * 128 + (e & 7) * 16) = make_uint4(0, 0, 0, 0);
           }
@@ -502,9 +483,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
         float* part = dp.partials + (((int64_t)b * dp.n_q_heads + head) * dp.max_splits + s) * (kR + 2);
         T* orow = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq +
-                  (int64_t)head * dp.out_stride_head + dq * kDQ;
+                  (int64_t)head * dp.out_stride_head + dh * kDH;
 #pragma unroll 1
-        for (int cc = 0; cc < kDQ; cc += 32) {
+        for (int cc = 0; cc < kDH; cc += 32) {
           float o[32];
           tmem_ld32(t_row + kColO + cc, o);
           tmem_wait_ld();
@@ -517,10 +498,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
 #pragma unroll
             for (int j = 0; j < 32; j += 2)
-              *reinterpret_cast<float2*>(part + 2 + dq * kDQ + cc + j) = make_float2(o[j], o[j + 1]);
+              *reinterpret_cast<float2*>(part + 2 + dh * kDH + cc + j) = make_float2(o[j], o[j + 1]);
           }
         }
-        if (!direct && dq == 0) {
+        if (!direct && dh == 0) {
           part[0] = m_ref == -INFINITY ? -INFINITY : m_ref * 0.6931471805599453f;  // natural-log units
           part[1] = l_run;
         }
@@ -531,9 +512,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int head = tid;
     if (direct) {
       T* o = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)head * dp.out_stride_head +
-             dq * kDQ;
-      for (int d = 0; d < kDQ; d += 8) *reinterpret_cast<uint4*>(o + d) = make_uint4(0, 0, 0, 0);
-    } else if (dq == 0) {
+             dh * kDH;
+      for (int d = 0; d < kDH; d += 8) *reinterpret_cast<uint4*>(o + d) = make_uint4(0, 0, 0, 0);
+    } else if (dh == 0) {
       float* part = dp.partials + (((int64_t)b * dp.n_q_heads + head) * dp.max_splits + s) * (kR + 2);
       part[0] = -INFINITY;
       part[1] = 0.f;
@@ -600,7 +581,7 @@ __global__ void __launch_bounds__(256) sparse_mla_merge_kernel(DecodeParams dp, 
 }  // namespace
 
 int sparse_mla_umma_splits(int batch) {
-  const int per_seq = num_sms() / (kParts * (batch > 0 ? batch : 1));
+  const int per_seq = num_sms() / (2 * (batch > 0 ? batch : 1));
   return per_seq < 1 ? 1 : (per_seq > 64 ? 64 : per_seq);
 }
 
@@ -613,9 +594,10 @@ bool sparse_mla_umma_supported(const SparseParams& p, int dtype) {
 
 int launch_sparse_mla_umma(const SparseParams& p, int dtype, cudaStream_t st) {
   const bool bf16 = dtype == SNAPMIND_DTYPE_BF16;
-  CUtensorMap qpe, lat, rope;
+  CUtensorMap qlat, qpe, lat, rope;
   const uint64_t rows = (uint64_t)p.num_blocks * kBs;
-  if (!tensor_map_2d(&qpe, bf16, p.q_pe, kP, (uint64_t)p.batch * kH, kP * 2, 64, kH) ||
+  if (!tensor_map_2d(&qlat, bf16, p.q_lat, kR, (uint64_t)p.batch * kH, kR * 2, 64, kH) ||
+      !tensor_map_2d(&qpe, bf16, p.q_pe, kP, (uint64_t)p.batch * kH, kP * 2, 64, kH) ||
       !tensor_map_2d(&lat, bf16, p.latent, kR, rows, kR * 2, 64, kTok) ||
       !tensor_map_2d(&rope, bf16, p.rope, kP, rows, kP * 2, 64, kTok)) {
     set_last_error("sparse_mla_umma: tensor map encoding failed");
@@ -628,7 +610,7 @@ int launch_sparse_mla_umma(const SparseParams& p, int dtype, cudaStream_t st) {
       if (e != cudaSuccess) return cuda_status(e, "sparse_mla_umma smem attribute");
       attr = true;
     }
-    kernel<<<dim3(p.n_splits, kParts, p.batch), kThreads, kSmemBytes, st>>>(qpe, lat, rope, p);
+    kernel<<<dim3(p.n_splits, 2, p.batch), kThreads, kSmemBytes, st>>>(qlat, qpe, lat, rope, p);
     int rc = cuda_status(cudaGetLastError(), "sparse_mla_umma launch");
     if (rc != SNAPMIND_OK || p.n_splits == 1) return rc;
     merge<<<dim3(p.batch * kH * 4 / 8), 256, 0, st>>>(p.dp, p.n_splits);
