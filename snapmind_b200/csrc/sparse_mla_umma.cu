@@ -305,47 +305,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           last_bar = smem_u32(&C.o_done);
           last_parity = t & 1;
         };
-        // S = Q K^T of tile t into S buffer t & 1, one k-block (4 MMAs) per call
-        auto issue_s_block = [&](int t, int kb) {
+        auto issue_s = [&](int t) {  // S = Q K^T of tile t into S buffer t & 1
           const int sb = t & 1;
           const uint8_t* stage = kv_s + (t % kStages) * kTileBytes;
-          if (kb == 0) tc_fence_after();
+          tc_fence_after();
+#pragma unroll 1
+          for (int kb = 0; kb < kKB; ++kb) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = smem_desc(smem_u32(q_s + kb * kQBlock + kk * 32), 16, 1024, kSwizzle128B);
-            const uint64_t bd = smem_desc(smem_u32(stage + kb * kTBlock + kk * 32), 16, 1024, kSwizzle128B);
-            umma_f16(tmem + kColS + sb * kTok, ad, bd, kIdescS, (kb | kk) != 0);
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = smem_desc(smem_u32(q_s + kb * kQBlock + kk * 32), 16, 1024, kSwizzle128B);
+              const uint64_t bd = smem_desc(smem_u32(stage + kb * kTBlock + kk * 32), 16, 1024, kSwizzle128B);
+              umma_f16(tmem + kColS + sb * kTok, ad, bd, kIdescS, (kb | kk) != 0);
+            }
           }
-          if (kb == kKB - 1) {
-            umma_commit(smem_u32(&C.s_full[sb]));
-            last_bar = smem_u32(&C.s_full[sb]);
-            last_parity = (t >> 1) & 1;
-          }
+          umma_commit(smem_u32(&C.s_full[sb]));
+          last_bar = smem_u32(&C.s_full[sb]);
+          last_parity = (t >> 1) & 1;
         };
         // Issue whichever is ready: O += P V of the oldest tile whose P is written
-        // (it frees a stage for the producer), else the next k-block of the score
-        // MMAs in progress, else start S of the next staged tile (at most two S
-        // buffers ahead of O += P V).  Issuing S a k-block at a time keeps a
-        // ready O += P V from queueing behind a whole tile of score MMAs.
-        int ns = 0, s_kb = 0, np = 0;  // ns: tile whose S is being issued (s_kb k-blocks done)
+        // (it frees a stage for the producer), else S of the next staged tile (at
+        // most two S buffers ahead of O += P V).
+        int ns = 0, np = 0;
         long long idle_since = clock64();
         while (ok && np < n_tiles) {
           bool progressed = false;
           if (np < ns && mbar_try_wait(smem_u32(&C.p_full), np & 1)) {
             issue_pv(np++);
             progressed = true;
-          } else if (s_kb > 0) {
-            issue_s_block(ns, s_kb);
-            if (++s_kb == kKB) {
-              s_kb = 0;
-              ++ns;
-            }
-            progressed = true;
           } else if (ns < n_tiles && ns <= np + 1 &&
                      mbar_try_wait(smem_u32(&C.full[ns % kStages]), (ns / kStages) & 1) &&
                      (ns < 2 || mbar_try_wait(smem_u32(&C.s_empty[ns & 1]), ((ns >> 1) - 1) & 1))) {
-            issue_s_block(ns, 0);
-            s_kb = 1;
+            issue_s(ns++);
             progressed = true;
           }
           if (progressed) {
