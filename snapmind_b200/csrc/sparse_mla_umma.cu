@@ -70,6 +70,11 @@ constexpr int kStages = 2;
 constexpr int kBits = 4096;                             // chunks per sequence (bitmaps)
 constexpr uint32_t kTmemCols = 512, kColO = 0, kColS = 256;
 constexpr float kRescale = 8.f;                         // log2 headroom of the reference maximum
+// The two stages interleave per k-block: k-block kb of stage st at
+// kb * kKBStride + st * kTBlock, so the 64 rows of a stage pair are contiguous
+// in every k-block and one N = 64 MMA scores two tiles.
+constexpr uint32_t kKBStride = kStages * kTBlock;
+static_assert(kStages == 2, "tiles are scored in pairs of stages");
 
 struct Ctrl {
   uint64_t full[kStages];    // producer -> MMA, softmax: tile staged
@@ -154,6 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = idesc_f16(kBf16, kH, kTok, false, false);
+  constexpr uint32_t kIdescS2 = idesc_f16(kBf16, kH, 2 * kTok, false, false);
   constexpr uint32_t kIdescPV = idesc_f16(kBf16, kH, kDH, false, true);
   const DecodeParams& dp = p.dp;
 
@@ -270,12 +276,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(bar);
           } else {
             mbar_arrive_expect_tx(bar, kTileBytes);
-            uint8_t* stage = kv_s + st * kTileBytes;
+            uint8_t* stage = kv_s + st * kTBlock;
             const int y = phys * kBs + ((u_lo + t) & 1) * kTok;
 #pragma unroll
             for (int kb = 0; kb < kKB - 1; ++kb)
-              tma_load_2d(smem_u32(stage + kb * kTBlock), &lat_map, kb * 64, y, bar);
-            tma_load_2d(smem_u32(stage + (kKB - 1) * kTBlock), &rope_map, 0, y, bar);
+              tma_load_2d(smem_u32(stage + kb * kKBStride), &lat_map, kb * 64, y, bar);
+            tma_load_2d(smem_u32(stage + (kKB - 1) * kKBStride), &rope_map, 0, y, bar);
           }
           issued = t + 1;
           if (t + 1 < n_tiles) locate(t + 1, c_next, phys_next);
@@ -291,13 +297,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = role_wait(C, smem_u32(&C.q_full), 0);
         uint32_t last_bar = 0, last_parity = 0;  // the latest commit: covers every MMA issued
         auto issue_pv = [&](int t) {  // O += P V of tile t
-          const uint8_t* stage = kv_s + (t % kStages) * kTileBytes;
+          const uint8_t* stage = kv_s + (t % kStages) * kTBlock;
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < kTok / 16; ++ks) {
             const uint64_t ad = smem_desc(smem_u32(p_s + ks * 32), 16, 512, kSwizzle64B);
             const uint64_t bd =
-                smem_desc(smem_u32(stage + dh * 4 * kTBlock + ks * 16 * 128), kTBlock, 1024, kSwizzle128B);
+                smem_desc(smem_u32(stage + dh * 4 * kKBStride + ks * 16 * 128), kKBStride, 1024, kSwizzle128B);
             umma_f16(tmem + kColO, ad, bd, kIdescPV, (t > 0 || ks > 0) ? 1u : 0u);
           }
           umma_commit(smem_u32(&C.empty[t % kStages]));
@@ -305,21 +311,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           last_bar = smem_u32(&C.o_done);
           last_parity = t & 1;
         };
-        auto issue_s = [&](int t) {  // S = Q K^T of tile t into S buffer t & 1
-          const int sb = t & 1;
-          const uint8_t* stage = kv_s + (t % kStages) * kTileBytes;
+        // S = Q K^T of tile t (even, stage 0) into S buffer 0, and of tile t + 1
+        // (stage 1) into S buffer 1 with the same MMAs (N = 64) when `pair`
+        auto issue_s = [&](int t, bool pair) {
+          const uint32_t idesc = pair ? kIdescS2 : kIdescS;
           tc_fence_after();
 #pragma unroll 1
           for (int kb = 0; kb < kKB; ++kb) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t ad = smem_desc(smem_u32(q_s + kb * kQBlock + kk * 32), 16, 1024, kSwizzle128B);
-              const uint64_t bd = smem_desc(smem_u32(stage + kb * kTBlock + kk * 32), 16, 1024, kSwizzle128B);
-              umma_f16(tmem + kColS + sb * kTok, ad, bd, kIdescS, (kb | kk) != 0);
+              const uint64_t bd = smem_desc(smem_u32(kv_s + kb * kKBStride + kk * 32), 16, 1024, kSwizzle128B);
+              umma_f16(tmem + kColS, ad, bd, idesc, (kb | kk) != 0);
             }
           }
-          umma_commit(smem_u32(&C.s_full[sb]));
-          last_bar = smem_u32(&C.s_full[sb]);
+          umma_commit(smem_u32(&C.s_full[0]));
+          if (pair) umma_commit(smem_u32(&C.s_full[1]));
+          last_bar = smem_u32(&C.s_full[pair ? 1 : 0]);
           last_parity = (t >> 1) & 1;
         };
         // Issue whichever is ready: O += P V of the oldest tile whose P is written
@@ -332,11 +340,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (np < ns && mbar_try_wait(smem_u32(&C.p_full), np & 1)) {
             issue_pv(np++);
             progressed = true;
-          } else if (ns < n_tiles && ns <= np + 1 &&
-                     mbar_try_wait(smem_u32(&C.full[ns % kStages]), (ns / kStages) & 1) &&
-                     (ns < 2 || mbar_try_wait(smem_u32(&C.s_empty[ns & 1]), ((ns >> 1) - 1) & 1))) {
-            issue_s(ns++);
-            progressed = true;
+          } else if (ns < n_tiles) {
+            // tiles ns (even) and ns + 1 once both are staged and both S buffers were read
+            const bool pair = ns + 1 < n_tiles;
+            const uint32_t par = (ns >> 1) & 1, prev = ((ns >> 1) - 1) & 1;
+            if (mbar_try_wait(smem_u32(&C.full[0]), par) && (!pair || mbar_try_wait(smem_u32(&C.full[1]), par)) &&
+                (ns < 2 || (mbar_try_wait(smem_u32(&C.s_empty[0]), prev) &&
+                            mbar_try_wait(smem_u32(&C.s_empty[1]), prev)))) {
+              issue_s(ns, pair);
+              ns += pair ? 2 : 1;
+              progressed = true;
+            }
           }
           if (progressed) {
             idle_since = clock64();
@@ -449,12 +463,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]);
         }
         if (good < kTok) {  // rows holding no token: zero this CTA's V columns (S of the tile is done)
-          uint8_t* stage = kv_s + st * kTileBytes;
+          uint8_t* stage = kv_s + st * kTBlock;
           const int rows = kTok - good;
           for (int e = tid; e < 4 * rows * 8; e += kSoftmaxThreads) {
             const int kb = dh * 4 + e / (rows * 8);
             const int r = good + (e / 8) % rows;
-            *reinterpret_cast<uint4*>(stage + kb * kTBlock + r * 128 + (e & 7) * 16) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(stage + kb * kKBStride + r * 128 + (e & 7) * 16) = make_uint4(0, 0, 0, 0);
           }
         }
         fence_proxy_async_smem();
