@@ -10,27 +10,30 @@
 //   (thread = head row = TMEM lane), warp 4 TMA producer, warp 5 MMA issuer.
 //   Shared memory (1024-aligned, 128-byte swizzle, written by TMA):
 //     Q: 9 k-blocks x [128 rows x 64] = 144 KB, resident;
-//     2 stages of 32 attended rows: 9 k-blocks x [32 rows x 64] = 36 KB each;
+//     one attended chunk (block) of 64 rows as two 32-row stages,
+//       9 k-blocks x [64 rows x 64] (72 KB, one TMA box per k-block);
 //     P: [128 x 32] bf16, 64-byte swizzle, written by the softmax threads.
 //   TMEM (512 columns): O [128 x 256] f32 at column 0 (this CTA's half of the
-//     512 output dims), two S buffers [128 x 32] f32 at columns 256 and 288.
-//   Per tile of 32 tokens (half a block):
-//     S = Q K^T: 36 MMAs (M 128, N 32, K 16), K-major operands;
-//     softmax: each thread loads its row of S from TMEM, masks the tokens
-//       outside the selection, keeps a reference maximum that is raised only
-//       when a score exceeds it by 2^8 (then O's row is rescaled in TMEM), and
-//       writes P = exp2(s - m) as bf16 into shared memory;
-//     O += P V: 2 MMAs (M 128, N 256, K 16), V = the tile's latent columns
-//       [256 dh, 256 dh + 256) read MN-major from the same staged rows.
-//   Pipeline: the producer refills a stage once O += P V of its previous tile
-//   has completed; the MMA warp issues, whichever is ready first, O += P V of
-//   the oldest tile whose P is written (it frees a stage) or S of the next
-//   staged tile (into S buffer t & 1, at most two ahead), so the tensor core
-//   computes the next scores while the softmax warps work on the current
-//   ones and no load waits behind a later tile's data.  Handshakes are
-//   mbarriers (tcgen05.commit for the tensor core), every wait is bounded
-//   (about a second) and ends early once another role gave up, and TMEM is
-//   released on every path.
+//     512 output dims); the scores of a chunk [128 x 64] f32 as two
+//     accumulator chains (even and odd k-blocks) at columns 256 and 320.
+//   Per chunk of 64 tokens (two tiles of 32):
+//     S = Q K^T: 36 MMAs (M 128, N 64, K 16), K-major operands, alternating
+//       between the two chains so consecutive MMAs do not wait on one
+//       accumulator;
+//     softmax, per tile: each thread loads and adds its row of both chains
+//       from TMEM, masks the tokens outside the selection, keeps a reference
+//       maximum that is raised only when a score exceeds it by 2^8 (then O's
+//       row is rescaled in TMEM), and writes P = exp2(s - m) as bf16 into
+//       shared memory;
+//     O += P V per tile: 2 MMAs (M 128, N 256, K 16), V = the tile's latent
+//       columns [256 dh, 256 dh + 256) read MN-major from the staged rows.
+//   Pipeline: the producer loads the next chunk once O += P V of the current
+//   chunk's second tile has completed, resolving its block id beforehand; the
+//   MMA warp polls (non-blocking) and issues whichever is ready first: O += P V
+//   of the oldest tile whose P is written, or S of the next staged chunk.
+//   Handshakes are mbarriers (tcgen05.commit for the tensor core), every wait
+//   is bounded (about a second) and ends early once another role gave up, and
+//   TMEM is released on every path.
 // Splits write fp32 partials (max, sum, unnormalised output) in the layout of
 // the paged GQA decode; a second kernel merges them over all (sequence, head)
 // rows in parallel.
@@ -68,7 +71,8 @@ constexpr uint32_t kTileBytes = kKB * kTBlock;          // 36 KB
 constexpr uint32_t kPBytes = kH * kTok * 2;             // 8 KB
 constexpr int kStages = 2;
 constexpr int kBits = 4096;                             // chunks per sequence (bitmaps)
-constexpr uint32_t kTmemCols = 512, kColO = 0, kColS = 256;
+// TMEM columns: O (f32) at 0; the scores of a chunk as two accumulator chains of 64 columns
+constexpr uint32_t kTmemCols = 512, kColO = 0, kColS = 256, kSChain = 64;
 constexpr float kRescale = 8.f;                         // log2 headroom of the reference maximum
 // The two stages interleave per k-block: k-block kb of stage st at
 // kb * kKBStride + st * kTBlock, so the 64 rows of a stage pair are contiguous
@@ -77,8 +81,8 @@ constexpr uint32_t kKBStride = kStages * kTBlock;
 static_assert(kStages == 2, "tiles are scored in pairs of stages");
 
 struct Ctrl {
-  uint64_t full[kStages];    // producer -> MMA, softmax: tile staged
-  uint64_t empty[kStages];   // MMA commit after O += P V: stage free
+  uint64_t full;             // producer -> MMA, softmax: the chunk (both tiles) staged
+  uint64_t empty;            // MMA commit after O += P V of the chunk's second tile
   uint64_t s_full[2];        // MMA commit after S = Q K^T: S buffer ready
   uint64_t s_empty[2];       // softmax threads: S buffer read
   uint64_t q_full;
@@ -87,8 +91,8 @@ struct Ctrl {
   uint32_t tmem_base;
   int32_t abort;
   int32_t count;
-  int32_t tile_phys[kStages];
-  int32_t tile_chunk[kStages];
+  int32_t chunk_phys;        // block and chunk id of the staged chunk
+  int32_t chunk_id;
   uint32_t sel_bits[kBits / 32];
   uint32_t inc_bits[kBits / 32];
   int32_t word_pre[kBits / 32 + 1];
@@ -158,15 +162,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int s = blockIdx.x, dh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kIdescS = idesc_f16(kBf16, kH, kTok, false, false);
   constexpr uint32_t kIdescS2 = idesc_f16(kBf16, kH, 2 * kTok, false, false);
   constexpr uint32_t kIdescPV = idesc_f16(kBf16, kH, kDH, false, true);
   const DecodeParams& dp = p.dp;
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(smem_u32(&C.full[i]), 1);
-      mbar_init(smem_u32(&C.empty[i]), 1);
+    mbar_init(smem_u32(&C.full), 1);
+    mbar_init(smem_u32(&C.empty), 1);
+    for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&C.s_full[i]), 1);
       mbar_init(smem_u32(&C.s_empty[i]), kSoftmaxThreads);
     }
@@ -233,11 +236,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = C.tmem_base;
   const int count = C.count;
 
-  // tiles of this split: tile u = half (u & 1) of the (u >> 1)-th attended chunk
-  const int total = 2 * count;
-  const int per = (total + p.n_splits - 1) / max(p.n_splits, 1);
-  const int u_lo = min(total, s * per), u_hi = min(total, u_lo + per);
-  const int n_tiles = u_hi - u_lo;
+  // chunks of this split; tile t = half (t & 1) of chunk c_lo + (t >> 1)
+  const int per = (count + p.n_splits - 1) / max(p.n_splits, 1);
+  const int c_lo = min(count, s * per), c_hi = min(count, c_lo + per);
+  const int n_tiles = 2 * (c_hi - c_lo);
   const bool direct = (p.n_splits == 1);
 
   if (n_tiles > 0) {
@@ -250,45 +252,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < kKB - 1; ++kb)
           tma_load_2d(smem_u32(q_s + kb * kQBlock), &qlat_map, kb * 64, b * kH, qb);
         tma_load_2d(smem_u32(q_s + (kKB - 1) * kQBlock), &qpe_map, 0, b * kH, qb);
-        // block of tile t, resolved before its stage frees up
-        auto locate = [&](int t, int& c, int32_t& phys) {
-          c = chunk_of_rank(C, words, (u_lo + t) >> 1);
+        // block of the i-th chunk of the split, resolved before the stages free up
+        auto locate = [&](int i, int& c, int32_t& phys) {
+          c = chunk_of_rank(C, words, c_lo + i);
           phys = c < p.table_width ? p.tables[(int64_t)b * p.table_stride + c] : -1;
           if (phys >= p.num_blocks) phys = -1;
         };
+        const int n_ck = n_tiles / 2;
         int c_next;
         int32_t phys_next;
         locate(0, c_next, phys_next);
         int issued = 0;
-        for (int t = 0; t < n_tiles; ++t) {
-          const int st = t % kStages;
+        for (int i = 0; i < n_ck; ++i) {
           const int c = c_next;
           const int32_t phys = phys_next;
-          if (t >= kStages && !role_wait(C, smem_u32(&C.empty[st]), ((t / kStages) - 1) & 1)) {
+          if (i >= 1 && !role_wait(C, smem_u32(&C.empty), (i - 1) & 1)) {
             give_up(C, dp.err);
             break;
           }
-          C.tile_phys[st] = phys;
-          C.tile_chunk[st] = c;
-          const uint32_t bar = smem_u32(&C.full[st]);
+          C.chunk_phys = phys;
+          C.chunk_id = c;
+          const uint32_t bar = smem_u32(&C.full);
           if (phys < 0) {
             flag_error(dp.err, SNAPMIND_DEVERR_BLOCK_ID);
             mbar_arrive(bar);
           } else {
-            mbar_arrive_expect_tx(bar, kTileBytes);
-            uint8_t* stage = kv_s + st * kTBlock;
-            const int y = phys * kBs + ((u_lo + t) & 1) * kTok;
+            // the chunk's 64 rows, k-block by k-block: both stages in one copy
+            mbar_arrive_expect_tx(bar, kStages * kTileBytes);
+            const int y = phys * kBs;
 #pragma unroll
             for (int kb = 0; kb < kKB - 1; ++kb)
-              tma_load_2d(smem_u32(stage + kb * kKBStride), &lat_map, kb * 64, y, bar);
-            tma_load_2d(smem_u32(stage + (kKB - 1) * kKBStride), &rope_map, 0, y, bar);
+              tma_load_2d(smem_u32(kv_s + kb * kKBStride), &lat_map, kb * 64, y, bar);
+            tma_load_2d(smem_u32(kv_s + (kKB - 1) * kKBStride), &rope_map, 0, y, bar);
           }
-          issued = t + 1;
-          if (t + 1 < n_tiles) locate(t + 1, c_next, phys_next);
+          issued = i + 1;
+          if (i + 1 < n_ck) locate(i + 1, c_next, phys_next);
         }
         // before the shared memory is released: every copy issued has landed (bounded)
-        for (int t = max(0, issued - kStages); t < issued; ++t)
-          mbar_wait(smem_u32(&C.full[t % kStages]), (t / kStages) & 1);
+        if (issued > 0) mbar_wait(smem_u32(&C.full), (issued - 1) & 1);
         mbar_wait(smem_u32(&C.q_full), 0);
       }
     } else if (warp == kMmaWarp) {
@@ -306,49 +307,49 @@ __global__ void __launch_bounds__(kThreads, 1)
                 smem_desc(smem_u32(stage + dh * 4 * kKBStride + ks * 16 * 128), kKBStride, 1024, kSwizzle128B);
             umma_f16(tmem + kColO, ad, bd, kIdescPV, (t > 0 || ks > 0) ? 1u : 0u);
           }
-          umma_commit(smem_u32(&C.empty[t % kStages]));
+          if (t & 1) umma_commit(smem_u32(&C.empty));
           umma_commit(smem_u32(&C.o_done));
           last_bar = smem_u32(&C.o_done);
           last_parity = t & 1;
         };
-        // S = Q K^T of tile t (even, stage 0) into S buffer 0, and of tile t + 1
-        // (stage 1) into S buffer 1 with the same MMAs (N = 64) when `pair`
-        auto issue_s = [&](int t, bool pair) {
-          const uint32_t idesc = pair ? kIdescS2 : kIdescS;
+        // S = Q K^T of both tiles of a chunk (N = 64: tile t in columns 0-31,
+        // t + 1 in 32-63), as two independent accumulator chains (even and odd
+        // k-blocks) that the softmax threads add.
+        auto issue_s = [&](int t) {
           tc_fence_after();
 #pragma unroll 1
           for (int kb = 0; kb < kKB; ++kb) {
+            const uint32_t d = tmem + kColS + (kb & 1) * kSChain;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t ad = smem_desc(smem_u32(q_s + kb * kQBlock + kk * 32), 16, 1024, kSwizzle128B);
               const uint64_t bd = smem_desc(smem_u32(kv_s + kb * kKBStride + kk * 32), 16, 1024, kSwizzle128B);
-              umma_f16(tmem + kColS, ad, bd, idesc, (kb | kk) != 0);
+              umma_f16(d, ad, bd, kIdescS2, (kb > 1 || kk > 0) ? 1u : 0u);
             }
           }
           umma_commit(smem_u32(&C.s_full[0]));
-          if (pair) umma_commit(smem_u32(&C.s_full[1]));
-          last_bar = smem_u32(&C.s_full[pair ? 1 : 0]);
+          umma_commit(smem_u32(&C.s_full[1]));
+          last_bar = smem_u32(&C.s_full[1]);
           last_parity = (t >> 1) & 1;
         };
         // Issue whichever is ready: O += P V of the oldest tile whose P is written
         // (it frees a stage for the producer), else S of the next staged tile (at
         // most two S buffers ahead of O += P V).
-        int ns = 0, np = 0;
+        int ns = 0, np = 0;  // next tile to score (even), next tile for O += P V
         long long idle_since = clock64();
         while (ok && np < n_tiles) {
           bool progressed = false;
-          if (np < ns && mbar_try_wait(smem_u32(&C.p_full), np & 1)) {
+          if (np < ns && mbar_test_wait(smem_u32(&C.p_full), np & 1)) {
             issue_pv(np++);
             progressed = true;
           } else if (ns < n_tiles) {
-            // tiles ns (even) and ns + 1 once both are staged and both S buffers were read
-            const bool pair = ns + 1 < n_tiles;
+            // the chunk of tiles ns, ns + 1 once staged and both S buffers were read
             const uint32_t par = (ns >> 1) & 1, prev = ((ns >> 1) - 1) & 1;
-            if (mbar_try_wait(smem_u32(&C.full[0]), par) && (!pair || mbar_try_wait(smem_u32(&C.full[1]), par)) &&
-                (ns < 2 || (mbar_try_wait(smem_u32(&C.s_empty[0]), prev) &&
-                            mbar_try_wait(smem_u32(&C.s_empty[1]), prev)))) {
-              issue_s(ns, pair);
-              ns += pair ? 2 : 1;
+            if (mbar_test_wait(smem_u32(&C.full), par) &&
+                (ns < 2 || (mbar_test_wait(smem_u32(&C.s_empty[0]), prev) &&
+                            mbar_test_wait(smem_u32(&C.s_empty[1]), prev)))) {
+              issue_s(ns);
+              ns += 2;
               progressed = true;
             }
           }
@@ -372,14 +373,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = 0; t < n_tiles; ++t) {
         const int st = t % kStages, sb = t & 1;
-        ok = role_wait(C, smem_u32(&C.full[st]), (t / kStages) & 1) &&
-             role_wait(C, smem_u32(&C.s_full[sb]), (t >> 1) & 1);
+        ok = role_wait(C, smem_u32(&C.full), (t >> 1) & 1) && role_wait(C, smem_u32(&C.s_full[sb]), (t >> 1) & 1);
         if (__any_sync(0xffffffffu, !ok)) {
           ok = false;
           break;
         }
-        const int phys = C.tile_phys[st], c = C.tile_chunk[st];
-        const int pos0 = c * kBs + ((t + u_lo) & 1) * kTok;
+        const int phys = C.chunk_phys, c = C.chunk_id;
+        const int pos0 = c * kBs + (t & 1) * kTok;
         const int good = phys < 0 ? 0 : max(0, min(kTok, len - pos0));  // rows holding a token
         // attended tokens of the tile as a bit mask: [0, good) for a selected chunk,
         // else [0, min(good, sink - pos0)) and [max(0, wstart - pos0), good)
@@ -398,9 +398,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         tc_fence_after();
-        float sv[kTok];
+        float sv[kTok], sv2[kTok];
         tmem_ld32(t_row + kColS + sb * kTok, sv);
+        tmem_ld32(t_row + kColS + kSChain + sb * kTok, sv2);
         tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < kTok; ++j) sv[j] += sv2[j];
         tc_fence_before();
         mbar_arrive(smem_u32(&C.s_empty[sb]));
         // masked row maximum (raw scores; scale > 0), as a tree
@@ -602,8 +605,8 @@ int launch_sparse_mla_umma(const SparseParams& p, int dtype, cudaStream_t st) {
   const uint64_t rows = (uint64_t)p.num_blocks * kBs;
   if (!tensor_map_2d(&qlat, bf16, p.q_lat, kR, (uint64_t)p.batch * kH, kR * 2, 64, kH) ||
       !tensor_map_2d(&qpe, bf16, p.q_pe, kP, (uint64_t)p.batch * kH, kP * 2, 64, kH) ||
-      !tensor_map_2d(&lat, bf16, p.latent, kR, rows, kR * 2, 64, kTok) ||
-      !tensor_map_2d(&rope, bf16, p.rope, kP, rows, kP * 2, 64, kTok)) {
+      !tensor_map_2d(&lat, bf16, p.latent, kR, rows, kR * 2, 64, kBs) ||
+      !tensor_map_2d(&rope, bf16, p.rope, kP, rows, kP * 2, 64, kBs)) {
     set_last_error("sparse_mla_umma: tensor map encoding failed");
     return SNAPMIND_ERR_CUDA;
   }
