@@ -280,9 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // the chunk's 64 rows, k-block by k-block: both stages in one copy
             mbar_arrive_expect_tx(bar, kStages * kTileBytes);
             const int y = phys * kBs;
-#pragma unroll
-            for (int kb = 0; kb < kKB - 1; ++kb)
-              tma_load_2d(smem_u32(kv_s + kb * kKBStride), &lat_map, kb * 64, y, bar);
+            tma_load_3d(smem_u32(kv_s), &lat_map, 0, y, 0, bar);  // the 8 latent k-blocks
             tma_load_2d(smem_u32(kv_s + (kKB - 1) * kKBStride), &rope_map, 0, y, bar);
           }
           issued = i + 1;
@@ -605,7 +603,7 @@ int launch_sparse_mla_umma(const SparseParams& p, int dtype, cudaStream_t st) {
   const uint64_t rows = (uint64_t)p.num_blocks * kBs;
   if (!tensor_map_2d(&qlat, bf16, p.q_lat, kR, (uint64_t)p.batch * kH, kR * 2, 64, kH) ||
       !tensor_map_2d(&qpe, bf16, p.q_pe, kP, (uint64_t)p.batch * kH, kP * 2, 64, kH) ||
-      !tensor_map_2d(&lat, bf16, p.latent, kR, rows, kR * 2, 64, kBs) ||
+      !tensor_map_col_blocks(&lat, bf16, p.latent, rows, kR * 2, kKB - 1, kBs) ||
       !tensor_map_2d(&rope, bf16, p.rope, kP, rows, kP * 2, 64, kBs)) {
     set_last_error("sparse_mla_umma: tensor map encoding failed");
     return SNAPMIND_ERR_CUDA;
