@@ -741,6 +741,9 @@ __global__ void __launch_bounds__(kTopkThreads) indexer_topk_kernel(
 
 constexpr int kSliceChunks = 128;  // chunks scored and pre-selected by one CTA
 constexpr int kSliceThreads = 256;
+constexpr int kWarpMergeK = 64;        // k up to this: one warp merges the slices' sorted lists
+constexpr int kMaxTopkChunks = 16384;  // chunks per sequence the top-k accepts
+constexpr int kMaxMergeSlices = kMaxTopkChunks / kSliceChunks;
 
 // Two-phase top-k over many CTAs.  CTA (slice, b) scores chunks
 // [slice * 128, slice * 128 + 128) of sequence b and keeps the best
@@ -757,6 +760,7 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
     int32_t* out_idx, float* out_score, float* all_scores, int vec) {
   extern __shared__ unsigned long long sk[];  // [max(kSliceChunks, merge_n)]
   __shared__ int s_last;
+  __shared__ int s_head[kMaxMergeSlices];  // merge: next unread entry of each slice's list
   const int slice = blockIdx.x, b = blockIdx.y;
   int nc = n_chunks_arr ? n_chunks_arr[b] : n_chunks0;
   nc = max(0, min(nc, max_chunks));
@@ -800,6 +804,7 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
   const unsigned long long* all = cand + (int64_t)b * n_slices * keep;
   const int n_cand = n_slices * keep;
   for (int i = threadIdx.x; i < n_cand; i += blockDim.x) sk[i] = __ldcg(all + i);
+  for (int i = threadIdx.x; i < n_slices && k <= kWarpMergeK; i += blockDim.x) s_head[i] = 0;
   __syncthreads();
   // the same rank selection over the union of candidates; output slots past the
   // valid chunks are -1 (real keys rank before the zero fillers)
@@ -809,6 +814,48 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
       out_idx[(int64_t)b * k + i] = -1;
       if (out_score) out_score[(int64_t)b * k + i] = -INFINITY;
     }
+  }
+  if (k <= kWarpMergeK) {
+    // small k: one warp merges the slices' lists (each sorted, descending) by
+    // repeatedly taking the largest list head.  Real keys are unique (score
+    // bits, then the inverted chunk id) and above the zero fillers, so the
+    // order is the same as ranking the union.
+    if (warp == 0) {
+      const int per_lane = (n_slices + 31) / 32;
+      for (int i = 0; i < n_out; ++i) {
+        unsigned long long best = 0ull;
+        int best_list = -1;
+        for (int j = 0; j < per_lane; ++j) {
+          const int L = lane + 32 * j;
+          if (L < n_slices && s_head[L] < keep) {
+            const unsigned long long h = sk[L * keep + s_head[L]];
+            if (h > best) {
+              best = h;
+              best_list = L;
+            }
+          }
+        }
+        unsigned long long m = best;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          const unsigned long long o = __shfl_xor_sync(0xffffffffu, m, off);
+          m = o > m ? o : m;
+        }
+        if (m == 0ull) break;  // only fillers left (cannot happen while i < n_out)
+        if (best == m && best_list >= 0) {  // the one lane holding the largest head
+          s_head[best_list] += 1;
+          out_idx[(int64_t)b * k + i] = (int32_t)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFull));
+          if (out_score) {
+            const uint32_t ob = (uint32_t)(m >> 32);
+            const uint32_t u = (ob & 0x80000000u) ? (ob & 0x7FFFFFFFu) : ~ob;
+            out_score[(int64_t)b * k + i] = __uint_as_float(u);
+          }
+        }
+        __syncwarp();
+      }
+    }
+    if (threadIdx.x == 0) tickets[b] = 0;
+    return;
   }
   // each slice's candidates are in rank order (descending): a candidate's global
   // rank is its place in its own list plus, per other list, the keys ahead of it
@@ -985,7 +1032,8 @@ int snapmind_indexer_topk(const void* q, const void* keys, int dtype, const int3
                           int32_t* out_idx, float* out_score, float* all_scores, void* workspace,
                           int64_t workspace_bytes, void* stream) {
   SNAPMIND_CHECK_ARG(dtype_size(dtype) > 0, "indexer_topk: unknown dtype");
-  SNAPMIND_CHECK_ARG(batch >= 0 && max_chunks > 0 && max_chunks <= 16384 && dim > 0 && k > 0 && k <= max_chunks,
+  SNAPMIND_CHECK_ARG(batch >= 0 && max_chunks > 0 && max_chunks <= kMaxTopkChunks && dim > 0 && k > 0 &&
+                         k <= max_chunks,
                      "indexer_topk: bad sizes (max_chunks <= 16384, 0 < k <= max_chunks)");
   if (batch == 0) return SNAPMIND_OK;
   SNAPMIND_CHECK_ARG(q && keys && out_idx, "indexer_topk: null pointer");

@@ -179,7 +179,8 @@ def test_topk_tie_break_on_equal_scores(cuda_device, sliced):
     assert idx.cpu().tolist() == [want, want]
 
 
-@pytest.mark.parametrize("k,n_chunks", [(32, [2048, 1500, 7]), (200, [600, 129, 1000]), (5, [1, 0, 257])])
+@pytest.mark.parametrize("k,n_chunks", [(32, [2048, 1500, 7]), (200, [600, 129, 1000]), (5, [1, 0, 257]),
+                                         (64, [5000, 4500, 10])])  # 40 slices: lanes merge two lists each
 def test_topk_sliced_equals_single_cta(cuda_device, k, n_chunks):
     """Both kernels against the oracle's stable top-k of the scores, at sizes
     where slices, ragged lengths and k > 128 (all candidates kept) occur."""
