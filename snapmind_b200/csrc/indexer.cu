@@ -822,9 +822,10 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
     // order is the same as ranking the union.
     if (warp == 0) {
       const int per_lane = (n_slices + 31) / 32;
-      for (int i = 0; i < n_out; ++i) {
-        unsigned long long best = 0ull;
-        int best_list = -1;
+      // this lane's largest unread head among its lists (lane + 32 j)
+      auto own_best = [&](unsigned long long& best, int& best_list) {
+        best = 0ull;
+        best_list = -1;
         for (int j = 0; j < per_lane; ++j) {
           const int L = lane + 32 * j;
           if (L < n_slices && s_head[L] < keep) {
@@ -835,21 +836,25 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
             }
           }
         }
-        unsigned long long m = best;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-          const unsigned long long o = __shfl_xor_sync(0xffffffffu, m, off);
-          m = o > m ? o : m;
-        }
+      };
+      unsigned long long best;
+      int best_list;
+      own_best(best, best_list);
+      for (int i = 0; i < n_out; ++i) {
+        // 64-bit warp maximum as (high word, then low word among the high-word winners)
+        const uint32_t hi = (uint32_t)(best >> 32), lo = (uint32_t)best;
+        const uint32_t mhi = __reduce_max_sync(0xffffffffu, hi);
+        const uint32_t mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? lo : 0u);
+        const unsigned long long m = ((unsigned long long)mhi << 32) | mlo;
         if (m == 0ull) break;  // only fillers left (cannot happen while i < n_out)
-        if (best == m && best_list >= 0) {  // the one lane holding the largest head
-          s_head[best_list] += 1;
-          out_idx[(int64_t)b * k + i] = (int32_t)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFull));
+        if (best == m) {        // the one lane holding the largest head
+          out_idx[(int64_t)b * k + i] = (int32_t)(0xFFFFFFFFu - lo);
           if (out_score) {
-            const uint32_t ob = (uint32_t)(m >> 32);
-            const uint32_t u = (ob & 0x80000000u) ? (ob & 0x7FFFFFFFu) : ~ob;
+            const uint32_t u = (mhi & 0x80000000u) ? (mhi & 0x7FFFFFFFu) : ~mhi;
             out_score[(int64_t)b * k + i] = __uint_as_float(u);
           }
+          s_head[best_list] += 1;
+          own_best(best, best_list);
         }
         __syncwarp();
       }
