@@ -744,6 +744,7 @@ constexpr int kSliceThreads = 256;
 constexpr int kWarpMergeK = 64;        // k up to this: one warp merges the slices' sorted lists
 constexpr int kMaxTopkChunks = 16384;  // chunks per sequence the top-k accepts
 constexpr int kMaxMergeSlices = kMaxTopkChunks / kSliceChunks;
+constexpr int kListsPerLane = (kMaxMergeSlices + 31) / 32;  // warp merge: lists owned by one lane
 
 // Two-phase top-k over many CTAs.  CTA (slice, b) scores chunks
 // [slice * 128, slice * 128 + 128) of sequence b and keeps the best
@@ -760,7 +761,6 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
     int32_t* out_idx, float* out_score, float* all_scores, int vec) {
   extern __shared__ unsigned long long sk[];  // [max(kSliceChunks, merge_n)]
   __shared__ int s_last;
-  __shared__ int s_head[kMaxMergeSlices];  // merge: next unread entry of each slice's list
   const int slice = blockIdx.x, b = blockIdx.y;
   int nc = n_chunks_arr ? n_chunks_arr[b] : n_chunks0;
   nc = max(0, min(nc, max_chunks));
@@ -804,7 +804,6 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
   const unsigned long long* all = cand + (int64_t)b * n_slices * keep;
   const int n_cand = n_slices * keep;
   for (int i = threadIdx.x; i < n_cand; i += blockDim.x) sk[i] = __ldcg(all + i);
-  for (int i = threadIdx.x; i < n_slices && k <= kWarpMergeK; i += blockDim.x) s_head[i] = 0;
   __syncthreads();
   // the same rank selection over the union of candidates; output slots past the
   // valid chunks are -1 (real keys rank before the zero fillers)
@@ -821,26 +820,28 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
     // bits, then the inverted chunk id) and above the zero fillers, so the
     // order is the same as ranking the union.
     if (warp == 0) {
-      const int per_lane = (n_slices + 31) / 32;
-      // this lane's largest unread head among its lists (lane + 32 j)
-      auto own_best = [&](unsigned long long& best, int& best_list) {
-        best = 0ull;
-        best_list = -1;
-        for (int j = 0; j < per_lane; ++j) {
-          const int L = lane + 32 * j;
-          if (L < n_slices && s_head[L] < keep) {
-            const unsigned long long h = sk[L * keep + s_head[L]];
-            if (h > best) {
-              best = h;
-              best_list = L;
-            }
-          }
-        }
-      };
-      unsigned long long best;
-      int best_list;
-      own_best(best, best_list);
+      // lane owns lists lane + 32 j (j < kListsPerLane); their current heads and
+      // the entries after them live in registers, so a step has no dependent
+      // shared-memory load
+      unsigned long long head[kListsPerLane], nxt[kListsPerLane];
+      int pos[kListsPerLane];
+#pragma unroll
+      for (int j = 0; j < kListsPerLane; ++j) {
+        const int L = lane + 32 * j;
+        const bool has = L < n_slices;
+        pos[j] = 0;
+        head[j] = has ? sk[L * keep] : 0ull;
+        nxt[j] = has && keep > 1 ? sk[L * keep + 1] : 0ull;
+      }
       for (int i = 0; i < n_out; ++i) {
+        unsigned long long best = head[0];
+        int bj = 0;
+#pragma unroll
+        for (int j = 1; j < kListsPerLane; ++j)
+          if (head[j] > best) {
+            best = head[j];
+            bj = j;
+          }
         // 64-bit warp maximum as (high word, then low word among the high-word winners)
         const uint32_t hi = (uint32_t)(best >> 32), lo = (uint32_t)best;
         const uint32_t mhi = __reduce_max_sync(0xffffffffu, hi);
@@ -853,8 +854,13 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
             const uint32_t u = (mhi & 0x80000000u) ? (mhi & 0x7FFFFFFFu) : ~mhi;
             out_score[(int64_t)b * k + i] = __uint_as_float(u);
           }
-          s_head[best_list] += 1;
-          own_best(best, best_list);
+#pragma unroll
+          for (int j = 0; j < kListsPerLane; ++j)
+            if (j == bj) {
+              head[j] = nxt[j];
+              pos[j] += 1;
+              nxt[j] = pos[j] + 1 < keep ? sk[(lane + 32 * j) * keep + pos[j] + 1] : 0ull;
+            }
         }
         __syncwarp();
       }
