@@ -178,6 +178,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(&C.o_done), 1);
     C.abort = 0;
     mbar_init_fence();
+    // Q depends only on the sequence: its copy overlaps the selection set-up below
+    const uint32_t qb = smem_u32(&C.q_full);
+    mbar_arrive_expect_tx(qb, kQBytes);
+#pragma unroll
+    for (int kb = 0; kb < kKB - 1; ++kb) tma_load_2d(smem_u32(q_s + kb * kQBlock), &qlat_map, kb * 64, b * kH, qb);
+    tma_load_2d(smem_u32(q_s + (kKB - 1) * kQBlock), &qpe_map, 0, b * kH, qb);
   }
   if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(&C.tmem_base), kTmemCols);
@@ -246,12 +252,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kProducerWarp) {
       // ---------------------------------------------------------------- TMA producer
       if (lane == 0) {
-        const uint32_t qb = smem_u32(&C.q_full);
-        mbar_arrive_expect_tx(qb, kQBytes);
-#pragma unroll
-        for (int kb = 0; kb < kKB - 1; ++kb)
-          tma_load_2d(smem_u32(q_s + kb * kQBlock), &qlat_map, kb * 64, b * kH, qb);
-        tma_load_2d(smem_u32(q_s + (kKB - 1) * kQBlock), &qpe_map, 0, b * kH, qb);
         // block of the i-th chunk of the split, resolved before the stages free up
         auto locate = [&](int i, int& c, int32_t& phys) {
           c = chunk_of_rank(C, words, c_lo + i);
@@ -515,6 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (tid < kSoftmaxThreads) {
     // no tile in this split: an empty partial (or a zero output when nothing is attended)
     const int head = tid;
+    if (tid == 0) mbar_wait(smem_u32(&C.q_full), 0);  // the Q copy lands before the CTA exits (bounded)
     if (direct) {
       T* o = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)head * dp.out_stride_head +
              dh * kDH;
