@@ -270,6 +270,16 @@ SNAPMIND_API int snapmind_indexer_score_ref(const float *q, const float *w, int3
                                void *stream);
 
 /*
+ * The query of the chunk selector, out[b][o] = sum_d w[o][d] * hidden[b][d]
+ * with fp32 accumulation and fp32 output: hidden [batch][d_model] and w
+ * [out_dim][d_model] in `dtype`.  One launch that reads w once (the selector's
+ * W_q projection; the reference indexer projects its query with nn.Linear
+ * layers, snapmind/layers/indexer/lookahead.py:32-35).
+ */
+SNAPMIND_API int snapmind_indexer_query(const void *hidden, const void *w, int dtype, float *out, int32_t batch,
+                                        int32_t d_model, int32_t out_dim, void *stream);
+
+/*
  * Sigmoid-gated chunk scores sigmoid(q . k * scale + bias) and the k best
  * chunks per sequence (no reference counterpart: IndexerConfig.score_k exists
  * but is never read, snapmind/core/config.py:92).  Order: score descending,

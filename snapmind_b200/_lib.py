@@ -88,6 +88,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _p, _p],
     ),
     "snapmind_indexer_score_ref": (_int, [_p, _p, _i32, _i32, _p, _i32, _i32, _p, _p]),
+    "snapmind_indexer_query": (_int, [_p, _p, _int, _p, _i32, _i32, _i32, _p]),
     "snapmind_indexer_topk": (
         _int,
         [_p, _p, _int, _p, _i32, _i32, _i32, _i32, _f32, _f32, _i32, _p, _p, _p, _p, _i64, _p],

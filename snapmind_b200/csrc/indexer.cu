@@ -904,6 +904,80 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
   if (threadIdx.x == 0) tickets[b] = 0;
 }
 
+// ---------------------------------------------------------------------------
+// query projection q[b] = W . h[b] (fp32 out): one read of W, HBM-bound
+// ---------------------------------------------------------------------------
+constexpr int kQueryRows = 2;    // output rows per CTA
+constexpr int kQueryParts = 4;   // warps splitting d_model for one output row
+constexpr int kQueryBatch = 16;  // sequences per CTA (grid.y covers the rest)
+
+// CTA = (2 output rows, up to 16 sequences), 8 warps: warp (row, part) sums
+// part `part` of d_model for its row over the CTA's sequences with 16-byte
+// loads (W read once; the hidden rows are shared by every CTA through L2),
+// then the 4 parts meet in shared memory.
+template <typename T>
+__global__ void __launch_bounds__(32 * kQueryRows * kQueryParts) indexer_query_kernel(
+    const T* hidden, const T* w, float* out, int batch, int d_model, int out_dim, int vec) {
+  __shared__ float part_sum[kQueryRows][kQueryParts][kQueryBatch];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row_l = warp / kQueryParts, part = warp % kQueryParts;
+  const int o = blockIdx.x * kQueryRows + row_l;
+  const int b0 = blockIdx.y * kQueryBatch;
+  const int nb = min(kQueryBatch, batch - b0);
+  float acc[kQueryBatch];
+#pragma unroll
+  for (int j = 0; j < kQueryBatch; ++j) acc[j] = 0.f;
+  if (o < out_dim) {
+    const T* wr = w + (int64_t)o * d_model;
+    if (vec) {
+      constexpr int V = 16 / (int)sizeof(T);
+      const int nv = d_model / V;
+      const int v0 = part * nv / kQueryParts, v1 = (part + 1) * nv / kQueryParts;
+      for (int v = v0 + lane; v < v1; v += 32) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(wr + (int64_t)v * V);
+        const T* wt = reinterpret_cast<const T*>(&wv);
+#pragma unroll
+        for (int j = 0; j < kQueryBatch; ++j) {
+          if (j < nb) {
+            const uint4 hv = *reinterpret_cast<const uint4*>(hidden + (int64_t)(b0 + j) * d_model + (int64_t)v * V);
+            const T* ht = reinterpret_cast<const T*>(&hv);
+#pragma unroll
+            for (int e = 0; e < V; ++e) acc[j] = fmaf(Conv<T>::to_f(wt[e]), Conv<T>::to_f(ht[e]), acc[j]);
+          }
+        }
+      }
+    } else {
+      const int d0 = part * d_model / kQueryParts, d1 = (part + 1) * d_model / kQueryParts;
+      for (int d = d0 + lane; d < d1; d += 32) {
+        const float wd = Conv<T>::to_f(wr[d]);
+#pragma unroll
+        for (int j = 0; j < kQueryBatch; ++j)
+          if (j < nb) acc[j] = fmaf(wd, Conv<T>::to_f(hidden[(int64_t)(b0 + j) * d_model + d]), acc[j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kQueryBatch; ++j) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], off);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < kQueryBatch; ++j) part_sum[row_l][part][j] = acc[j];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < kQueryRows * nb; e += blockDim.x) {
+    const int r = e / nb, j = e - r * nb;
+    const int oo = blockIdx.x * kQueryRows + r;
+    if (oo < out_dim) {
+      float sum = 0.f;
+#pragma unroll
+      for (int q = 0; q < kQueryParts; ++q) sum += part_sum[r][q][j];
+      out[(int64_t)(b0 + j) * out_dim + oo] = sum;
+    }
+  }
+}
+
 struct TopkPlan {
   int n_slices, keep, merge_n;
   int64_t tickets_bytes, total;
@@ -1031,6 +1105,38 @@ int snapmind_indexer_score_ref(const float* q, const float* w, int32_t n_rows, i
   indexer_score_ref_kernel<<<grid, 32 * warps_per_block, 0, static_cast<cudaStream_t>(stream)>>>(
       q, w, n_rows, n_heads, keys, n_chunks, dim, scores);
   SNAPMIND_LAUNCH_CHECK("indexer_score_ref launch");
+}
+
+int snapmind_indexer_query(const void* hidden, const void* w, int dtype, float* out, int32_t batch, int32_t d_model,
+                           int32_t out_dim, void* stream) {
+  const int esz = dtype_size(dtype);
+  SNAPMIND_CHECK_ARG(esz > 0, "indexer_query: unknown dtype");
+  SNAPMIND_CHECK_ARG(batch >= 0 && d_model > 0 && out_dim > 0, "indexer_query: bad sizes");
+  if (batch == 0) return SNAPMIND_OK;
+  SNAPMIND_CHECK_ARG(hidden && w && out, "indexer_query: null pointer");
+  SNAPMIND_CHECK_ARG((batch + kQueryBatch - 1) / kQueryBatch <= 65535, "indexer_query: batch too large");
+  const int vec = (d_model * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(hidden) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+  dim3 grid((out_dim + kQueryRows - 1) / kQueryRows, (batch + kQueryBatch - 1) / kQueryBatch);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int threads = 32 * kQueryRows * kQueryParts;
+  switch (dtype) {
+    case SNAPMIND_DTYPE_F32:
+      indexer_query_kernel<float><<<grid, threads, 0, st>>>(static_cast<const float*>(hidden),
+                                                           static_cast<const float*>(w), out, batch, d_model,
+                                                           out_dim, vec);
+      break;
+    case SNAPMIND_DTYPE_BF16:
+      indexer_query_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(hidden), static_cast<const __nv_bfloat16*>(w), out, batch, d_model,
+          out_dim, vec);
+      break;
+    default:
+      indexer_query_kernel<__half><<<grid, threads, 0, st>>>(static_cast<const __half*>(hidden),
+                                                            static_cast<const __half*>(w), out, batch, d_model,
+                                                            out_dim, vec);
+  }
+  SNAPMIND_LAUNCH_CHECK("indexer_query launch");
 }
 
 int64_t snapmind_indexer_topk_workspace_bytes(int32_t batch, int32_t max_chunks, int32_t k) {

@@ -174,7 +174,14 @@ class ChunkSelector:
         _lib.check(status, "ChunkSelector.update_keys")
 
     def query(self, hidden: torch.Tensor) -> torch.Tensor:
-        return (hidden.to(self.w_q.dtype) @ self.w_q.T).float().contiguous()
+        """q [B, index_dim] fp32 = W_q . h for hidden [B, d_model] (one kernel, W_q read once)."""
+        h = hidden.to(self.w_q.dtype).contiguous()
+        out = torch.empty((h.shape[0], self.index_dim), dtype=torch.float32, device=h.device)
+        status = _lib.load().snapmind_indexer_query(
+            h.data_ptr(), self.w_q.data_ptr(), _lib.dtype_code(self.w_q.dtype), out.data_ptr(), h.shape[0],
+            h.shape[1], self.index_dim, _lib.stream_handle(h.device))
+        _lib.check(status, "ChunkSelector.query")
+        return out
 
     def select(self, q: torch.Tensor, n_chunks: torch.Tensor | int, k: int = 32, all_scores: bool = False):
         """Top-k chunk ids (int32 [B, k], -1 past the valid chunks) and their scores."""

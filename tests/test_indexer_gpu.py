@@ -329,3 +329,23 @@ def test_sparse_mla_tcgen05_rising_scores_and_poisoned_slots(cuda_device, n_spli
         want = omla.sparse_mla_decode(q_lat[b], q_pe[b], _seq_rows(lat, tables, b, lens[b], bs),
                                       _seq_rows(rope, tables, b, lens[b], bs), pos, scale)
         np.testing.assert_allclose(got[b], want, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("dt,batch,d_model,out_dim", [(torch.bfloat16, 8, 7168, 128), (torch.bfloat16, 37, 1000, 96),
+                                                      (torch.float32, 5, 300, 128), (torch.float16, 17, 4100, 64)])
+def test_indexer_query_matches_fp64_product(cuda_device, dt, batch, d_model, out_dim):
+    """snapmind_indexer_query (the selector's W_q . h): 16-byte and scalar paths,
+    more than 16 sequences (a second grid row), against the fp64 product of the
+    same rounded inputs."""
+    from snapmind_b200 import _lib
+
+    g = torch.Generator(device="cpu").manual_seed(d_model + batch)
+    h = torch.randn((batch, d_model), generator=g).to(dt)
+    w = (torch.randn((out_dim, d_model), generator=g) * d_model ** -0.5).to(dt)
+    out = torch.empty((batch, out_dim), dtype=torch.float32, device="cuda")
+    hd, wd = h.cuda(), w.cuda()
+    rc = _lib.load().snapmind_indexer_query(hd.data_ptr(), wd.data_ptr(), _lib.dtype_code(dt), out.data_ptr(), batch,
+                                            d_model, out_dim, _lib.stream_handle())
+    _lib.check(rc, "indexer_query")
+    want = h.double() @ w.double().T
+    np.testing.assert_allclose(out.cpu().double().numpy(), want.numpy(), rtol=1e-4, atol=1e-4)
