@@ -908,13 +908,13 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
 // query projection q[b] = W . h[b] (fp32 out): one read of W, HBM-bound
 // ---------------------------------------------------------------------------
 constexpr int kQueryRows = 2;    // output rows per CTA
-constexpr int kQueryParts = 4;   // warps splitting d_model for one output row
-constexpr int kQueryBatch = 16;  // sequences per CTA (grid.y covers the rest)
+constexpr int kQueryParts = 8;   // warps splitting d_model for one output row
+constexpr int kQueryBatch = 8;   // sequences per CTA (grid.y covers the rest)
 
-// CTA = (2 output rows, up to 16 sequences), 8 warps: warp (row, part) sums
+// CTA = (2 output rows, up to 8 sequences), 16 warps: warp (row, part) sums
 // part `part` of d_model for its row over the CTA's sequences with 16-byte
-// loads (W read once; the hidden rows are shared by every CTA through L2),
-// then the 4 parts meet in shared memory.
+// loads, two vectors per lane in flight (W read once; the hidden rows are
+// shared by every CTA through L2), then the 8 parts meet in shared memory.
 template <typename T>
 __global__ void __launch_bounds__(32 * kQueryRows * kQueryParts) indexer_query_kernel(
     const T* hidden, const T* w, float* out, int batch, int d_model, int out_dim, int vec) {
@@ -933,6 +933,7 @@ __global__ void __launch_bounds__(32 * kQueryRows * kQueryParts) indexer_query_k
       constexpr int V = 16 / (int)sizeof(T);
       const int nv = d_model / V;
       const int v0 = part * nv / kQueryParts, v1 = (part + 1) * nv / kQueryParts;
+#pragma unroll 2
       for (int v = v0 + lane; v < v1; v += 32) {
         const uint4 wv = *reinterpret_cast<const uint4*>(wr + (int64_t)v * V);
         const T* wt = reinterpret_cast<const T*>(&wv);
