@@ -734,11 +734,11 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
 
     graphs: dict[int, torch.cuda.CUDAGraph] = {}
 
-    # kernels per step: reserve, append, top-k, sparse attention (+ the split merge when it splits)
+    # kernels per step: reserve, append, indexer query, top-k, sparse attention (+ the split merge when it splits)
     from snapmind_b200 import _lib as slib
 
     n_spl = slib.load().snapmind_sparse_mla_default_splits(B, MLA_HEADS, MLA_RANK, MLA_ROPE, MLA_CHUNK, 1)
-    per_core = 4 + (1 if n_spl > 1 else 0)
+    per_core = 5 + (1 if n_spl > 1 else 0)
 
     def capture(n_core: int) -> None:  # recorded, not run
         gr = torch.cuda.CUDAGraph()
