@@ -11,7 +11,8 @@
 //   Shared memory (1024-aligned, 128-byte swizzle, written by TMA):
 //     Q: 9 k-blocks x [128 rows x 64] = 144 KB, resident;
 //     one attended chunk (block) of 64 rows as two 32-row stages,
-//       9 k-blocks x [64 rows x 64] (72 KB, one TMA box per k-block);
+//       9 k-blocks x [64 rows x 64] (72 KB: one 3-D TMA box for the 8 latent
+//       k-blocks, one 2-D box for the rope k-block);
 //     P: [128 x 32] bf16, 64-byte swizzle, written by the softmax threads.
 //   TMEM (512 columns): O [128 x 256] f32 at column 0 (this CTA's half of the
 //     512 output dims); the scores of a chunk [128 x 64] f32 as two
