@@ -218,7 +218,7 @@ class TieredKVPool:
             self.L, self.B, 1, self.H, self.D, self.chunk, self.total_slots, self.err.data_ptr(), self._stream(),
         )  # fmt: skip
         _lib.check(status, "TieredKVPool.append")
-        max_len = self.n_slots * self.chunk
+        max_len = self._resident_bound() * self.chunk
         # split plan sized for the average resident length (the pool shared by the batch)
         split = split_tokens or self.lib.snapmind_paged_gqa_decode_split_tokens(
             self.B, self.H, max(self.chunk, 2 * self.n_slots * self.chunk // self.B), self.chunk)
@@ -236,6 +236,19 @@ class TieredKVPool:
                 self.err.data_ptr(), self._stream(),
             )  # fmt: skip
             _lib.check(status, "TieredKVPool.decode")
+
+    def _resident_bound(self) -> int:
+        """An upper bound on any sequence's resident chunks at this step's decode:
+        the largest count in the residency snapshot of two steps ago plus what
+        three steps can add (per step at most the requested chunks and one new
+        chunk per sequence), capped at the pool's slots.  It sizes the decode's
+        split plan; without a snapshot yet, every slot."""
+        cap = self.n_slots
+        snap = self.snapshot(2)
+        if snap is None:
+            return cap
+        most = int((snap >= 0).sum(axis=1).max()) if snap.size else 0
+        return max(1, min(cap, most + 3 * (self.n_requests + 1)))
 
     def pick_requests(self, rng: np.random.RandomState, n: int, exclude: set | None = None) -> list[tuple[int, int]]:
         """n seeded-random chunks that were cold two steps ago (completed, unpinned, not recently requested)."""
