@@ -5,8 +5,6 @@ from __future__ import annotations
 import json
 from pathlib import Path
 
-import numpy as np
-
 from inputs import digest, randn
 
 GOLDEN = Path(__file__).resolve().parent / "golden"

@@ -10,7 +10,6 @@ from inputs import randn
 from oracle import bf16
 from oracle import indexer as oidx
 from oracle import mla as omla
-from oracle import paged
 from replay import GOLDEN
 from test_oracle_golden import indexer_key_states
 

@@ -4,7 +4,6 @@ import pytest
 import torch
 
 from inputs import randn
-from oracle import bf16
 from oracle import tiered as otiered
 from replay import load_tiered_ops, replay_tiered
 
