@@ -178,6 +178,20 @@ def shuffled_tables(seed: int, lens: np.ndarray, growth: int, slack: float = 1.1
 
 
 # ----------------------------------------------------------------------------- GPU arm
+def decode_config(world: int) -> dict:
+    """The headline workload, as both arms report it."""
+    return {
+        "workload": f"paged GQA decode step, Llama-3-8B KV shape: {L} layers x (append 1 token/seq + "
+                    "paged decode attention); 32 q / 8 kv heads, head_dim 128, bf16, block 16, "
+                    "ctx U[1024,8192], shuffled block tables",
+        "batch_per_gpu": DECODE_BATCH,
+        "global_batch": DECODE_BATCH * world,
+        "layers": L,
+        "parallelism": f"dp{world} (sequence sharding, no data-path collective)",
+        "l2": "inputs larger than L2 (about 2.4 GB of K/V per decode launch)",
+    }
+
+
 def run_b200(args, rank: int, world: int, dist) -> dict | None:
     import torch
 
@@ -215,7 +229,7 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
 
     # ---------------- decode workload ----------------
     lens = seeded_lengths(seed, DECODE_BATCH, *DECODE_CTX)
-    growth = steps + warmup + 16
+    growth = 2 * steps + warmup + 16  # the timed steps, then as many e2e steps
     nb, width, tables, free = shuffled_tables(seed, lens, growth)
     pool = PagedKVPool(L, H, D, nb, max_seqs=DECODE_BATCH, max_blocks_per_seq=width, block_size=BS,
                        dtype=torch.bfloat16, device=dev)
@@ -315,7 +329,7 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
             o_h[i].copy_(od, non_blocking=True)
             ev_out[i].record(d2h_stream)
 
-    e2e_steps = max(1, min(steps, 10))
+    e2e_steps = steps
     h2d(0)
     e2e_step(0)
     torch.cuda.synchronize()
@@ -355,16 +369,7 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) K/V/q, seeded context lengths and shuffled block tables)",
-        "config": {
-            "workload": f"paged GQA decode step, Llama-3-8B KV shape: {L} layers x (append 1 token/seq + "
-                        "paged decode attention); 32 q / 8 kv heads, head_dim 128, bf16, block 16, "
-                        "ctx U[1024,8192], shuffled block tables",
-            "batch_per_gpu": DECODE_BATCH,
-            "global_batch": DECODE_BATCH * world,
-            "layers": L,
-            "parallelism": f"dp{world} (sequence sharding, no data-path collective)",
-            "l2": "inputs larger than L2 (about 2.4 GB of K/V per decode launch)",
-        },
+        "config": decode_config(world),
         "roofline": {
             "kernel": "paged_gqa_decode",
             "bound": "hbm",
@@ -1083,53 +1088,57 @@ def reduce_max(dist, x: float, dev) -> float:
 
 
 # ----------------------------------------------------------------------------- CPU (reference algorithm)
-def _cpu_build(seed: int, lens: list[int], n_layer_pools: int):
-    """Reference-layout paged data (a few layer pools) for each sequence of ``lens``."""
+def _cpu_build(seed: int, unit_lens: list[int]):
+    """One reference-layout paged cache, with its own pool, per (sequence, layer) unit
+    of the sample: ``unit_lens`` holds each unit's context length."""
     import oracle.paged as op
 
     rng = np.random.RandomState(seed)
     caches = []
-    for n in lens:
-        layers = []
-        for _ in range(n_layer_pools):
-            c = op.PagedKVCacheOracle(max_seq_len=n + 64, n_layers=1, n_heads=H, head_dim=D, block_size=BS)
-            k = rng.standard_normal((1, H, n, D)).astype(np.float32)
-            v = rng.standard_normal((1, H, n, D)).astype(np.float32)
-            # prefill without the per-token loop (not timed), same slot layout as store()
-            nbk = (n + BS - 1) // BS
-            blocks = [c.free_blocks.pop() for _ in range(nbk)]
-            c.block_tables[0] = blocks
-            for j, p in enumerate(blocks):
-                t0, t1 = j * BS, min(n, (j + 1) * BS)
-                c.k[p, : t1 - t0] = k[0, :, t0:t1].transpose(1, 0, 2)
-                c.v[p, : t1 - t0] = v[0, :, t0:t1].transpose(1, 0, 2)
-            c.slot_counts[0] = n
-            layers.append(c)
-        caches.append(layers)
+    for n in unit_lens:
+        c = op.PagedKVCacheOracle(max_seq_len=n + 64, n_layers=1, n_heads=H, head_dim=D, block_size=BS)
+        k = rng.standard_normal((1, H, n, D)).astype(np.float32)
+        v = rng.standard_normal((1, H, n, D)).astype(np.float32)
+        # prefill without the per-token loop (not timed), same slot layout as store()
+        nbk = (n + BS - 1) // BS
+        blocks = [c.free_blocks.pop() for _ in range(nbk)]
+        c.block_tables[0] = blocks
+        for j, p in enumerate(blocks):
+            t0, t1 = j * BS, min(n, (j + 1) * BS)
+            c.k[p, : t1 - t0] = k[0, :, t0:t1].transpose(1, 0, 2)
+            c.v[p, : t1 - t0] = v[0, :, t0:t1].transpose(1, 0, 2)
+        c.slot_counts[0] = n
+        caches.append(c)
     q = rng.standard_normal((1, HQ, 1, D)).astype(np.float32)
     kv = rng.standard_normal((1, H, 1, D)).astype(np.float32)
     return caches, q, kv
 
 
 def _cpu_decode(caches, q, kv):
-    """One decode step of each sequence over all layers: store + fetch + GQA math (reference path)."""
+    """One decode step of every (sequence, layer) unit: store + fetch + GQA math (reference path)."""
     import oracle.gqa as og
 
-    for layers in caches:
-        for layer in range(L):
-            c = layers[layer % len(layers)]
-            c.store(0, kv, kv, 0)
-            k, v = c.fetch(0)
-            og.gqa_attention(q, k, v, D ** -0.5, dtype=np.float32)
-            c.slot_counts[0] -= 1  # the sample's context stays fixed across steps
+    for c in caches:
+        c.store(0, kv, kv, 0)
+        k, v = c.fetch(0)
+        og.gqa_attention(q, k, v, D ** -0.5, dtype=np.float32)
+        c.slot_counts[0] -= 1  # the sample's context stays fixed across steps
 
 
-def _cpu_worker(conn, seed: int, lens: list[int]):
-    caches, q, kv = _cpu_build(seed, lens, 2)
+def _cpu_worker(conn, seed: int, unit_lens: list[int]):
+    caches, q, kv = _cpu_build(seed, unit_lens)
     conn.send("ready")
     while conn.recv() == "step":
         _cpu_decode(caches, q, kv)
         conn.send("done")
+
+
+def cpu_sample_size(requested: int) -> int:
+    """Sequences in the CPU sample: as requested, but at most what fits in a
+    quarter of the free host memory (each holds 32 fp32 layer pools, about
+    1.2 GB at the mean context)."""
+    per_seq = L * (sum(DECODE_CTX) // 2 + 64) * H * D * 4 * 2
+    return max(1, min(requested, int(0.25 * host_memory_budget() // per_seq)))
 
 
 def cpu_reference_timing(n_seqs: int, steps: int, warmup: int, seed: int = 99) -> dict:
@@ -1138,8 +1147,9 @@ def cpu_reference_timing(n_seqs: int, steps: int, warmup: int, seed: int = 99) -
     import multiprocessing as mp
 
     cores = os.cpu_count() or 1
-    workers = max(1, min(cores, n_seqs))
     lens = seeded_lengths(seed, n_seqs, *DECODE_CTX).tolist()
+    units = [n for n in lens for _ in range(L)]  # (sequence, layer) pairs, each with its own pool
+    workers = max(1, min(cores, len(units)))
     ctx = mp.get_context("spawn")
     procs, conns = [], []
     # one BLAS thread per worker process: the workers themselves cover the cores
@@ -1149,7 +1159,7 @@ def cpu_reference_timing(n_seqs: int, steps: int, warmup: int, seed: int = 99) -
     try:
         for w in range(workers):
             parent, child = ctx.Pipe()
-            p = ctx.Process(target=_cpu_worker, args=(child, seed + w, lens[w::workers]), daemon=True)
+            p = ctx.Process(target=_cpu_worker, args=(child, seed + w, units[w::workers]), daemon=True)
             p.start()
             procs.append(p)
             conns.append(parent)
@@ -1183,35 +1193,36 @@ def cpu_reference_timing(n_seqs: int, steps: int, warmup: int, seed: int = 99) -
                 p.terminate()
     step_s = statistics.median(times)
     return {"value": round(n_seqs / step_s, 3), "unit": "tok/s", "cores": workers, "kind": "port",
-            "sample": f"{n_seqs} sequences (ctx U[1024,8192]) x 32 layers per step, reference algorithm "
-                      f"(per-token store, per-block fetch concat, repeat_interleave/matmul/softmax/matmul, fp32) "
-                      f"in {workers} worker processes; median of {steps} steps",
+            "sample": f"{n_seqs} sequences (ctx U[1024,8192]) x {L} layers per step, each (sequence, layer) "
+                      f"with its own fp32 pool; reference algorithm (per-token store, per-block fetch concat, "
+                      f"repeat_interleave/matmul/softmax/matmul) in {workers} worker processes; "
+                      f"{warmup} warm-up + median of {steps} steps",
             "step_s": round(step_s, 3)}
 
 
 def run_reference_arm(args, rank: int, world: int) -> dict | None:
+    """The reference's CPU implementation of the headline workload (the oracle port)
+    on rank 0's host cores: --warmup untimed and --steps timed steps, each over a
+    bounded sample of the decode batch, reported on the B200 arm's config."""
     if rank != 0:
         return None
-    # each step is seconds of CPU work: time at most 5 of them so the run stays within minutes
-    timed = max(1, min(args.steps, 5))
-    res = cpu_reference_timing(n_seqs=args.cpu_sample, steps=timed, warmup=min(args.warmup, 1))
+    n_seqs = cpu_sample_size(args.cpu_sample)
+    res = cpu_reference_timing(n_seqs=n_seqs, steps=args.steps, warmup=args.warmup)
     return {
         "impl": "reference",
         "metric": METRIC,
         "value": res["value"],
         "unit": "tok/s",
         "n_gpus": world,
-        "steps": timed,
+        "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(res["step_s"] * 1e3, 2),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic (seeded)",
-        "config": {"workload": "reference paged KV decode path on the host CPU (oracle port of "
-                               "snapmind/kv_cache/paged.py + snapmind/layers/attention/gqa.py), Llama-3-8B KV shape",
-                   "batch_sample": args.cpu_sample, "layers": L},
+        "data": "synthetic (seeded N(0,1) K/V/q, seeded context lengths)",
+        "config": decode_config(world),
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -1253,7 +1264,7 @@ def main():
     # the CPU baseline's spawn pool starts before any CUDA work on this process
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_reference_timing(n_seqs=args.cpu_sample, steps=3, warmup=1)
+        cpu = cpu_reference_timing(n_seqs=cpu_sample_size(args.cpu_sample), steps=3, warmup=1)
 
     dist = None
     if world > 1:

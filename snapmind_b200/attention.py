@@ -44,6 +44,11 @@ from snapmind_b200.kv_cache.sliding_window import SlidingLayerView
 from snapmind_b200.paged_pool import PoolLayerView
 from snapmind_b200.registry import ATTENTION
 
+try:  # the reference's attention contract (snapmind/layers/attention/base.py:9-22) when importable
+    from snapmind.layers.attention.base import AttentionABC as _AttentionBase
+except ImportError:
+    _AttentionBase = nn.Module
+
 _ROPE_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
 
 
@@ -70,7 +75,7 @@ def _is_window_mask(mask: torch.Tensor, n: int, window: int) -> bool:
 
 
 @ATTENTION.register("gqa_paged")
-class PagedGroupedQueryAttention(nn.Module):
+class PagedGroupedQueryAttention(_AttentionBase):
     def __init__(
         self,
         d_model: int,

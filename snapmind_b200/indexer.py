@@ -28,12 +28,15 @@ from snapmind_b200 import _lib
 from snapmind_b200.registry import INDEXER
 
 
-class IndexerABC(abc.ABC):
-    """snapmind/layers/indexer/base.py:6-18."""
+try:  # the reference's indexer contract itself (snapmind/layers/indexer/base.py:6-18) when importable
+    from snapmind.layers.indexer.base import IndexerABC
+except ImportError:
 
-    @abc.abstractmethod
-    def score(self, hidden_states: dict[int, torch.Tensor], chunk_ids: list[int]) -> dict[int, torch.Tensor]:
-        """Score each historical chunk for relevance to the current decoding window."""
+    class IndexerABC(abc.ABC):  # type: ignore[no-redef]
+        """Stand-in for the reference's indexer contract: one abstract ``score``."""
+
+        @abc.abstractmethod
+        def score(self, hidden_states: dict[int, torch.Tensor], chunk_ids: list[int]) -> dict[int, torch.Tensor]: ...
 
 
 def chunk_means(k: torch.Tensor, width: int) -> torch.Tensor:

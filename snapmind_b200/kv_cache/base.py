@@ -1,41 +1,45 @@
-"""The KV-cache plugin contract, restated from snapmind/kv_cache/base.py:9-43.
+"""The KV-cache plugin contract (snapmind/kv_cache/base.py:9-43).
 
+When the reference package is importable, ``KVCacheABC`` here IS the
+reference's class, so every cache of this package is a real subclass of it and
+``isinstance(cache, snapmind.kv_cache.base.KVCacheABC)`` holds.  Without the
+reference (a serving host that ships only this package) a stand-in with the
+same six abstract methods takes its place:
 ``store(layer_idx, key, value, seq_pos)``, ``fetch(layer_idx) -> (k, v)``,
 ``evict(tokens_to_keep)``, ``reset()``, ``memory_usage() -> dict`` and
-``layer_dicts() -> {layer: {"k": ..., "v": ...}}`` — same names, argument
-meaning and return shapes, so the B200 plugins swap in by registry key.
+``layer_dicts() -> {layer: {"k": ..., "v": ...}}``.
 """
 from __future__ import annotations
 
 import abc
 from typing import Any
 
-import torch
+try:
+    from snapmind.kv_cache.base import KVCacheABC
+    FROM_REFERENCE = True
+except ImportError:
+    FROM_REFERENCE = False
+
+    class KVCacheABC(abc.ABC):  # type: ignore[no-redef]
+        """Stand-in for the reference's KV-cache contract (same abstract methods)."""
+
+        @abc.abstractmethod
+        def store(self, layer_idx: int, key, value, seq_pos: int) -> None: ...
+
+        @abc.abstractmethod
+        def fetch(self, layer_idx: int): ...
+
+        @abc.abstractmethod
+        def evict(self, tokens_to_keep: int) -> None: ...
+
+        @abc.abstractmethod
+        def reset(self) -> None: ...
+
+        @abc.abstractmethod
+        def memory_usage(self) -> dict: ...
+
+        @abc.abstractmethod
+        def layer_dicts(self) -> dict[int, dict[str, Any]]: ...
 
 
-class KVCacheABC(abc.ABC):
-    """Base class for KV cache strategies."""
-
-    @abc.abstractmethod
-    def store(self, layer_idx: int, key: torch.Tensor, value: torch.Tensor, seq_pos: int) -> None:
-        """Store *key* and *value* tensors for the given layer at *seq_pos*."""
-
-    @abc.abstractmethod
-    def fetch(self, layer_idx: int) -> tuple[torch.Tensor, torch.Tensor]:
-        """Return ``(keys, values)`` for the given layer, concatenated along the sequence dim."""
-
-    @abc.abstractmethod
-    def evict(self, tokens_to_keep: int) -> None:
-        """Drop all but the *tokens_to_keep* most recent entries."""
-
-    @abc.abstractmethod
-    def reset(self) -> None:
-        """Clear all cached data."""
-
-    @abc.abstractmethod
-    def memory_usage(self) -> dict:
-        """Return a dict with memory/block statistics (keys vary by strategy)."""
-
-    @abc.abstractmethod
-    def layer_dicts(self) -> dict[int, dict[str, Any]]:
-        """Return the per-layer ``{layer_idx: {"k": tensor, "v": tensor}}`` dict."""
+__all__ = ["KVCacheABC", "FROM_REFERENCE"]

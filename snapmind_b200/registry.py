@@ -7,9 +7,10 @@ rejects a duplicate key without ``override`` with ``RegistryError``;
 ``create(key, **kw)`` instantiates, ``get(key)`` returns the stored object, both
 raise ``RegistryError`` for unknown keys; ``list()`` and ``in`` enumerate keys.
 The singletons mirror ``KV_CACHE``, ``ATTENTION`` and ``INDEXER``
-(snapmind/core/registry.py:92-111).  When the real snapmind package is
-importable, :func:`snapmind_b200.integration.register_with_snapmind` also
-registers these plugins into snapmind's own registries.
+(snapmind/core/registry.py:92-111), so this package's plugins can be created
+by key on a host that does not ship snapmind.  Where snapmind is importable,
+:func:`snapmind_b200.integration.register_with_snapmind` registers the same
+plugins into snapmind's own ``KV_CACHE`` / ``ATTENTION`` / ``INDEXER``.
 """
 from __future__ import annotations
 

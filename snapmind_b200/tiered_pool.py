@@ -139,6 +139,16 @@ class TieredKVPool:
         self._plan(0, [])  # rebuild tables (no growth, no requests)
         self.step_idx = 0
         torch.cuda.synchronize(self.device)
+        # every residency snapshot starts as the installed map: the snapshot read at
+        # step 2 is the one of step 0, which no step writes
+        installed = self.chunk_slot.cpu()
+        for snap, ev in zip(self._snap, self._snap_ev):
+            snap.copy_(installed)
+            ev.record(torch.cuda.current_stream(self.device))
+
+    def _check_requests(self, requests: list[tuple[int, int]]) -> None:
+        if len(requests) > self.n_requests:
+            raise ValueError(f"TieredKVPool: {len(requests)} requests exceed the {self.n_requests} staging slots")
 
     def check(self) -> None:
         word = int(self.err.item())
@@ -163,6 +173,7 @@ class TieredKVPool:
 
     def prefetch(self, requests: list[tuple[int, int]]) -> None:
         """Copy the next step's requested chunks into the inbound staging slots (copy stream)."""
+        self._check_requests(requests)
         cs = self.copy_stream
         cs.wait_event(self._staging_free)
         for i, (b, c) in enumerate(requests):
@@ -186,6 +197,9 @@ class TieredKVPool:
         of the previous step); ``next_requests`` are prefetched after this
         step's slot moves so their copies overlap this step's attention.
         """
+        self._check_requests(requests)
+        if next_requests:
+            self._check_requests(next_requests)
         main = torch.cuda.current_stream(self.device)
         self.step_idx += 1
         if requests:

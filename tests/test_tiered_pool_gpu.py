@@ -109,3 +109,42 @@ def test_tiered_pool_policy_data_and_attention(cuda_device):
         for c in range(int(lens[b]) // chunk, length // chunk):
             assert torch.equal(pool.backing[b, c, 0].float(), shadow_k[b, c]), (b, c)
     assert pool.h2d_bytes > 0 and pool.d2h_bytes > 0
+
+
+def test_tiered_pool_install_over_stale_snapshots(cuda_device):
+    """Install over a pool whose residency snapshots show fewer resident chunks than
+    the installed set: the decode's split plan at step 2 comes from the installed
+    map, so no sequence is cut short, and the attention matches the oracle."""
+    pool, _ = _make(B=2, L=1, H=2, pool_chunks=40, window=128, n_req=4)
+    B, H, D, chunk = pool.B, pool.H, pool.D, pool.chunk
+    lens = np.array([64 * 30, 64 * 30])
+    pool.fill_backing(seed=3, lens=lens + 64)
+    for snap in pool._snap:  # stale snapshots from an earlier use: nothing resident
+        snap.fill_(-1)
+    resident = [list(range(18)) + [29], list(range(18)) + [29]]
+    pool.install(lens, resident)
+    rng = np.random.RandomState(5)
+    Hq = 4
+    for _ in range(3):
+        q = torch.from_numpy(bf16.round_to_bf16(rng.standard_normal((1, B, Hq, D)).astype(np.float32))).cuda()
+        kn = torch.from_numpy(bf16.round_to_bf16(rng.standard_normal((1, B, H, D)).astype(np.float32))).cuda()
+        out = torch.empty((1, B, Hq, D), dtype=torch.bfloat16, device="cuda")
+        pool.step(q.to(torch.bfloat16), kn.to(torch.bfloat16), kn.to(torch.bfloat16), out, [], None)
+        assert pool._resident_bound() >= int((pool.chunk_slot >= 0).sum(dim=1).max().item())
+    torch.cuda.synchronize()
+    pool.check()  # a split plan sized below a resident length would have flagged a device error
+    kk, vv = pool.k.float().cpu(), pool.v.float().cpu()
+    slots = pool.chunk_slot.cpu().numpy()
+    for b in range(B):
+        length = int(pool.host_lens[b])
+        res = [c for c in range(pool.max_chunks) if slots[b, c] >= 0]
+        ks = np.concatenate([kk[0, slots[b, c], :, : min(chunk, length - c * chunk)].numpy() for c in res], axis=1)
+        vs = np.concatenate([vv[0, slots[b, c], :, : min(chunk, length - c * chunk)].numpy() for c in res], axis=1)
+        want = gqa.gqa_attention(q[0, b].float().cpu().numpy()[None, :, None, :], ks[None], vs[None], D ** -0.5)
+        np.testing.assert_allclose(out[0, b].float().cpu().numpy(), want[0, :, 0], rtol=2e-2, atol=2e-2)
+
+
+def test_tiered_pool_rejects_too_many_requests(cuda_device):
+    pool, _ = _make(n_req=2)
+    with pytest.raises(ValueError, match="staging slots"):
+        pool.prefetch([(0, 1), (0, 2), (1, 1)])

@@ -5,8 +5,10 @@ memory on the decode path (a foreign host bound through the C ABI without a
 CUDA allocator of its own, or a serving loop that must not call cudaMalloc
 between steps).  It keeps its scratch in a static device array shared by every
 call, so these tests check that two calls in a row — the second one reusing
-the scratch the first left behind — give the same output as the allocating
-entry point, and that an oversized call is refused.
+the scratch the first left behind — give exactly the output of the allocating
+entry point (the same kernel and split plan, so bit for bit), that a smaller
+call after a larger one is not disturbed by the larger call's leftovers, and
+that an oversized call is refused.
 
 The file name sorts last so that a run stopping at the first failure has run
 every other test before this one.
@@ -73,7 +75,26 @@ def test_noalloc_decode_matches_allocating_decode_twice(cuda_device, split_token
         _lib.check(rc, "snapmind_paged_gqa_decode_noalloc")
         torch.cuda.synchronize()
         pool.check()
-        torch.testing.assert_close(got.float(), want.float(), rtol=2e-2, atol=2e-2)
+        assert torch.equal(got, want), f"call {call}: allocation-free output differs from the allocating decode"
+
+
+def test_noalloc_decode_smaller_call_after_larger_call(cuda_device):
+    """A larger call (more sequences, longer contexts, more splits) leaves tickets and
+    partials in the shared scratch; the smaller call after it, and the larger one
+    again after that, still equal the allocating decode bit for bit."""
+    from snapmind_b200 import _lib
+
+    big, small = _pool(seed=5, batch=24), _pool(seed=6, batch=5)
+    for i, (pool, B, split) in enumerate(((big, 24, 64), (small, 5, 128), (big, 24, 64), (small, 5, 0))):
+        max_len = int(pool.host_lens[:B].max())
+        gen = torch.Generator(device="cuda").manual_seed(100 + i)
+        q = torch.randn(B, 32, 128, device="cuda", generator=gen).to(torch.bfloat16)
+        want = pool.decode(0, q, split_tokens=split, max_seq_len=max_len)
+        got = torch.full_like(want, float("nan"))
+        _lib.check(_noalloc(pool, q, got, split, max_len), "snapmind_paged_gqa_decode_noalloc")
+        torch.cuda.synchronize()
+        pool.check()
+        assert torch.equal(got, want), f"call {i} (batch {B}): allocation-free output differs"
 
 
 def test_noalloc_decode_rejects_oversized_scratch(cuda_device):
