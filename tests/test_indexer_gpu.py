@@ -348,3 +348,53 @@ def test_indexer_query_matches_fp64_product(cuda_device, dt, batch, d_model, out
     _lib.check(rc, "indexer_query")
     want = h.double() @ w.double().T
     np.testing.assert_allclose(out.cpu().double().numpy(), want.numpy(), rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("n_splits", [1, 2, 5])
+def test_sparse_mla_tcgen05_dtypes_and_splits(cuda_device, dt, n_splits):
+    """128 heads on the tcgen05 kernel in both 16-bit types: every chunk scored by
+    the two CTAs of a cluster (each over half of the 576 columns) and combined,
+    at split counts that leave some splits with one chunk and some with none."""
+    B, H, R, P, bs, k = 3, 128, 512, 64, 64, 6
+    lens = [64 * 9 + 33, 64 * 2, 64 * 14]
+    pool, lat, rope, tables = _latent_pool(B, lens, bs=bs, seed=61, dtype=dt)
+    selected = np.array([[0, 3, 5, 8, -1, 2], [1, 1, 0, -1, -1, -1], [13, 2, 7, 9, 4, 11]], np.int32)
+    q_lat = bf16.round_to_bf16(randn(62, (B, H, R)) * 0.05)
+    q_pe = bf16.round_to_bf16(randn(63, (B, H, P)) * 0.05)
+    scale = (128 + 64) ** -0.5
+    out = pool.sparse_decode(0, torch.from_numpy(q_lat).cuda().to(dt), torch.from_numpy(q_pe).cuda().to(dt),
+                             torch.from_numpy(selected).cuda(), sink=4, window=100, scale=scale, n_splits=n_splits)
+    pool.check()
+    got = out.float().cpu().numpy()
+    for b in range(B):
+        sel_b = [int(c) for c in selected[b] if 0 <= c < (lens[b] + bs - 1) // bs]
+        pos = omla.sparse_positions(lens[b], sel_b, bs, 4, 100)
+        want = omla.sparse_mla_decode(q_lat[b], q_pe[b], _seq_rows(lat, tables, b, lens[b], bs),
+                                      _seq_rows(rope, tables, b, lens[b], bs), pos, scale)
+        np.testing.assert_allclose(got[b], want, rtol=2e-2, atol=2e-2)
+
+
+def test_sparse_mla_tcgen05_flags_block_outside_pool(cuda_device):
+    """A table entry past the pool is skipped by the kernel (no load is issued for
+    it) and reported through the device error word; the other sequence is
+    unaffected."""
+    B, H, R, P, bs = 2, 128, 512, 64, 64
+    lens = [64 * 6, 64 * 5 + 3]
+    pool, lat, rope, tables = _latent_pool(B, lens, bs=bs, seed=71)
+    bad = pool.block_tables.clone()
+    bad[0, 2] = pool.num_blocks + 5
+    pool.block_tables.copy_(bad)
+    q_lat = torch.from_numpy(bf16.round_to_bf16(randn(72, (B, H, R)) * 0.05)).cuda().to(torch.bfloat16)
+    q_pe = torch.from_numpy(bf16.round_to_bf16(randn(73, (B, H, P)) * 0.05)).cuda().to(torch.bfloat16)
+    selected = torch.tensor([[1, 2, 3], [0, 1, 2]], dtype=torch.int32, device="cuda")
+    scale = (128 + 64) ** -0.5
+    out = pool.sparse_decode(0, q_lat, q_pe, selected, sink=4, window=64, scale=scale, n_splits=2)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="block id outside the pool"):
+        pool.check()
+    pos = omla.sparse_positions(lens[1], [0, 1, 2], bs, 4, 64)
+    want = omla.sparse_mla_decode(q_lat[1].float().cpu().numpy(), q_pe[1].float().cpu().numpy(),
+                                  _seq_rows(lat, tables, 1, lens[1], bs), _seq_rows(rope, tables, 1, lens[1], bs),
+                                  pos, scale)
+    np.testing.assert_allclose(out[1].float().cpu().numpy(), want, rtol=2e-2, atol=2e-2)
