@@ -19,6 +19,10 @@ Writes, next to this script:
                           the output is the attention result itself);
   * tiered_ops.json, mla.npz/json, indexer.npz/json — the tiered cache, MLA
                           layer and lookahead indexer driven the same way;
+  * engine_indexer.json — the reference engine's indexer cadence
+                          (GenerateEngine._run_indexer) over a tiered cache
+                          and a lookahead indexer: scores, hot set and live
+                          contents after every re-page;
   * e2e_llama.npz / e2e_llama.json — the reference ``LlamaModel`` generating
                           greedily from a seeded prompt with seeded N(0, 0.02)
                           weights (a small shape and the TinyLlama shape).
@@ -38,7 +42,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
-from inputs import digest, randn  # noqa: E402
+from inputs import digest, engine_hidden, engine_key_state, engine_repage_steps, engine_token, randn  # noqa: E402,E501
 
 
 def _bf16_bits(t):
@@ -572,6 +576,90 @@ def make_indexer(out_npz: Path, out_json: Path):
     out_json.write_text(json.dumps(meta, indent=1))
 
 
+ENGINE_CASES = [
+    # The reference engine's indexer cadence (snapmind/engine/generate.py:76-86, 112-114) over a
+    # tiered cache: the prompt is stored token-major, _run_indexer runs once after the prompt and
+    # then every `interval` decode steps.  "frozen": keys are frozen for every completed chunk
+    # before each re-page (the reference engine itself never builds them, so its indexer stays
+    # uninitialised and scores every chunk 0.5 -- the case without frozen keys).
+    {"name": "engine_uninitialised", "seed": 81, "prompt": 300, "end": 900, "interval": 64, "frozen": False,
+     "threshold": 0.5, "cache": {"max_seq_len": 2048, "n_layers": 2, "n_heads": 2, "head_dim": 16,
+                                 "pool_tokens": 256, "chunk_size": 64},
+     "indexer": {"d_model": 64, "kv_lora_rank": 32}},
+    {"name": "engine_frozen_keys", "seed": 82, "prompt": 333, "end": 1300, "interval": 64, "frozen": True,
+     "threshold": 0.5, "cache": {"max_seq_len": 2048, "n_layers": 2, "n_heads": 2, "head_dim": 16,
+                                 "pool_tokens": 256, "chunk_size": 64},
+     "indexer": {"d_model": 64, "kv_lora_rank": 32}},
+    {"name": "engine_frozen_keys_wide_pool", "seed": 83, "prompt": 200, "end": 1100, "interval": 64,
+     "frozen": True, "threshold": 0.6, "cache": {"max_seq_len": 2048, "n_layers": 3, "n_heads": 2,
+                                                  "head_dim": 16, "pool_tokens": 512, "chunk_size": 64},
+     "indexer": {"d_model": 96, "kv_lora_rank": 32}},
+]
+
+
+def make_engine_indexer(out: Path):
+    """Drive the reference TieredPagedKVCache and LookaheadSparseIndexer through the
+    reference engine's own _run_indexer (called on a stand-in holding the attributes
+    it reads) and record the scores, hot set and live contents after every re-page."""
+    from types import SimpleNamespace
+
+    import torch
+    from snapmind.core.config import IndexerConfig
+    from snapmind.engine.generate import GenerateEngine
+    from snapmind.kv_cache.tiered import TieredPagedKVCache
+    from snapmind.layers.indexer.lookahead import LookaheadSparseIndexer
+
+    data = []
+    for case in ENGINE_CASES:
+        cache = TieredPagedKVCache(**case["cache"], device="cpu")
+        torch.manual_seed(case["seed"])
+        idx = LookaheadSparseIndexer(d_model=case["indexer"]["d_model"], n_layers=24,
+                                     kv_lora_rank=case["indexer"]["kv_lora_rank"])
+        cfg = IndexerConfig(indexer_type="lookahead_sparse", indexer_interval=case["interval"],
+                            score_threshold=case["threshold"], kv_lora_rank=case["indexer"]["kv_lora_rank"])
+        engine = SimpleNamespace(_indexer=idx, _hook_states={}, _kvcache=cache, _indexer_config=cfg)
+        cache.reset()  # GenerateEngine._make_kv_cache (snapmind/engine/generate.py:88-90)
+        cache.layer_dicts()
+        chunk = case["cache"]["chunk_size"]
+        repage = set(engine_repage_steps(case))
+        frozen_done = 0
+        records, margin = [], float("inf")
+        with torch.no_grad():
+            for t in range(case["end"]):
+                for layer in range(case["cache"]["n_layers"]):
+                    k, v = engine_token(case, t, layer)
+                    cache.store(layer, torch.from_numpy(k), torch.from_numpy(v), t)
+                step = t + 1
+                if step not in repage:
+                    continue
+                if case["frozen"]:
+                    done = step // chunk
+                    ks = {c: torch.from_numpy(engine_key_state(case, c)) for c in range(frozen_done, done)}
+                    idx.build_frozen_keys(ks, list(range(frozen_done, done)))
+                    frozen_done = done
+                engine._hook_states = {lid: torch.from_numpy(h) for lid, h in engine_hidden(case, step).items()}
+                # the reference engine's own indexer step (snapmind/engine/generate.py:76-86)
+                n_ids = max(1, step // chunk)
+                scores = idx.score(engine._hook_states, list(range(n_ids)))
+                GenerateEngine._run_indexer(engine, step)
+                margin = min([margin] + [abs(float(sc) - case["threshold"]) for sc in scores.values()
+                                         if float(sc) != case["threshold"]])
+                live = cache._live_dicts
+                records.append({
+                    "step": step,
+                    "scores": {str(c): float(sc) for c, sc in scores.items()},
+                    "hot": sorted(cache._hot_set),
+                    "chunks": sorted(cache._chunks),
+                    "total_tokens": cache._total_tokens,
+                    "live": None if live is None else {str(i): _live_record(e["k"], e["v"]) for i, e in live.items()},
+                })
+        if case["frozen"]:
+            assert margin > 1e-3, f"{case['name']}: a score within {margin} of the threshold; pick another seed"
+        data.append({**case, "threshold_margin": margin, "records": records})
+        print(f"engine {case['name']}: {len(records)} re-pages, hot after last {records[-1]['hot']}")
+    out.write_text(json.dumps(data, indent=1))
+
+
 SLIDING_OPS = [  # (op, layer, tokens or keep, seed)
     ("store", 0, 5, 401), ("store", 1, 3, 402), ("store", 0, 1, 403), ("store", 0, 9, 404),
     ("store", 1, 20, 405), ("store", 0, 1, 406), ("evict", None, 0, None), ("store", 1, 1, 407),
@@ -696,14 +784,15 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SNAPMIND_REFERENCE", "/root/reference"))
     ap.add_argument("--only", nargs="*", default=None,
-                    help="fixtures to regenerate: paged, gqa, tiered, mla, indexer, e2e, sliding (default: all)")
+                    help="fixtures to regenerate: paged, gqa, tiered, mla, indexer, engine, e2e, sliding "
+                         "(default: all)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     sys.path.insert(0, str(HERE.parent))
     import torch
 
     torch.set_num_threads(4)
-    want = set(args.only) if args.only else {"paged", "gqa", "tiered", "mla", "indexer", "e2e", "sliding"}
+    want = set(args.only) if args.only else {"paged", "gqa", "tiered", "mla", "indexer", "engine", "e2e", "sliding"}
     if "paged" in want:
         make_paged_ops(HERE / "paged_ops.json")
         make_paged_batched(HERE / "paged_batched.json")
@@ -715,6 +804,8 @@ def main():
         make_mla(HERE / "mla.npz", HERE / "mla.json")
     if "indexer" in want:
         make_indexer(HERE / "indexer.npz", HERE / "indexer.json")
+    if "engine" in want:
+        make_engine_indexer(HERE / "engine_indexer.json")
     if "e2e" in want:
         make_e2e(HERE / "e2e_llama.npz", HERE / "e2e_llama.json")
     if "sliding" in want:

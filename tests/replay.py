@@ -5,7 +5,7 @@ from __future__ import annotations
 import json
 from pathlib import Path
 
-from inputs import digest, randn
+from inputs import digest, engine_hidden, engine_key_state, engine_token, randn
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
@@ -182,3 +182,62 @@ def _check_live(k, v, rec, to_numpy, where):
     assert list(k.shape) == rec["shape"], f"{where}: {tuple(k.shape)} vs {rec['shape']}"
     assert digest(to_numpy(k)) == rec["k"], f"{where}: K differs"
     assert digest(to_numpy(v)) == rec["v"], f"{where}: V differs"
+
+
+# ---- the engine's indexer cadence over a tiered cache (engine_indexer.json)
+def load_engine_indexer():
+    return json.loads((GOLDEN / "engine_indexer.json").read_text())
+
+
+def engine_run_indexer(score, hook_states, kvcache, step, threshold, chunk_size=64):
+    """GenerateEngine._run_indexer (snapmind/engine/generate.py:76-86), restated:
+    score chunks 0 .. max(1, step // chunk_size) - 1 from the hooked hidden states,
+    then re-page the cache at the configured threshold."""
+    if score is None or not hook_states:
+        return None
+    chunk_ids = list(range(max(1, step // chunk_size)))
+    scores = score(hook_states, chunk_ids)
+    if hasattr(kvcache, "score_and_repage"):
+        kvcache.score_and_repage(scores, threshold=threshold)
+    return scores
+
+
+def replay_engine_indexer(case, cache, indexer, to_input, to_numpy, state_of, live_of, score_tol):
+    """Drive ``cache`` and ``indexer`` the way the reference engine does (stores of every
+    layer per token, frozen keys of completed chunks, the indexer step at the recorded
+    steps) and check the scores, hot set, chunk ids, token count and live contents
+    after every re-page against the reference's record."""
+    chunk = case["cache"]["chunk_size"]
+    recs = {r["step"]: r for r in case["records"]}
+    cache.reset()
+    cache.layer_dicts()
+    frozen_done = 0
+    for t in range(case["end"]):
+        for layer in range(case["cache"]["n_layers"]):
+            k, v = engine_token(case, t, layer)
+            cache.store(layer, to_input(k), to_input(v), t)
+        step = t + 1
+        if step not in recs:
+            continue
+        rec = recs[step]
+        where = f"{case['name']} step {step}"
+        if case["frozen"]:
+            done = step // chunk
+            ids = list(range(frozen_done, done))
+            indexer.build_frozen_keys({c: to_input(engine_key_state(case, c)) for c in ids}, ids)
+            frozen_done = done
+        hidden = {lid: to_input(h) for lid, h in engine_hidden(case, step).items()}
+        scores = engine_run_indexer(indexer.score, hidden, cache, step, case["threshold"], chunk)
+        assert sorted(scores) == sorted(int(c) for c in rec["scores"]), where
+        for c, want in rec["scores"].items():
+            got = float(scores[int(c)])
+            assert abs(got - want) <= score_tol, f"{where}: chunk {c} score {got} vs {want}"
+        hot, chunks, total = state_of(cache)
+        assert sorted(hot) == rec["hot"], f"{where}: hot {sorted(hot)} vs {rec['hot']}"
+        assert sorted(chunks) == rec["chunks"], where
+        assert total == rec["total_tokens"], where
+        live = live_of(cache)
+        for i in range(case["cache"]["n_layers"]):
+            e = live[i]
+            _check_live(e["k"], e["v"], rec["live"][str(i)], to_numpy, f"{where} layer {i}")
+    assert frozen_done > 0 or not case["frozen"]
