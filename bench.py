@@ -208,8 +208,15 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": r["workload"]},
                 "e2e_llama": r}
     if args.only in ("tiered", "mla"):
-        fn = run_tiered if args.only == "tiered" else run_mla_sparse
-        r = fn(args, dev, seed, dist, world)
+        if args.only == "tiered":
+            r = run_tiered(args, dev, seed, dist, world)
+        else:
+            r = run_mla_sparse(args, dev, seed, dist, world, cpu_baseline=not args.no_cpu_baseline and world == 1)
+        if "omitted" in r:
+            return {"metric": METRIC, "value": None, "unit": "tok/s", "n_gpus": world, "steps": steps,
+                    "warmup": warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": {"workload": "tiered"},
+                    args.only: r}
         return {"metric": METRIC, "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": steps,
                 "warmup": warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": {"workload": r["workload"]},
@@ -247,17 +254,18 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
     def decode_step(events=None):
         pool.reserve(1, batch=DECODE_BATCH)
         for layer in range(L):
-            pool.append(layer, k_all[layer], v_all[layer])
+            # the layer's new token is stored by the decode launch itself (no append launch)
             if events is not None:
                 events[layer][0].record()
-            pool.decode(layer, q_all[layer], out=out[layer], max_seq_len=max_len, split_tokens=split)
+            pool.decode(layer, q_all[layer], out=out[layer], max_seq_len=max_len, split_tokens=split,
+                        append=(k_all[layer], v_all[layer]))
             if events is not None:
                 events[layer][1].record()
 
     for _ in range(warmup):
         decode_step()
     pool.check()
-    launches_per_step = 1 + 2 * L
+    launches_per_step = 1 + L
     kv_tokens_before = int(pool.host_lens[:DECODE_BATCH].sum())
     ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
           for _ in range(steps)]
@@ -275,10 +283,12 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
     pool.check()
     ms_max = reduce_max(dist, ms, dev)
     kernel_ms = [e0.elapsed_time(e1) for row in ev for (e0, e1) in row]
-    # algorithmic bytes of one decode launch: every cached K and V row once, q in, out back;
+    # algorithmic bytes of one decode launch: every cached K and V row once (the new token's
+    # included), q in, out back, and the new K and V rows read and stored;
     # step s (1-based) attends over kv_tokens_before + s * batch tokens
     mean_ctx_tokens = kv_tokens_before + DECODE_BATCH * (steps + 1) / 2.0
-    bytes_per_launch = mean_ctx_tokens * H * D * ELEM * 2 + 2 * DECODE_BATCH * HQ * D * ELEM
+    bytes_per_launch = (mean_ctx_tokens * H * D * ELEM * 2 + 2 * DECODE_BATCH * HQ * D * ELEM
+                        + 2 * 2 * DECODE_BATCH * H * D * ELEM)
     kernel_avg_ms = statistics.fmean(kernel_ms)
     achieved_gbs = bytes_per_launch / (kernel_avg_ms * 1e-3) / 1e9
     pk = peaks()
@@ -321,8 +331,8 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
         compute.wait_event(ev_out[i])  # the outputs of two steps ago are on the host
         pool.reserve(1, batch=DECODE_BATCH)
         for layer in range(L):
-            pool.append(layer, kd[layer], vd[layer])
-            pool.decode(layer, qd[layer], out=od[layer], max_seq_len=max_len, split_tokens=split)
+            pool.decode(layer, qd[layer], out=od[layer], max_seq_len=max_len, split_tokens=split,
+                        append=(kd[layer], vd[layer]))
         ev_done[i].record(compute)
         with torch.cuda.stream(d2h_stream):
             d2h_stream.wait_event(ev_done[i])
@@ -371,7 +381,7 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
         "data": "synthetic (seeded N(0,1) K/V/q, seeded context lengths and shuffled block tables)",
         "config": decode_config(world),
         "roofline": {
-            "kernel": "paged_gqa_decode",
+            "kernel": "paged_gqa_decode (with the step's K/V append fused in)",
             "bound": "hbm",
             "achieved": round(achieved_gbs, 1),
             "peak": pk["hbm_gbs"],
@@ -391,7 +401,9 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
         },
         "kv_append_gather": ag,
         "tiered": run_tiered(args, dev, seed, dist, world) if args.only == "all" else None,
-        "mla_sparse": run_mla_sparse(args, dev, seed, dist, world) if args.only == "all" else None,
+        "mla_sparse": run_mla_sparse(args, dev, seed, dist, world,
+                                     cpu_baseline=not args.no_cpu_baseline and world == 1)
+        if args.only == "all" else None,
         "e2e_llama": run_e2e_llama(args, dev, seed, dist, world, cpu_baseline=not args.no_cpu_baseline and world == 1)
         if args.only == "all" else None,
         "gpu_launches": launches_per_step * steps,
@@ -580,11 +592,19 @@ def run_tiered(args, dev, seed, dist, world) -> dict:
 
     from snapmind_b200.tiered_pool import TieredKVPool
 
-    # every chunk lives in host-pinned backing (4 GiB per 32768-token sequence at this
-    # shape): bound the batch by the host memory the ranks of this node share
+    # every chunk lives in host-pinned backing (4.5 GB per 32768-token sequence at this
+    # shape).  The batch per rank is held fixed across GPU counts (weak scaling compares
+    # like with like): when the ranks of this node cannot all pin it, every rank leaves
+    # the line out instead of shrinking it.
     per_seq = TIER_L * 2 * H * D * 2 * (TIER_CTX + 4096)
     local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
-    B = max(1, min(args.tiered_batch, int(0.4 * host_memory_budget() / local_world / per_seq)))
+    B = max(1, args.tiered_batch)
+    fits = B * per_seq <= 0.4 * host_memory_budget() / local_world
+    if not all_ranks(dist, fits, dev):
+        return {"omitted": f"{B} sequences x {per_seq / 1e9:.1f} GB of pinned host backing per rank x "
+                           f"{local_world} ranks exceed this host's free memory; the batch per rank is held "
+                           "fixed across GPU counts, so the line is left out rather than shrunk",
+                "batch_per_gpu": B}
     steps = min(args.steps, 100)
     warmup = args.warmup
     max_tokens = TIER_CTX + 2 * (steps + warmup) + 2 * TIER_CHUNK
@@ -691,7 +711,73 @@ def run_tiered(args, dev, seed, dist, world) -> dict:
 MLA_B, MLA_CTX, MLA_HEADS, MLA_RANK, MLA_ROPE, MLA_CHUNK, MLA_TOPK, MLA_DMODEL = 8, 131072, 128, 512, 64, 64, 32, 7168
 
 
-def run_mla_sparse(args, dev, seed, dist, world) -> dict:
+def attended_positions(length: int, selected: list[int], chunk: int, sink: int, window: int) -> int:
+    """How many positions one query attends: the sink prefix, the recent window and
+    the selected chunks, each position once."""
+    pos = np.zeros(length, bool)
+    pos[: min(sink, length)] = True
+    pos[max(0, length - window):] = True
+    for c in selected:
+        if 0 <= c * chunk < length:
+            pos[c * chunk: (c + 1) * chunk] = True
+    return int(pos.sum())
+
+
+def mla_cpu_baseline(seed: int, n_seqs: int = 2, steps: int = 3) -> dict:
+    """The step's chunk selection and sparse attention restated on the host (the oracle
+    port): sigmoid-gated scores of every chunk key, stable top-32, then the absorbed
+    MLA attention over the attended rows, per sequence, in float64 numpy with the
+    host's BLAS threads.  A bounded sample: ``n_seqs`` sequences of the workload's
+    length, ``steps`` timed steps after one warm-up."""
+    import oracle.indexer as oidx
+    import oracle.mla as omla
+
+    rng = np.random.default_rng(seed + 60)
+    n_chunks = MLA_CTX // MLA_CHUNK
+    seqs = []
+    for _ in range(n_seqs):
+        sq = {
+            "keys": rng.standard_normal((n_chunks, 128), dtype=np.float32),
+            "q_idx": rng.standard_normal(128, dtype=np.float32),
+            "q_lat": (rng.standard_normal((MLA_HEADS, MLA_RANK), dtype=np.float32) * 0.05),
+            "q_pe": (rng.standard_normal((MLA_HEADS, MLA_ROPE), dtype=np.float32) * 0.05),
+            # full-length caches; only the rows the selection attends are ever read, so
+            # only those are filled (the rest stay untouched zero pages)
+            "latent": np.zeros((MLA_CTX, MLA_RANK), np.float32),
+            "rope": np.zeros((MLA_CTX, MLA_ROPE), np.float32),
+        }
+        sc = oidx.sigmoid_scores(sq["q_idx"], sq["keys"], 128 ** -0.5, 0.1)
+        pos = omla.sparse_positions(MLA_CTX, [int(c) for c in oidx.stable_topk(sc, MLA_TOPK)], MLA_CHUNK, 4, 1024)
+        sq["latent"][pos] = rng.standard_normal((len(pos), MLA_RANK), dtype=np.float32)
+        sq["rope"][pos] = rng.standard_normal((len(pos), MLA_ROPE), dtype=np.float32)
+        seqs.append(sq)
+    scale = (128 + 64) ** -0.5
+
+    def step():
+        for sq in seqs:
+            sc = oidx.sigmoid_scores(sq["q_idx"], sq["keys"], 128 ** -0.5, 0.1)
+            top = [int(c) for c in oidx.stable_topk(sc, MLA_TOPK) if c >= 0]
+            pos = omla.sparse_positions(MLA_CTX, top, MLA_CHUNK, 4, 1024)
+            # gather the attended rows first, then widen (not the whole cache)
+            omla.sparse_mla_decode(sq["q_lat"], sq["q_pe"], sq["latent"][pos], sq["rope"][pos],
+                                   np.arange(len(pos)), scale)
+
+    step()
+    ts = []
+    for _ in range(steps):
+        t = time.perf_counter()
+        step()
+        ts.append(time.perf_counter() - t)
+    per_step = statistics.median(ts)
+    return {"value": round(n_seqs / per_step, 2), "unit": "tok/s (one MLA layer)", "cores": os.cpu_count() or 1,
+            "kind": "port",
+            "sample": f"{n_seqs} sequences x {MLA_CTX} tokens: sigmoid scores of {n_chunks} chunk keys, stable "
+                      f"top-{MLA_TOPK}, absorbed MLA attention over the selected chunks + 4-token sink + "
+                      f"1024-token window (float64 numpy, host BLAS threads); median of {steps} steps",
+            "step_s": round(per_step, 4)}
+
+
+def run_mla_sparse(args, dev, seed, dist, world, cpu_baseline: bool = False) -> dict:
     """One MLA layer at DeepSeek shape (128 heads, kv_lora_rank 512, rope 64, bf16), 8 seqs
     of 131072 tokens in the paged latent pool (block = 64-token chunk).  A step: reserve and
     append one latent row per sequence, add the key of a chunk that just completed, score
@@ -831,9 +917,25 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
 
     select_us = graph_us(lambda: sel.select(qsel, n_chunks_dev, k=MLA_TOPK))
     sparse_us = graph_us(lambda: pool.sparse_decode(0, q_lat, q_pe, idx0, sink=4, window=1024, scale=scale))
-    # attended rows per sequence: top-k chunks + the sink chunk + the window chunks (about)
-    att_tokens = B * (MLA_TOPK * MLA_CHUNK + MLA_CHUNK + 1024 + MLA_CHUNK)
-    sparse_bytes = att_tokens * (MLA_RANK + MLA_ROPE) * 2
+    # the dominant kernel (sparse attention + its split merge), each launch timed alone on the
+    # launching stream after an L2 flush: the ~29 MB it reads would otherwise stay in the 126 MB L2
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    evs = []
+    for _ in range(20):
+        flush.zero_()
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        pool.sparse_decode(0, q_lat, q_pe, idx0, sink=4, window=1024, scale=scale)
+        b_.record()
+        evs.append((a_, b_))
+    torch.cuda.synchronize(dev)
+    del flush
+    attn_us = statistics.fmean(a_.elapsed_time(b_) for a_, b_ in evs) * 1e3
+    # algorithmic work of one launch: every attended row (selected chunks, sink, window) read
+    # once at 1152 B and scored + accumulated by 128 heads; q in, latent output out
+    length = int(pool.host_lens[0])
+    att_tokens = sum(attended_positions(length, idx0[b].tolist(), MLA_CHUNK, 4, 1024) for b in range(B))
+    sparse_bytes = att_tokens * (MLA_RANK + MLA_ROPE) * 2 + B * MLA_HEADS * (MLA_RANK + MLA_ROPE + MLA_RANK) * 2
     sparse_flops = att_tokens * MLA_HEADS * 2 * ((MLA_RANK + MLA_ROPE) + MLA_RANK)
     key_bytes = B * (int(pool.host_lens[0]) // MLA_CHUNK) * 128 * 4
     # full latent gather and all-chunk key pooling (HBM-bound)
@@ -855,6 +957,27 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
     gather_bytes = 2 * B * length * (MLA_RANK + MLA_ROPE) * 2  # read pool + write output
     pool_bytes = B * (length // MLA_CHUNK) * MLA_CHUNK * MLA_RANK * 2
     pk = peaks()
+    t_hbm = sparse_bytes / (pk["hbm_gbs"] * 1e9)
+    t_tc = sparse_flops / (pk["bf16_tflops"] * 1e12) if pk.get("bf16_tflops") else 0.0
+    traffic = profile_traffic("sparse_mla")
+    roofline = {
+        "kernel": "sparse_mla_umma_kernel + sparse_mla_merge_kernel",
+        "bound": "hbm" if t_hbm >= t_tc else "tensor",
+        "achieved": round(sparse_bytes / (attn_us * 1e-6) / 1e9, 1) if t_hbm >= t_tc
+        else round(sparse_flops / (attn_us * 1e-6) / 1e12, 1),
+        "peak": pk["hbm_gbs"] if t_hbm >= t_tc else pk["bf16_tflops"],
+        "peak_source": pk["source"],
+        "unit": "GB/s" if t_hbm >= t_tc else "TFLOP/s",
+        "frac": round(max(t_hbm, t_tc) / (attn_us * 1e-6), 4),
+        "hbm_frac": round(t_hbm / (attn_us * 1e-6), 4),
+        "tensor_frac": round(t_tc / (attn_us * 1e-6), 4) if t_tc else None,
+        "traffic": None if traffic is None else traffic.get("bytes_per_launch_scaled"),
+        "algorithmic_bytes_per_launch": int(sparse_bytes),
+        "flops_per_launch": int(sparse_flops),
+        "attended_tokens_per_launch": int(att_tokens),
+        "kernel_us_avg": round(attn_us, 2),
+        "timing": "20 launches, each after a 256 MB L2 flush, CUDA events on the launching stream",
+    }
     res = {
         "value": round(B * world * steps / (ms * 1e-3), 1),
         "unit": "tok/s (one MLA layer)",
@@ -874,7 +997,10 @@ def run_mla_sparse(args, dev, seed, dist, world) -> dict:
         "sparse_attn_tflops": round(sparse_flops / (sparse_us * 1e-6) / 1e12, 2),
         "sparse_attn_tensor_frac": round(sparse_flops / (sparse_us * 1e-6) / 1e12 / pk["bf16_tflops"], 4)
         if pk.get("bf16_tflops") else None,
+        "roofline": roofline,
     }
+    if cpu_baseline:
+        res["cpu_baseline"] = mla_cpu_baseline(seed)
     del pool, lo, ro
     torch.cuda.empty_cache()
     return res
@@ -972,10 +1098,12 @@ def run_append_gather(args, dev, seed, dist, world) -> dict:
 def run_head_shard(args, dev, dist, world) -> dict:
     """KV-head-sharded decode: every rank serves the same batch with H/N kv heads.
 
-    Three timings per layer call over the same shards: the local decode alone,
-    the decode + NCCL all-gather of the head slices (+ reorder), and the decode
-    whose epilogue stores the rows into every rank's buffer over NVLink + the
-    bounded epoch wait.  Whole-job throughput counts each sequence's token once
+    Timings of one step (all layers) over the same shards: the local decodes
+    alone; per layer, the decode + NCCL all-gather of the head slices (+ reorder)
+    and the decode whose epilogue stores the rows into every rank's buffer over
+    NVLink + the bounded epoch wait; and both with one exchange for the whole
+    step (one all-gather of every layer's slices, or one epoch signal and wait
+    after the last layer's peer stores).  Whole-job throughput counts each sequence's token once
     (all ranks serve the same sequences)."""
     import torch
 
@@ -1002,7 +1130,7 @@ def run_head_shard(args, dev, dist, world) -> dict:
     local = torch.empty((B, HQ // world, D), device=dev, dtype=torch.bfloat16)
     max_len = int(lens.max())
     nccl = HeadShardedDecode(pool, HQ, world, rank)
-    fused = PeerHeadShardedDecode(pool, HQ, world, rank, max_batch=B)
+    fused = PeerHeadShardedDecode(pool, HQ, world, rank, max_batch=B, n_layers=L)
     steps, warmup = args.steps, max(args.warmup, 3)
 
     def step_local():
@@ -1016,6 +1144,13 @@ def run_head_shard(args, dev, dist, world) -> dict:
     def step_fused():
         for layer in range(L):
             fused.decode(layer, q_all[layer], out=out[layer], max_seq_len=max_len)
+
+    # one exchange per step: the outputs of all layers in one all-gather / one epoch signal
+    def step_nccl_per_step():
+        nccl.decode_step(q_all, out=out, max_seq_len=max_len)
+
+    def step_fused_per_step():
+        fused.decode_step(q_all, max_seq_len=max_len)
 
     def timed(fn) -> float:
         for _ in range(warmup):
@@ -1035,9 +1170,13 @@ def run_head_shard(args, dev, dist, world) -> dict:
     ms_nccl = timed(step_nccl)
     ref = out.clone()
     ms_fused = timed(step_fused)
+    same = bool(torch.equal(out, ref))
+    ms_nccl_step = timed(step_nccl_per_step)
+    same = same and bool(torch.equal(out, ref))
+    ms_fused_step = timed(step_fused_per_step)
+    same = same and bool(torch.equal(fused.decode_step(q_all, max_seq_len=max_len), ref))
     fused.check()
     pool.check()
-    same = bool(torch.equal(out, ref))
     fused.close()
     kv_bytes = float(lens.sum()) * (hi - lo) * D * ELEM * 2 * L  # this rank's K/V rows per step
     pk = peaks()
@@ -1050,9 +1189,13 @@ def run_head_shard(args, dev, dist, world) -> dict:
         "ms_per_step_local_decode_only": round(ms_local, 4),
         "ms_per_step_nccl_all_gather": round(ms_nccl, 4),
         "ms_per_step_fused_peer_stores": round(ms_fused, 4),
+        "ms_per_step_nccl_one_gather_per_step": round(ms_nccl_step, 4),
+        "ms_per_step_fused_one_signal_per_step": round(ms_fused_step, 4),
         "exposed_exchange_us_per_layer": {
             "nccl": round((ms_nccl - ms_local) * 1e3 / L, 2),
             "fused": round((ms_fused - ms_local) * 1e3 / L, 2),
+            "nccl_one_gather_per_step": round((ms_nccl_step - ms_local) * 1e3 / L, 2),
+            "fused_one_signal_per_step": round((ms_fused_step - ms_local) * 1e3 / L, 2),
         },
         "fused_equals_nccl": same,
         "exchange_bytes_per_layer_per_rank": B * (HQ // world) * D * ELEM * (world - 1),
@@ -1065,7 +1208,8 @@ def run_head_shard(args, dev, dist, world) -> dict:
             "unit": "GB/s",
             "frac": round(kv_bytes / (ms_fused * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
         },
-        "gpu_launches_per_step": {"local": L, "nccl": 3 * L, "fused": 2 * L},
+        "gpu_launches_per_step": {"local": L, "nccl": 3 * L, "fused": 2 * L, "nccl_one_gather_per_step": L + 2,
+                                  "fused_one_signal_per_step": L + 1},
     }
     del pool
     torch.cuda.empty_cache()
@@ -1075,6 +1219,17 @@ def run_head_shard(args, dev, dist, world) -> dict:
 def barrier(dist):
     if dist is not None:
         dist.barrier()
+
+
+def all_ranks(dist, flag: bool, dev) -> bool:
+    """True when ``flag`` holds on every rank (the same answer on all of them)."""
+    if dist is None:
+        return bool(flag)
+    import torch
+
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
 
 
 def reduce_max(dist, x: float, dev) -> float:

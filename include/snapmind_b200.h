@@ -370,6 +370,32 @@ SNAPMIND_API int snapmind_paged_gqa_decode(const void *q, int64_t q_stride_seq, 
                               void *stream);
 
 /*
+ * snapmind_paged_gqa_decode with this step's token stored by the same launch:
+ * replaces snapmind_kv_append of one token per sequence (PagedKVCache.store,
+ * snapmind/kv_cache/paged.py:34-54) followed by snapmind_paged_gqa_decode
+ * (the attention of snapmind/layers/attention/gqa.py:62-85, whose cache
+ * concatenation the store stands for).  seq_lens already counts the token
+ * (after the reserve that gave it a slot): k_new[b] / v_new[b]
+ * ([batch][n_kv_heads][head_dim] in the pool's dtype, element strides
+ * new_stride_seq / new_stride_head, head dim contiguous) are written at
+ * position seq_lens[b] - 1 of sequence b, then every sequence attends over its
+ * seq_lens[b] tokens.  On the tensor-core path the split holding that
+ * position writes the rows before its loads; elsewhere the append kernel runs
+ * first on the same stream.  The stored bytes equal snapmind_kv_append's.
+ */
+SNAPMIND_API int snapmind_paged_gqa_decode_append(const void *q, int64_t q_stride_seq, int64_t q_stride_head,
+                                     void *k_pool, void *v_pool, int dtype,
+                                     const int32_t *block_tables, int64_t table_stride_seq,
+                                     int32_t table_width, const int32_t *seq_lens,
+                                     const void *k_new, const void *v_new, int64_t new_stride_seq,
+                                     int64_t new_stride_head, void *out, int64_t out_stride_seq,
+                                     int64_t out_stride_head, float scale, int32_t batch, int32_t n_q_heads,
+                                     int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+                                     int32_t num_blocks, int32_t max_seq_len, int32_t split_tokens,
+                                     int32_t flags, void *workspace, int64_t workspace_bytes,
+                                     int32_t *err_word, void *stream);
+
+/*
  * snapmind_paged_gqa_decode over a window of each sequence: sequence b attends
  * to tokens [seq_starts[b], seq_lens[b]) of its table row (seq_starts: int32,
  * device, one entry per sequence; a start at or past the length gives a zero

@@ -108,6 +108,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _i64, _i64, _p, _p, _int, _p, _i64, _i32, _p, _p, _i64, _i64, _f32, _i32, _i32, _i32,
          _i32, _i32, _i32, _i32, _i32, _i32, _p, _i64, _p, _p],
     ),
+    "snapmind_paged_gqa_decode_append": (
+        _int,
+        [_p, _i64, _i64, _p, _p, _int, _p, _i64, _i32, _p, _p, _p, _i64, _i64, _p, _i64, _i64, _f32, _i32,
+         _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _p, _i64, _p, _p],
+    ),
     "snapmind_paged_gqa_decode_window": (
         _int,
         [_p, _i64, _i64, _p, _p, _int, _p, _i64, _i32, _p, _p, _p, _i64, _i64, _f32, _i32, _i32, _i32,

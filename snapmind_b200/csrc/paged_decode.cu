@@ -360,7 +360,8 @@ static int decode_entry(const void* q, int64_t q_stride_seq, int64_t q_stride_he
                         int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
                         int32_t num_blocks, int32_t max_seq_len, int32_t split_tokens, int32_t flags,
                         void* workspace, int64_t workspace_bytes, int32_t* err_word, void* stream,
-                        const PeerArgs* peers = nullptr) {
+                        const PeerArgs* peers = nullptr, const void* new_k = nullptr,
+                        const void* new_v = nullptr, int64_t new_stride_seq = 0, int64_t new_stride_head = 0) {
   SNAPMIND_CHECK_ARG(dtype_size(dtype) > 0, "paged_decode: unknown dtype");
   SNAPMIND_CHECK_ARG(batch >= 0 && n_q_heads > 0 && n_kv_heads > 0 && head_dim > 0 &&
                          head_dim <= 256 && block_size > 0 && num_blocks > 0 && table_width >= 0,
@@ -423,12 +424,25 @@ static int decode_entry(const void* q, int64_t q_stride_seq, int64_t q_stride_he
     p.n_peers = peers->n;
     p.head_offset = peers->head_offset;
   }
+  p.new_k = new_k;
+  p.new_v = new_v;
+  p.new_stride_seq = new_stride_seq;
+  p.new_stride_head = new_stride_head;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   if (!(flags & SNAPMIND_DECODE_FORCE_GENERIC)) {
     int rc = SNAPMIND_ERR_UNSUPPORTED;
     if (decode_fast_supported(p, dtype)) rc = launch_decode_fast(p, dtype, st);
     if (rc != SNAPMIND_ERR_UNSUPPORTED) return rc;
+  }
+  if (new_k != nullptr) {
+    // the CUDA-core kernel attends only: store the token with the append kernel first
+    const int rc = snapmind_kv_append(const_cast<void*>(k_pool), const_cast<void*>(v_pool), dtype, 0, new_k, new_v,
+                                      dtype, 0, new_stride_seq, new_stride_head, 0, block_tables, table_stride_seq,
+                                      0, table_width, seq_lens, -1, 1, batch, 1, n_kv_heads, head_dim, block_size,
+                                      num_blocks, err_word, stream);
+    if (rc != SNAPMIND_OK) return rc;
+    p.new_k = p.new_v = nullptr;
   }
   dim3 grid(p.max_splits, n_kv_heads, batch);
   SNAPMIND_CHECK_ARG(grid.y <= 65535 && grid.z <= 65535, "paged_decode: grid too large");
@@ -455,6 +469,23 @@ int snapmind_paged_gqa_decode(const void* q, int64_t q_stride_seq, int64_t q_str
                       table_width, seq_lens, nullptr, out, out_stride_seq, out_stride_head, scale, batch,
                       n_q_heads, n_kv_heads, head_dim, block_size, num_blocks, max_seq_len, split_tokens, flags,
                       workspace, workspace_bytes, err_word, stream);
+}
+
+int snapmind_paged_gqa_decode_append(const void* q, int64_t q_stride_seq, int64_t q_stride_head, void* k_pool,
+                                     void* v_pool, int dtype, const int32_t* block_tables, int64_t table_stride_seq,
+                                     int32_t table_width, const int32_t* seq_lens, const void* k_new,
+                                     const void* v_new, int64_t new_stride_seq, int64_t new_stride_head, void* out,
+                                     int64_t out_stride_seq, int64_t out_stride_head, float scale, int32_t batch,
+                                     int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+                                     int32_t num_blocks, int32_t max_seq_len, int32_t split_tokens, int32_t flags,
+                                     void* workspace, int64_t workspace_bytes, int32_t* err_word, void* stream) {
+  SNAPMIND_CHECK_ARG(k_new != nullptr && v_new != nullptr, "paged_decode_append: k_new / v_new is NULL");
+  SNAPMIND_CHECK_ARG(out != nullptr, "paged_decode_append: out is NULL");
+  return decode_entry(q, q_stride_seq, q_stride_head, k_pool, v_pool, dtype, block_tables, table_stride_seq,
+                      table_width, seq_lens, nullptr, out, out_stride_seq, out_stride_head, scale, batch,
+                      n_q_heads, n_kv_heads, head_dim, block_size, num_blocks, max_seq_len, split_tokens, flags,
+                      workspace, workspace_bytes, err_word, stream, nullptr, k_new, v_new, new_stride_seq,
+                      new_stride_head);
 }
 
 int snapmind_paged_gqa_decode_window(const void* q, int64_t q_stride_seq, int64_t q_stride_head,

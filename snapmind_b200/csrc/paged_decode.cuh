@@ -27,6 +27,11 @@ struct DecodeParams {
   // n_peers = 0: the local `out` only
   void* const* peer_out = nullptr;       // [n_peers] output bases, rank order (own buffer included)
   int32_t n_peers = 0, head_offset = 0;  // q heads of this launch start at head_offset globally
+  // the token at position seq_lens[b] - 1 of every sequence, [batch][n_kv_heads][head_dim] in
+  // the pool's dtype, stored into the pool by the decode itself before it attends (NULL: none)
+  const void* new_k = nullptr;
+  const void* new_v = nullptr;
+  int64_t new_stride_seq = 0, new_stride_head = 0;  // elements
 };
 
 // Destinations of a decode whose outputs go straight to several GPUs.

@@ -172,6 +172,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (len < 0) len = 0;
   const int skip = p.seq_start ? max(0, p.seq_start[b]) : 0;  // tokens before the window start
   int n_splits = (len + p.split_tokens - 1) / p.split_tokens;
+  const int new_pos = len - 1;  // the position of this step's token, when the launch stores it
   if (n_splits > p.max_splits) {
     if (s == 0 && threadIdx.x == 0) flag_error(p.err, SNAPMIND_DEVERR_SPLIT);
     n_splits = p.max_splits;
@@ -221,6 +222,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       flag_error(p.err, SNAPMIND_DEVERR_TABLE);
     }
     S.table[j] = phys;
+  }
+  if (p.new_k != nullptr && warp == 0 && new_pos >= t0 && new_pos < t1) {
+    // this split holds the step's token: store its K and V rows of head kvh into the pool
+    // (lanes 0-15 K, 16-31 V, 16 bytes each), then make them visible to the TMA loads below
+    const int jj = new_pos / BS;
+    const int32_t phys = jj < p.table_width ? trow_ptr[jj] : -1;
+    if (phys >= 0 && phys < p.num_blocks) {
+      const bool is_v = lane >= 16;
+      const T* src = reinterpret_cast<const T*>(is_v ? p.new_v : p.new_k) + (int64_t)b * p.new_stride_seq +
+                     (int64_t)kvh * p.new_stride_head + (lane & 15) * 8;
+      T* dst = reinterpret_cast<T*>(const_cast<void*>(is_v ? p.v_pool : p.k_pool)) +
+               (((int64_t)phys * p.n_kv_heads + kvh) * BS + new_pos % BS) * kD + (lane & 15) * 8;
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
   }
   __syncthreads();
 
@@ -539,6 +555,10 @@ bool decode_fast_supported(const DecodeParams& p, int dtype) {
   if (p.q_stride_head % 2 != 0 || p.q_stride_seq % 2 != 0) return false;
   if ((reinterpret_cast<uintptr_t>(p.q) & 3) != 0) return false;
   if ((reinterpret_cast<uintptr_t>(p.k_pool) & 15) != 0 || (reinterpret_cast<uintptr_t>(p.v_pool) & 15) != 0)
+    return false;
+  if (p.new_k != nullptr &&  // the stored rows move as 16-byte vectors
+      (((reinterpret_cast<uintptr_t>(p.new_k) | reinterpret_cast<uintptr_t>(p.new_v)) & 15) != 0 ||
+       p.new_stride_seq % 8 != 0 || p.new_stride_head % 8 != 0 || p.seq_start != nullptr || p.n_peers > 0))
     return false;
   if ((int64_t)p.num_blocks * p.n_kv_heads * p.block_size >= (int64_t)1 << 31) return false;
   if (p.batch > 65535 || p.n_kv_heads > 65535) return false;

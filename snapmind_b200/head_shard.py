@@ -18,6 +18,14 @@ mappings), so the rows land in place while other CTAs are still attending.
 One warp after it publishes the call's epoch into every rank's flag array and
 waits (bounded) for all ranks' epochs.  No collective launch, no gathered
 copy, no reorder.
+
+Both offer ``decode_step``: every layer of one decode step (``q [L, B, Hq, D]``)
+with one exchange for the whole step instead of one per layer -- one
+all-gather of ``[L, B, Hq/N, D]`` for the NCCL form, and for the peer-store
+form every layer's rows stored into that layer's slice of an
+``[L, B, Hq, D]`` receive region, followed by a single epoch signal and wait.
+It suits callers whose consumer of the outputs runs after the whole step; a
+model layer that needs layer l's heads before layer l + 1 uses ``decode``.
 """
 from __future__ import annotations
 
@@ -76,6 +84,24 @@ class HeadShardedDecode:
         local = self.pool.decode(layer, q_local, **kw)
         return gather_heads(local, self.world, self.group, out)
 
+    def decode_step(self, q_layers: torch.Tensor, out: torch.Tensor | None = None, **kw) -> torch.Tensor:
+        """Layers 0 .. L-1 of one step: q [L, B, Hq, D] -> [L, B, Hq, D], one all-gather."""
+        n_l, b, n_q, d = q_layers.shape
+        hl = n_q // self.world
+        local = torch.empty((n_l, b, hl, d), dtype=q_layers.dtype, device=q_layers.device)
+        for layer in range(n_l):
+            q_local = shard_query(q_layers[layer], self.n_kv_total, self.world, self.rank)
+            self.pool.decode(layer, q_local, out=local[layer], **kw)
+        gathered = torch.empty((self.world, n_l, b, hl, d), dtype=local.dtype, device=local.device)
+        if dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(gathered, local, group=self.group)
+        else:
+            dist.all_gather(list(gathered.unbind(0)), local, group=self.group)
+        if out is None:
+            out = torch.empty((n_l, b, n_q, d), dtype=local.dtype, device=local.device)
+        out.view(n_l, b, self.world, hl, d).copy_(gathered.permute(1, 2, 0, 3, 4))
+        return out
+
 
 @dataclass
 class PeerTargets:
@@ -113,13 +139,14 @@ def _ipc_release(handle: bytes) -> None:
 class PeerHeadShardedDecode(HeadShardedDecode):
     """Head-sharded decode whose kernel writes the outputs of every rank directly.
 
-    Each rank owns one device buffer holding two ``[max_batch, Hq, D]`` receive
-    buffers and an int32 flag per rank; the ranks map each other's buffers with
-    CUDA IPC at construction (a collective: every rank constructs together).
-    Call ``k`` (epoch ``k``) writes the receive buffer of parity ``k & 1`` on
-    every rank, so ``decode`` returns a view that keeps its values until the
-    call after next: consume it on the same stream before then (the next layer
-    of a decode step does) or copy it.  Every rank must make the same sequence
+    Each rank owns one device buffer holding two receive regions of
+    ``n_layers`` ``[max_batch, Hq, D]`` slices and an int32 flag per rank; the
+    ranks map each other's buffers with CUDA IPC at construction (a collective:
+    every rank constructs together).  Call ``k`` (epoch ``k``, one ``decode`` or
+    one ``decode_step``) writes the region of parity ``k & 1`` on every rank, so
+    the returned view keeps its values until the call after next: consume it on
+    the same stream before then (the next layer of a decode step does) or copy
+    it.  Every rank must make the same sequence
     of calls with the same batch.  Eager only: the epoch is a launch argument,
     so a captured graph would replay a stale one.
 
@@ -129,16 +156,20 @@ class PeerHeadShardedDecode(HeadShardedDecode):
 
     MAX_RANKS = 64
 
-    def __init__(self, pool, n_q_heads: int, world: int, rank: int, group=None, max_batch: int | None = None):
+    def __init__(self, pool, n_q_heads: int, world: int, rank: int, group=None, max_batch: int | None = None,
+                 n_layers: int = 1):
         super().__init__(pool, n_q_heads, world, rank, group)
         if world > self.MAX_RANKS:
             raise ValueError(f"at most {self.MAX_RANKS} ranks")
         dev = pool.device
         self.max_batch = int(max_batch or pool.max_seqs)
+        self.n_layers = int(n_layers)
         self.head_dim, self.dtype = pool.head_dim, pool.dtype
         elem = torch.empty((), dtype=pool.dtype).element_size()
-        self._out_bytes = (self.max_batch * n_q_heads * self.head_dim * elem + 255) // 256 * 256
-        flags_off = 2 * self._out_bytes
+        self._elem = elem
+        self._out_bytes = (self.max_batch * n_q_heads * self.head_dim * elem + 255) // 256 * 256  # one slice
+        self._region_bytes = self.n_layers * self._out_bytes  # one parity
+        flags_off = 2 * self._region_bytes
         self._buf = torch.zeros(flags_off + 4 * self.MAX_RANKS, dtype=torch.uint8, device=dev)
         self._flags = self._buf[flags_off: flags_off + 4 * world].view(torch.int32)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -157,10 +188,11 @@ class PeerHeadShardedDecode(HeadShardedDecode):
             else:
                 bases.append(_ipc_open(h, o))
                 self._handles.append(h)
-        self._out_ptrs = [
-            torch.tensor([b + par * self._out_bytes for b in bases], dtype=torch.int64, device=dev)
-            for par in (0, 1)
-        ]
+        # [parity][layer][rank]: the destination of each (parity, layer slice) on every rank
+        self._slice_ptrs = torch.tensor(
+            [[[b + par * self._region_bytes + layer * self._out_bytes for b in bases]
+              for layer in range(self.n_layers)] for par in (0, 1)],
+            dtype=torch.int64, device=dev)
         self._flag_ptrs = torch.tensor([b + flags_off for b in bases], dtype=torch.int64, device=dev)
         lo, _ = head_range(self.n_kv_total, world, rank)
         self.head_offset = lo * (n_q_heads // self.n_kv_total)
@@ -177,22 +209,54 @@ class PeerHeadShardedDecode(HeadShardedDecode):
             return torch.empty((0, self.n_q_heads, self.head_dim), dtype=self.dtype, device=q.device)
         self.epoch += 1
         par = self.epoch & 1
+        self._decode_into(layer, q, par, 0, **kw)
+        self._sync()
+        view = self._region(par, 1, b)[0]
+        if out is None:
+            return view
+        out.copy_(view)
+        return out
+
+    def decode_step(self, q_layers: torch.Tensor, out: torch.Tensor | None = None, **kw) -> torch.Tensor:
+        """Layers 0 .. L-1 of one step (q [L, B, Hq, D]) with a single epoch signal and
+        wait after the last layer; returns a view [L, B, Hq, D] of the receive region
+        unless ``out`` is given (then copied there)."""
+        n_l, b = q_layers.shape[:2]
+        if n_l > self.n_layers:
+            raise ValueError(f"{n_l} layers > the {self.n_layers} receive slices (n_layers)")
+        if b > self.max_batch:
+            raise ValueError(f"batch {b} > max_batch {self.max_batch}")
+        self.epoch += 1
+        par = self.epoch & 1
+        for layer in range(n_l):
+            self._decode_into(layer, q_layers[layer], par, layer, **kw)
+        self._sync()
+        view = self._region(par, n_l, b)
+        if out is None:
+            return view
+        out.copy_(view)
+        return out
+
+    def _decode_into(self, layer: int, q: torch.Tensor, par: int, slot: int, **kw) -> None:
         q_local = shard_query(q, self.n_kv_total, self.world, self.rank)
-        targets = PeerTargets(self._out_ptrs[par], self.world, self.head_offset, self.n_q_heads * self.head_dim,
-                              self.head_dim)
+        targets = PeerTargets(self._slice_ptrs[par, slot], self.world, self.head_offset,
+                              self.n_q_heads * self.head_dim, self.head_dim)
         self.pool.decode(layer, q_local, peers=targets, **kw)
+
+    def _sync(self) -> None:
         _lib.check(
             _lib.load().snapmind_peer_sync(self._flag_ptrs.data_ptr(), self._flags.data_ptr(), self.world, self.rank,
                                            self.epoch, _lib.PEER_SIGNAL | _lib.PEER_WAIT, self.err.data_ptr(),
                                            self.pool._stream()),
             "snapmind_peer_sync",
         )
-        n = b * self.n_q_heads * self.head_dim
-        view = self._buf[par * self._out_bytes:].view(self.dtype)[:n].view(b, self.n_q_heads, self.head_dim)
-        if out is None:
-            return view
-        out.copy_(view)
-        return out
+
+    def _region(self, par: int, n_l: int, b: int) -> torch.Tensor:
+        """[n_l, b, Hq, D] view of the first slices of the parity-``par`` region."""
+        flat = self._buf[par * self._region_bytes:].view(self.dtype)
+        row = self.n_q_heads * self.head_dim
+        return flat.as_strided((n_l, b, self.n_q_heads, self.head_dim),
+                               (self._out_bytes // self._elem, row, self.head_dim, 1))
 
     def check(self) -> None:
         """Synchronise and raise if a decode or wait of this instance reported a device error."""

@@ -128,14 +128,19 @@ class PagedKVPool(BlockPool):
 
     def decode(self, layer: int, q: torch.Tensor, out: torch.Tensor | None = None, scale: float | None = None,
                batch: int | None = None, split_tokens: int = 0, force_generic: bool = False,
-               max_seq_len: int | None = None, peers=None) -> torch.Tensor | None:
+               max_seq_len: int | None = None, peers=None, append=None) -> torch.Tensor | None:
         """Paged GQA decode attention of ``q`` ``[B, Hq, D]`` against layer ``layer``.
 
         ``peers`` (a ``head_shard.PeerTargets``) sends the output rows to the
         output buffers of every rank of a head-sharded decode instead of ``out``
-        and returns None."""
+        and returns None.  ``append=(k_new, v_new)`` (``[B, H, D]``, the pool's
+        dtype) stores this step's token of every sequence (the last slot the
+        latest ``reserve(1)`` gave it) in the same launch, in place of an
+        ``append`` call before the decode."""
         batch = q.shape[0] if batch is None else batch
         n_q = q.shape[1]
+        if peers is not None and append is not None:
+            raise ValueError("decode with peers does not store the step's token: append it first")
         if q.dtype != self.dtype:
             raise TypeError(f"q dtype {q.dtype} != pool dtype {self.dtype}")
         if q.stride(-1) != 1:
@@ -164,6 +169,25 @@ class PagedKVPool(BlockPool):
             )  # fmt: skip
             _lib.check(status, "PagedKVPool.decode (peers)")
             return None
+        if append is not None:
+            k_new, v_new = append
+            if k_new.dtype != self.dtype or v_new.dtype != self.dtype or k_new.stride() != v_new.stride():
+                raise TypeError("append rows must have the pool's dtype and matching strides")
+            if k_new.shape != (batch, self.n_kv_heads, self.head_dim) or k_new.stride(-1) != 1:
+                raise ValueError(f"append rows must be [{batch}, {self.n_kv_heads}, {self.head_dim}], "
+                                 f"head dim contiguous, got {tuple(k_new.shape)}")
+            status = lib.snapmind_paged_gqa_decode_append(
+                q.data_ptr(), q.stride(0), q.stride(1),
+                self.k[layer].data_ptr(), self.v[layer].data_ptr(), self._dcode,
+                self.block_tables.data_ptr(), self.max_blocks_per_seq, self.max_blocks_per_seq,
+                self.seq_lens.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), k_new.stride(1),
+                out.data_ptr(), out.stride(0), out.stride(1),
+                float(scale), batch, n_q, self.n_kv_heads, self.head_dim, self.block_size, self.num_blocks,
+                max_len, split, _lib.DECODE_FORCE_GENERIC if force_generic else 0,
+                ws.data_ptr(), ws.numel(), self.err.data_ptr(), self._stream(),
+            )  # fmt: skip
+            _lib.check(status, "PagedKVPool.decode (append)")
+            return out
         status = lib.snapmind_paged_gqa_decode(
             q.data_ptr(), q.stride(0), q.stride(1),
             self.k[layer].data_ptr(), self.v[layer].data_ptr(), self._dcode,

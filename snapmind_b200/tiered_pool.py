@@ -16,7 +16,13 @@ by ``snapmind_tiered_move``; chunk data crosses the host link only as
 
 Device layout: ``k``/``v`` are ``[layer][slot][head][chunk][dim]`` — a slot is
 one block of the paged layout, so attention runs the paged GQA decode kernel
-over ``tables`` (resident slots in chunk order) and ``table_lens``.
+over ``tables`` (resident slots in chunk order) and ``table_lens``.  Because
+the layers are contiguous, block ``slot`` of layer ``l`` is block
+``l * total_slots + slot`` of one pool spanning every layer, so one decode
+launch serves all layers of a step: row ``l * B + b`` of that launch is
+sequence ``b`` of layer ``l`` (its table row shifted by ``l * total_slots``,
+its query and output rows at the same index of the contiguous
+``[L, B, Hq, D]`` tensors).
 """
 from __future__ import annotations
 
@@ -82,6 +88,11 @@ class TieredKVPool:
         self.host_lens = np.zeros(batch, np.int64)
         self.step_idx = 0
         self._workspace: torch.Tensor | None = None
+        # one decode launch for all layers: per-layer block offsets of the shared tables
+        self._layer_offsets = (torch.arange(n_layers, dtype=torch.int32, device=self.device)
+                               * self.total_slots).view(n_layers, 1, 1)
+        self._tables_all = torch.zeros((n_layers, batch, self.max_chunks), **i32)
+        self._lens_all = torch.zeros((n_layers, batch), **i32)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
 
@@ -233,13 +244,29 @@ class TieredKVPool:
         )  # fmt: skip
         _lib.check(status, "TieredKVPool.append")
         max_len = self._resident_bound() * self.chunk
-        # split plan sized for the average resident length (the pool shared by the batch)
+        one_launch = q.is_contiguous() and out.is_contiguous()
+        rows = self.B * self.L if one_launch else self.B
+        # split plan sized for the launch's rows and the average resident length (the pool
+        # shared by the batch)
         split = split_tokens or self.lib.snapmind_paged_gqa_decode_split_tokens(
-            self.B, self.H, max(self.chunk, 2 * self.n_slots * self.chunk // self.B), self.chunk)
-        need = self.lib.snapmind_paged_gqa_decode_workspace_bytes(self.B, q.shape[2], self.H, self.D, max_len, split)
+            rows, self.H, max(self.chunk, 2 * self.n_slots * self.chunk // self.B), self.chunk)
+        need = self.lib.snapmind_paged_gqa_decode_workspace_bytes(rows, q.shape[2], self.H, self.D, max_len, split)
         if self._workspace is None or self._workspace.numel() < need:
             self._workspace = torch.zeros(need, dtype=torch.uint8, device=self.device)
         ws = self._workspace
+        if one_launch:
+            # every layer in one launch: row l * B + b = sequence b of layer l
+            torch.add(self.tables.unsqueeze(0), self._layer_offsets, out=self._tables_all)
+            self._lens_all.copy_(self.table_lens.unsqueeze(0).expand(self.L, self.B))
+            status = self.lib.snapmind_paged_gqa_decode(
+                q.data_ptr(), q.stride(1), q.stride(2), self.k.data_ptr(), self.v.data_ptr(), self._dcode,
+                self._tables_all.data_ptr(), self.max_chunks, self.max_chunks, self._lens_all.data_ptr(),
+                out.data_ptr(), out.stride(1), out.stride(2), float(self.D ** -0.5), rows, q.shape[2], self.H,
+                self.D, self.chunk, self.L * self.total_slots, max_len, split, 0, ws.data_ptr(), ws.numel(),
+                self.err.data_ptr(), self._stream(),
+            )  # fmt: skip
+            _lib.check(status, "TieredKVPool.decode")
+            return
         for layer in range(self.L):
             qs, os_ = q[layer], out[layer]
             status = self.lib.snapmind_paged_gqa_decode(

@@ -1,6 +1,7 @@
 """KV-head-sharded paged decode on 2 GPUs (skipped with fewer GPUs): the NCCL
 all-gather version, and the version whose decode kernel stores the rows into
-every rank's buffer over NVLink (plain stores through CUDA IPC peer mappings)."""
+every rank's buffer over NVLink (plain stores through CUDA IPC peer mappings),
+each per layer and with one exchange per multi-layer step."""
 import os
 import socket
 
@@ -43,7 +44,7 @@ def _worker(rank, world, port, results):
         nb = int(nbs.sum())
         W = int(nbs.max())
         tables = np.zeros((B, W), np.int32)
-        pool = PagedKVPool(1, hi - lo, D, nb, B, W, block_size=bs, dtype=torch.bfloat16)
+        pool = PagedKVPool(2, hi - lo, D, nb, B, W, block_size=bs, dtype=torch.bfloat16)
         kp = np.zeros((nb, hi - lo, bs, D), np.float32)
         vp = np.zeros_like(kp)
         off = 0
@@ -54,8 +55,9 @@ def _worker(rank, world, port, results):
                 kp[off, :, : t1 - t0] = k[b, lo:hi, t0:t1]
                 vp[off, :, : t1 - t0] = v[b, lo:hi, t0:t1]
                 off += 1
-        pool.k[0].copy_(torch.from_numpy(kp).to(torch.bfloat16))
-        pool.v[0].copy_(torch.from_numpy(vp).to(torch.bfloat16))
+        for layer in range(2):  # layer 1 holds the same rows, swapped K/V
+            pool.k[layer].copy_(torch.from_numpy(kp if layer == 0 else vp).to(torch.bfloat16))
+            pool.v[layer].copy_(torch.from_numpy(vp if layer == 0 else kp).to(torch.bfloat16))
         pool.set_state(tables, lens, np.zeros(0, np.int32))
         dec = HeadShardedDecode(pool, Hq, world, rank)
         out = dec.decode(0, torch.from_numpy(q).cuda().to(torch.bfloat16))
@@ -76,6 +78,19 @@ def _worker(rank, world, port, results):
             pdec.check()
             same = same and bool(torch.equal(got, ref))
         pdec.close()
+        # one exchange per step for both layers: the fused form equals the NCCL form and
+        # the per-layer decode, over four steps (both receive regions twice)
+        sdec = PeerHeadShardedDecode(pool, Hq, world, rank, n_layers=2)
+        for _ in range(4):
+            qs = torch.from_numpy(bf16.round_to_bf16(rng.standard_normal((2, B, Hq, D)).astype(np.float32)))
+            qs = qs.cuda().to(torch.bfloat16)
+            ref = dec.decode_step(qs)
+            per = torch.stack([dec.decode(layer, qs[layer]) for layer in range(2)])
+            got = sdec.decode_step(qs).clone()
+            torch.cuda.synchronize()
+            sdec.check()
+            same = same and bool(torch.equal(got, ref)) and bool(torch.equal(ref, per))
+        sdec.close()
         results[rank] = (err, same)
     finally:
         dist.destroy_process_group()

@@ -154,3 +154,59 @@ def test_device_error_word_flags_bad_block_ids(cuda_device):
     pool.gather(batch=1)
     with pytest.raises(RuntimeError, match="block id outside the pool"):
         pool.check()
+
+
+@pytest.mark.parametrize("dtype,bs,split,force_generic", [
+    (torch.bfloat16, 16, 0, False), (torch.bfloat16, 16, 64, False), (torch.bfloat16, 64, 128, False),
+    (torch.float16, 32, 0, False), (torch.bfloat16, 16, 0, True), (torch.float32, 16, 0, False)])
+def test_decode_with_append_equals_append_then_decode(cuda_device, dtype, bs, split, force_generic):
+    """The fused store of this step's token (snapmind_paged_gqa_decode_append) leaves
+    the pool with exactly the bytes the append kernel writes and gives exactly the
+    output of append-then-decode, over steps that cross block and split boundaries;
+    the reference store these replace is snapmind/kv_cache/paged.py:34-54."""
+    from snapmind_b200 import PagedKVPool
+
+    rng = np.random.RandomState(11)
+    B, H, Hq, D = 7, 8, 32, 128
+    lens = rng.randint(1, 300, size=B)
+    lens[0] = 1  # a sequence whose first token arrives through the fused store
+    lens[1] = bs * 4 - 1  # its next token starts a new block
+    steps = 5
+    nbs = (lens + steps + bs - 1) // bs
+    nb = int(nbs.sum()) + 4
+    perm = rng.permutation(nb).astype(np.int32)
+    W = int(nbs.max())
+    tables = np.zeros((B, W), np.int32)
+    off = 0
+    need = (lens + bs - 1) // bs
+    for b in range(B):
+        tables[b, : need[b]] = perm[off: off + need[b]]
+        off += need[b]
+    pools = []
+    for _ in range(2):
+        pool = PagedKVPool(1, H, D, nb, max_seqs=B, max_blocks_per_seq=W, block_size=bs, dtype=dtype)
+        g = torch.Generator(device="cuda").manual_seed(5)
+        pool.k.normal_(generator=g)
+        pool.v.normal_(generator=g)
+        pool.set_state(tables, lens, perm[off:])
+        pools.append(pool)
+    fused, ref = pools
+    for step in range(steps):
+        gen = torch.Generator(device="cuda").manual_seed(100 + step)
+        q = torch.randn(B, Hq, D, device="cuda", generator=gen).to(dtype)
+        kn = torch.randn(B, H, D, device="cuda", generator=gen).to(dtype)
+        vn = torch.randn(B, H, D, device="cuda", generator=gen).to(dtype)
+        max_len = int(lens.max()) + steps
+        for pool in pools:
+            pool.reserve(1, batch=B)
+        want_out = None
+        ref.append(0, kn, vn)
+        want_out = ref.decode(0, q, split_tokens=split, force_generic=force_generic, max_seq_len=max_len)
+        got_out = fused.decode(0, q, split_tokens=split, force_generic=force_generic, max_seq_len=max_len,
+                               out=torch.empty_like(want_out), append=(kn, vn))
+        torch.cuda.synchronize()
+        fused.check()
+        ref.check()
+        assert torch.equal(fused.k, ref.k) and torch.equal(fused.v, ref.v), f"step {step}: pool bytes differ"
+        assert torch.equal(got_out, want_out), f"step {step}: outputs differ"
+    assert torch.equal(fused.block_tables, ref.block_tables)
