@@ -71,67 +71,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   return true;
 }
 
-// ---- thread-block clusters (distributed shared memory of one GPU) ------------
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// The shared::cluster address of the same offset in the shared memory of CTA `rank` of this cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
-__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-// Asynchronous 16-byte store into another CTA's shared memory that counts its
-// bytes on that CTA's mbarrier (complete_tx): the receiver arms the barrier
-// with the expected byte count, the sender neither arrives nor waits.
-__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float a, float b, float c, float d,
-                                            uint32_t cluster_bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
-                   cluster_addr),
-               "f"(a), "f"(b), "f"(c), "f"(d), "r"(cluster_bar)
-               : "memory");
-}
-// Arrive on an mbarrier of another CTA of the cluster, releasing this thread's
-// earlier writes (to that CTA's shared memory included) at cluster scope.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-// Phase check of a local mbarrier whose arrivals come from other CTAs of the
-// cluster: acquire at cluster scope, so their writes are visible afterwards.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Non-blocking form of the same check (a try_wait that suspends the thread is
-// not woken promptly by arrivals from another CTA: spin on this instead).
-__device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Every thread of every CTA of the cluster (all paths must reach it).
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-
 // ---- TMA --------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
                                             uint32_t bar) {
@@ -294,21 +233,6 @@ inline bool tensor_map_2d(CUtensorMap* map, bool bf16, const void* base, uint64_
   const cuuint32_t estr[2] = {1, 1};
   return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// Rows of `inner` 16-bit elements, boxes of 32 x box_rows with the 64-byte
-// swizzle (32 elements x 2 bytes = the 64-byte span).
-inline bool tensor_map_2d_sw64(CUtensorMap* map, bool bf16, const void* base, uint64_t inner, uint64_t rows,
-                               uint64_t pitch_bytes, uint32_t box_rows) {
-  EncodeTiledFn fn = encode_tiled();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {inner, rows};
-  const cuuint64_t strides[1] = {pitch_bytes};
-  const cuuint32_t box[2] = {32, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
-            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
