@@ -225,3 +225,33 @@ def raise_device_error(word: int, what: str) -> None:
     if word & DEVERR_POSITION:
         parts.append("rotary position outside the cos/sin tables")
     raise RuntimeError(f"{what}: device error 0x{word:x} ({', '.join(parts)})")
+
+
+class DecodeWorkspace:
+    """A reusable workspace for the paged GQA decode entry points.
+
+    Its layout (set by the library) is the split tickets first -- one int32 per
+    (row, kv head), which every call needs at zero and leaves at zero -- padded
+    to 256 bytes, then the partial softmax states.  A call over fewer rows puts
+    its partials where a later call over more rows keeps tickets, so the buffer
+    tracks how long a prefix is known to be zero, and before a call whose
+    tickets reach past it, clears that stretch on the current stream.
+    """
+
+    def __init__(self, device):
+        self.device = device
+        self.buf: torch.Tensor | None = None
+        self.clean = 0  # leading bytes known to be zero
+
+    def get(self, rows: int, n_kv_heads: int, need: int) -> torch.Tensor:
+        import torch
+
+        tickets = rows * n_kv_heads * 4
+        if self.buf is None or self.buf.numel() < need:
+            self.buf = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+            self.clean = self.buf.numel()
+        if tickets > self.clean:
+            self.buf[self.clean:tickets].zero_()
+        # after this call: its tickets are zero again, its partials start past the padding
+        self.clean = min(max(self.clean, tickets), (tickets + 255) // 256 * 256)
+        return self.buf

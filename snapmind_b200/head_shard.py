@@ -20,10 +20,11 @@ waits (bounded) for all ranks' epochs.  No collective launch, no gathered
 copy, no reorder.
 
 Both offer ``decode_step``: every layer of one decode step (``q [L, B, Hq, D]``)
-with one exchange for the whole step instead of one per layer -- one
-all-gather of ``[L, B, Hq/N, D]`` for the NCCL form, and for the peer-store
-form every layer's rows stored into that layer's slice of an
-``[L, B, Hq, D]`` receive region, followed by a single epoch signal and wait.
+in one decode launch (``PagedKVPool.decode_layers``) with one exchange for the
+whole step instead of one per layer -- one all-gather of ``[L, B, Hq/N, D]``
+for the NCCL form, and for the peer-store form every layer's rows stored into
+that layer's slice of an ``[L, B, Hq, D]`` receive region, followed by a
+single epoch signal and wait.
 It suits callers whose consumer of the outputs runs after the whole step; a
 model layer that needs layer l's heads before layer l + 1 uses ``decode``.
 """
@@ -89,9 +90,14 @@ class HeadShardedDecode:
         n_l, b, n_q, d = q_layers.shape
         hl = n_q // self.world
         local = torch.empty((n_l, b, hl, d), dtype=q_layers.dtype, device=q_layers.device)
-        for layer in range(n_l):
-            q_local = shard_query(q_layers[layer], self.n_kv_total, self.world, self.rank)
-            self.pool.decode(layer, q_local, out=local[layer], **kw)
+        group = n_q // self.n_kv_total
+        lo, hi = head_range(self.n_kv_total, self.world, self.rank)
+        q_local = q_layers[:, :, lo * group: hi * group]
+        if hasattr(self.pool, "decode_layers") and q_local.stride(0) == b * q_local.stride(1):
+            self.pool.decode_layers(q_local, out=local, **kw)  # every layer in one launch
+        else:
+            for layer in range(n_l):
+                self.pool.decode(layer, q_local[layer], out=local[layer], **kw)
         gathered = torch.empty((self.world, n_l, b, hl, d), dtype=local.dtype, device=local.device)
         if dist.get_backend(self.group) == "nccl":
             dist.all_gather_into_tensor(gathered, local, group=self.group)
@@ -228,8 +234,18 @@ class PeerHeadShardedDecode(HeadShardedDecode):
             raise ValueError(f"batch {b} > max_batch {self.max_batch}")
         self.epoch += 1
         par = self.epoch & 1
-        for layer in range(n_l):
-            self._decode_into(layer, q_layers[layer], par, layer, **kw)
+        group = self.n_q_heads // self.n_kv_total
+        lo, hi = head_range(self.n_kv_total, self.world, self.rank)
+        q_local = q_layers[:, :, lo * group: hi * group]
+        if b == self.max_batch and self._out_bytes == b * self.n_q_heads * self.head_dim * self._elem and \
+                q_local.stride(0) == b * q_local.stride(1):
+            # every layer in one launch: row l * B + b lands in layer l's slice of each rank's region
+            targets = PeerTargets(self._slice_ptrs[par, 0], self.world, self.head_offset,
+                                  self.n_q_heads * self.head_dim, self.head_dim)
+            self.pool.decode_layers(q_local, peers=targets, **kw)
+        else:
+            for layer in range(n_l):
+                self._decode_into(layer, q_layers[layer], par, layer, **kw)
         self._sync()
         view = self._region(par, n_l, b)
         if out is None:

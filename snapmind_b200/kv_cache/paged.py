@@ -79,7 +79,7 @@ class PagedKVCache(KVCacheABC):
         self._err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._version = 0  # bumped by every change of the cached contents
         self._ladder: torch.Tensor | None = None  # int32 [1, 2, ..., max_blocks * block_size]
-        self._workspace: torch.Tensor | None = None
+        self._workspace = _lib.DecodeWorkspace(self.device)
         # device-counter steps (begin_device_steps): slot of the next token, and length after it
         self._dev_len: torch.Tensor | None = None
         self._dev_len_p1: torch.Tensor | None = None
@@ -338,16 +338,14 @@ class PagedKVCache(KVCacheABC):
         lib = _lib.load()
         split = lib.snapmind_paged_gqa_decode_split_tokens(n_t, self.n_heads, n, self.block_size)
         need = lib.snapmind_paged_gqa_decode_workspace_bytes(n_t, n_q, self.n_heads, self.head_dim, n, split)
-        if self._workspace is None or self._workspace.numel() < need:
-            # zero-filled once; the kernel leaves its tickets at zero
-            self._workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+        ws = self._workspace.get(n_t, self.n_heads, need)
         status = lib.snapmind_paged_gqa_decode(
             q.data_ptr(), q.stride(2), q.stride(1),
             self._k_buffer.data_ptr(), self._v_buffer.data_ptr(), _lib.dtype_code(self.dtype),
             self._tables_dev[layer_idx].data_ptr(), 0, self.max_blocks, lens_ptr,
             out.data_ptr(), out.stride(2), out.stride(1),
             float(scale), n_t, n_q, self.n_heads, self.head_dim, self.block_size, self.max_blocks,
-            n, split, 0, self._workspace.data_ptr(), self._workspace.numel(), self._err.data_ptr(),
+            n, split, 0, ws.data_ptr(), ws.numel(), self._err.data_ptr(),
             self._stream(),
         )  # fmt: skip
         _lib.check(status, "PagedKVCache.attend")
@@ -428,15 +426,14 @@ class PagedKVCache(KVCacheABC):
         cap = self._dev_capacity
         split = lib.snapmind_paged_gqa_decode_split_tokens(1, self.n_heads, cap, self.block_size)
         need = lib.snapmind_paged_gqa_decode_workspace_bytes(1, n_q, self.n_heads, self.head_dim, cap, split)
-        if self._workspace is None or self._workspace.numel() < need:
-            self._workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+        ws = self._workspace.get(1, self.n_heads, need)
         status = lib.snapmind_paged_gqa_decode(
             q.data_ptr(), q.stride(2), q.stride(1),
             self._k_buffer.data_ptr(), self._v_buffer.data_ptr(), _lib.dtype_code(self.dtype),
             self._tables_dev[layer_idx].data_ptr(), 0, self.max_blocks, self._dev_len_p1.data_ptr(),
             out.data_ptr(), out.stride(2), out.stride(1),
             float(scale), 1, n_q, self.n_heads, self.head_dim, self.block_size, self.max_blocks,
-            cap, split, 0, self._workspace.data_ptr(), self._workspace.numel(), self._err.data_ptr(),
+            cap, split, 0, ws.data_ptr(), ws.numel(), self._err.data_ptr(),
             self._stream(),
         )  # fmt: skip
         _lib.check(status, "PagedKVCache.attend_device")

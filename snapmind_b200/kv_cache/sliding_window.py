@@ -70,7 +70,7 @@ class SlidingWindowKVCache(KVCacheABC):
         self._lens_dev = torch.zeros(n_layers, dtype=torch.int32, device=self.device)   # skip + n
         self._starts_dev = torch.zeros(n_layers, dtype=torch.int32, device=self.device)  # skip
         self._err = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self._workspace: torch.Tensor | None = None
+        self._workspace = _lib.DecodeWorkspace(self.device)
         self._version = 0
         self._reset_host()
 
@@ -248,15 +248,14 @@ class SlidingWindowKVCache(KVCacheABC):
         lib = _lib.load()
         split = lib.snapmind_paged_gqa_decode_split_tokens(n_t, self.n_heads, total, self.block_size)
         need = lib.snapmind_paged_gqa_decode_workspace_bytes(n_t, n_q, self.n_heads, self.head_dim, total, split)
-        if self._workspace is None or self._workspace.numel() < need:
-            self._workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+        ws = self._workspace.get(n_t, self.n_heads, need)
         status = lib.snapmind_paged_gqa_decode_window(
             q.data_ptr(), q.stride(2), q.stride(1),
             self._k.data_ptr(), self._v.data_ptr(), _lib.dtype_code(self.dtype),
             self._tables_dev[layer_idx].data_ptr(), 0, self.row_blocks, lens.data_ptr(), starts.data_ptr(),
             out.data_ptr(), out.stride(2), out.stride(1),
             float(scale), n_t, n_q, self.n_heads, self.head_dim, self.block_size, self.max_blocks,
-            total, split, 0, self._workspace.data_ptr(), self._workspace.numel(), self._err.data_ptr(),
+            total, split, 0, ws.data_ptr(), ws.numel(), self._err.data_ptr(),
             _lib.stream_handle(self.device),
         )  # fmt: skip
         _lib.check(status, "SlidingWindowKVCache.attend")

@@ -45,7 +45,7 @@ class PagedKVPool(BlockPool):
         self.k = torch.empty(shape, dtype=dtype, device=self.device)
         self.v = torch.empty(shape, dtype=dtype, device=self.device)
         self.layer_stride = num_blocks * n_kv_heads * block_size * head_dim
-        self._workspace: torch.Tensor | None = None
+        self._workspace = _lib.DecodeWorkspace(self.device)
 
     def append(self, layer: int | None, k_new: torch.Tensor, v_new: torch.Tensor, slot_starts=None,
                slot_start0: int | None = None) -> None:
@@ -121,10 +121,62 @@ class PagedKVPool(BlockPool):
         need = lib.snapmind_paged_gqa_decode_workspace_bytes(
             batch, n_q_heads, self.n_kv_heads, self.head_dim, max_len, split
         )
-        if self._workspace is None or self._workspace.numel() < need:
-            # zero-filled once; the kernel leaves its tickets at zero
-            self._workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
-        return self._workspace
+        return self._workspace.get(batch, self.n_kv_heads, need)
+
+    def decode_layers(self, q: torch.Tensor, out: torch.Tensor | None = None, scale: float | None = None,
+                      split_tokens: int = 0, max_seq_len: int | None = None, peers=None) -> torch.Tensor | None:
+        """Paged GQA decode of layers 0 .. L-1 in one launch: ``q`` ``[L, B, Hq, D]`` ->
+        ``[L, B, Hq, D]``.
+
+        The pool is layer-contiguous, so block ``p`` of layer ``l`` is block
+        ``l * num_blocks + p`` of one pool spanning every layer; launch row
+        ``l * B + b`` is sequence ``b`` of layer ``l``, its table row shifted by
+        ``l * num_blocks`` (entries outside ``[0, num_blocks)`` stay invalid, so the
+        kernel still flags them).  ``q`` (and ``out``) must step uniformly over
+        (layer, sequence) rows: ``stride(0) == B * stride(1)``.  ``peers`` as in
+        ``decode``, with ``out_stride_seq`` the row stride of every rank's
+        ``[L, B, Hq, D]`` receive region."""
+        n_l, batch, n_q, d = q.shape
+        if n_l > self.k.shape[0]:
+            raise ValueError(f"{n_l} layers > the pool's {self.k.shape[0]}")
+        if q.dtype != self.dtype or q.stride(-1) != 1 or q.stride(0) != batch * q.stride(1):
+            raise ValueError("q must be [L, B, Hq, D] in the pool's dtype with uniformly strided rows")
+        if out is None and peers is None:
+            out = torch.empty((n_l, batch, n_q, d), dtype=self.dtype, device=self.device)
+        if out is not None and (out.stride(-1) != 1 or out.stride(0) != batch * out.stride(1)):
+            raise ValueError("out must be [L, B, Hq, D] with uniformly strided rows")
+        scale = self.head_dim ** -0.5 if scale is None else scale
+        if max_seq_len is None:
+            max_seq_len = max(1, int(self._host_lens[:batch].max())) if batch else 1
+        rows = n_l * batch
+        lib = _lib.load()
+        split = split_tokens or lib.snapmind_paged_gqa_decode_split_tokens(rows, self.n_kv_heads, max_seq_len,
+                                                                           self.block_size)
+        ws = self._decode_workspace(rows, n_q, max_seq_len, split)
+        t = self.block_tables[:batch]
+        offs = torch.arange(n_l, dtype=torch.int32, device=self.device).view(n_l, 1, 1) * self.num_blocks
+        tables = torch.where((t >= 0) & (t < self.num_blocks), t.unsqueeze(0) + offs, torch.full_like(t, -1))
+        lens = self.seq_lens[:batch].unsqueeze(0).expand(n_l, batch).contiguous()
+        span = n_l * self.num_blocks
+        if peers is not None:
+            status = lib.snapmind_paged_gqa_decode_peers(
+                q.data_ptr(), q.stride(1), q.stride(2), self.k.data_ptr(), self.v.data_ptr(), self._dcode,
+                tables.data_ptr(), self.max_blocks_per_seq, self.max_blocks_per_seq, lens.data_ptr(), None,
+                peers.out_ptrs.data_ptr(), peers.n, peers.head_offset, peers.out_stride_seq, peers.out_stride_head,
+                float(scale), rows, n_q, self.n_kv_heads, self.head_dim, self.block_size, span,
+                max_seq_len, split, 0, ws.data_ptr(), ws.numel(), self.err.data_ptr(), self._stream(),
+            )  # fmt: skip
+            _lib.check(status, "PagedKVPool.decode_layers (peers)")
+            return None
+        status = lib.snapmind_paged_gqa_decode(
+            q.data_ptr(), q.stride(1), q.stride(2), self.k.data_ptr(), self.v.data_ptr(), self._dcode,
+            tables.data_ptr(), self.max_blocks_per_seq, self.max_blocks_per_seq, lens.data_ptr(),
+            out.data_ptr(), out.stride(1), out.stride(2), float(scale), rows, n_q, self.n_kv_heads, self.head_dim,
+            self.block_size, span, max_seq_len, split, 0, ws.data_ptr(), ws.numel(), self.err.data_ptr(),
+            self._stream(),
+        )  # fmt: skip
+        _lib.check(status, "PagedKVPool.decode_layers")
+        return out
 
     def decode(self, layer: int, q: torch.Tensor, out: torch.Tensor | None = None, scale: float | None = None,
                batch: int | None = None, split_tokens: int = 0, force_generic: bool = False,

@@ -87,7 +87,7 @@ class TieredKVPool:
         self._snap_ev = [torch.cuda.Event() for _ in range(3)]
         self.host_lens = np.zeros(batch, np.int64)
         self.step_idx = 0
-        self._workspace: torch.Tensor | None = None
+        self._workspace = _lib.DecodeWorkspace(self.device)
         # one decode launch for all layers: per-layer block offsets of the shared tables
         self._layer_offsets = (torch.arange(n_layers, dtype=torch.int32, device=self.device)
                                * self.total_slots).view(n_layers, 1, 1)
@@ -251,9 +251,7 @@ class TieredKVPool:
         split = split_tokens or self.lib.snapmind_paged_gqa_decode_split_tokens(
             rows, self.H, max(self.chunk, 2 * self.n_slots * self.chunk // self.B), self.chunk)
         need = self.lib.snapmind_paged_gqa_decode_workspace_bytes(rows, q.shape[2], self.H, self.D, max_len, split)
-        if self._workspace is None or self._workspace.numel() < need:
-            self._workspace = torch.zeros(need, dtype=torch.uint8, device=self.device)
-        ws = self._workspace
+        ws = self._workspace.get(rows, self.H, need)
         if one_launch:
             # every layer in one launch: row l * B + b = sequence b of layer l
             torch.add(self.tables.unsqueeze(0), self._layer_offsets, out=self._tables_all)

@@ -84,9 +84,10 @@ def _worker(rank, world, port, results):
         for _ in range(4):
             qs = torch.from_numpy(bf16.round_to_bf16(rng.standard_normal((2, B, Hq, D)).astype(np.float32)))
             qs = qs.cuda().to(torch.bfloat16)
-            ref = dec.decode_step(qs)
-            per = torch.stack([dec.decode(layer, qs[layer]) for layer in range(2)])
-            got = sdec.decode_step(qs).clone()
+            # one split plan for every form, so each (layer, sequence) row is computed the same way
+            ref = dec.decode_step(qs, split_tokens=64)
+            per = torch.stack([dec.decode(layer, qs[layer], split_tokens=64) for layer in range(2)])
+            got = sdec.decode_step(qs, split_tokens=64).clone()
             torch.cuda.synchronize()
             sdec.check()
             same = same and bool(torch.equal(got, ref)) and bool(torch.equal(ref, per))

@@ -210,3 +210,79 @@ def test_decode_with_append_equals_append_then_decode(cuda_device, dtype, bs, sp
         assert torch.equal(fused.k, ref.k) and torch.equal(fused.v, ref.v), f"step {step}: pool bytes differ"
         assert torch.equal(got_out, want_out), f"step {step}: outputs differ"
     assert torch.equal(fused.block_tables, ref.block_tables)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_decode_layers_one_launch_equals_per_layer(cuda_device, dtype):
+    """decode_layers (every layer in one launch over the layer-contiguous pool, row
+    l * B + b = sequence b of layer l) equals the per-layer decode bit for bit under
+    the same split plan, for contiguous queries and for a head slice of them."""
+    from snapmind_b200 import PagedKVPool
+
+    rng = np.random.RandomState(21)
+    L, B, H, Hq, D, bs = 3, 5, 8, 32, 128, 16
+    lens = rng.randint(1, 500, size=B)
+    nbs = (lens + bs - 1) // bs
+    nb = int(nbs.sum()) + 2
+    perm = rng.permutation(nb).astype(np.int32)
+    W = int(nbs.max())
+    tables = np.zeros((B, W), np.int32)
+    off = 0
+    for b in range(B):
+        tables[b, : nbs[b]] = perm[off: off + nbs[b]]
+        off += nbs[b]
+    pool = PagedKVPool(L, H, D, nb, max_seqs=B, max_blocks_per_seq=W, block_size=bs, dtype=dtype)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    pool.k.normal_(generator=g)
+    pool.v.normal_(generator=g)
+    pool.set_state(tables, lens, perm[off:])
+    q = torch.randn(L, B, Hq, D, device="cuda", generator=g).to(dtype)
+    got = pool.decode_layers(q, split_tokens=64)
+    want = torch.stack([pool.decode(layer, q[layer], split_tokens=64) for layer in range(L)])
+    torch.cuda.synchronize()
+    pool.check()
+    assert torch.equal(got, want)
+    # a strided view (rows of a wider tensor, as a head-sharded rank's query slice is)
+    wide = torch.randn(L, B, 2 * Hq, D, device="cuda", generator=g).to(dtype)
+    qv = wide[:, :, :Hq]
+    got_v = pool.decode_layers(qv, split_tokens=64)
+    want_v = torch.stack([pool.decode(layer, qv[layer], split_tokens=64) for layer in range(L)])
+    torch.cuda.synchronize()
+    assert torch.equal(got_v, want_v)
+
+
+def test_decode_after_a_smaller_batch_keeps_tickets_zero(cuda_device):
+    """The decode workspace holds split tickets for every (row, kv head) first and
+    partials after them: a multi-split call over few rows writes partials where a
+    later call over more rows keeps tickets.  The pool clears that stretch before
+    the larger call, which must equal the same call on a fresh pool."""
+    from snapmind_b200 import PagedKVPool
+
+    rng = np.random.RandomState(31)
+    B, H, Hq, D, bs = 15, 8, 32, 128, 16
+    lens = rng.randint(200, 900, size=B)
+    nbs = (lens + bs - 1) // bs
+    nb = int(nbs.sum())
+    perm = rng.permutation(nb).astype(np.int32)
+    W = int(nbs.max())
+    tables = np.zeros((B, W), np.int32)
+    off = 0
+    for b in range(B):
+        tables[b, : nbs[b]] = perm[off: off + nbs[b]]
+        off += nbs[b]
+    pools = []
+    for _ in range(2):
+        pool = PagedKVPool(1, H, D, nb, max_seqs=B, max_blocks_per_seq=W, block_size=bs, dtype=torch.bfloat16)
+        g = torch.Generator(device="cuda").manual_seed(3)
+        pool.k.normal_(generator=g)
+        pool.v.normal_(generator=g)
+        pool.set_state(tables, lens, np.zeros(0, np.int32))
+        pools.append(pool)
+    used, fresh = pools
+    q = torch.randn(B, Hq, D, device="cuda", generator=torch.Generator(device="cuda").manual_seed(4)).to(torch.bfloat16)
+    used.decode(0, q[:2], split_tokens=64)  # 2 rows, many splits: partials right after 16 ticket slots
+    got = used.decode(0, q, split_tokens=64)
+    want = fresh.decode(0, q, split_tokens=64)
+    torch.cuda.synchronize()
+    used.check()
+    assert torch.equal(got, want)
