@@ -143,10 +143,10 @@ class MLALatentPool(BlockPool):
             n_splits = lib.snapmind_sparse_mla_default_splits(batch, H, self.kv_lora_rank, self.rope_dim,
                                                               self.block_size, self._dcode)
         need = lib.snapmind_sparse_mla_workspace_bytes(batch, H, self.kv_lora_rank, n_splits)
-        ws = getattr(self, "_sparse_ws", None)
-        if ws is None or ws.numel() < need:
-            ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
-            self._sparse_ws = ws
+        if getattr(self, "_sparse_ws", None) is None:
+            self._sparse_ws = _lib.DecodeWorkspace(self.device)
+        # tickets: one per (sequence, group of 16 heads) of the split-combining kernel
+        ws = self._sparse_ws.get(batch, (H + 15) // 16, need)
         status = lib.snapmind_sparse_mla_decode(
             q_lat.data_ptr(), q_pe.data_ptr(), self._dcode, self.latent[layer].data_ptr(),
             self.rope[layer].data_ptr(), self.block_tables.data_ptr(), self.max_blocks_per_seq,
