@@ -349,9 +349,14 @@ SNAPMIND_API int snapmind_sparse_mla_decode(const void *q_lat, const void *q_pe,
  * Long sequences are split into chunks of split_tokens tokens (a multiple of
  * block_size; <= 0 picks snapmind_paged_gqa_decode_split_tokens) processed by
  * separate CTAs; the last CTA of a sequence merges the partial softmax states.
- * `workspace` must hold snapmind_paged_gqa_decode_workspace_bytes(...) bytes
- * and be zero-filled once before its first use; each call leaves it reusable.
- * Calls sharing one workspace must not overlap on the GPU.
+ * `workspace` must hold snapmind_paged_gqa_decode_workspace_bytes(...) bytes.
+ * It starts with the split tickets, one int32 per (sequence, kv head), which
+ * must be zero when a call starts and are zero again when it ends; the
+ * partial states follow at the next 256-byte boundary.  A zero-filled
+ * workspace is reusable by calls over the same or fewer sequences; a call over
+ * more sequences than an earlier one needs the bytes of its extra tickets
+ * cleared first (the earlier call may have put partials there).  Calls
+ * sharing one workspace must not overlap on the GPU.
  */
 SNAPMIND_API int32_t snapmind_paged_gqa_decode_split_tokens(int32_t batch, int32_t n_kv_heads,
                                                int32_t max_seq_len, int32_t block_size);
