@@ -918,11 +918,13 @@ def run_mla_sparse(args, dev, seed, dist, world, cpu_baseline: bool = False) -> 
     select_us = graph_us(lambda: sel.select(qsel, n_chunks_dev, k=MLA_TOPK))
     sparse_us = graph_us(lambda: pool.sparse_decode(0, q_lat, q_pe, idx0, sink=4, window=1024, scale=scale))
     # the dominant kernel (sparse attention + its split merge), each launch timed alone on the
-    # launching stream after an L2 flush: the ~29 MB it reads would otherwise stay in the 126 MB L2
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    # launching stream after an L2 flush: the ~29 MB it reads would otherwise stay in the 126 MB L2.
+    # The flush reads 256 MB (a sum): evicting by writing would leave dirty lines whose write-back
+    # competes with the timed kernel.
+    flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
     evs = []
     for _ in range(20):
-        flush.zero_()
+        flush.sum()
         a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a_.record()
         pool.sparse_decode(0, q_lat, q_pe, idx0, sink=4, window=1024, scale=scale)
@@ -976,7 +978,7 @@ def run_mla_sparse(args, dev, seed, dist, world, cpu_baseline: bool = False) -> 
         "flops_per_launch": int(sparse_flops),
         "attended_tokens_per_launch": int(att_tokens),
         "kernel_us_avg": round(attn_us, 2),
-        "timing": "20 launches, each after a 256 MB L2 flush, CUDA events on the launching stream",
+        "timing": "20 launches, each after reading 256 MB to flush L2, CUDA events on the launching stream",
     }
     res = {
         "value": round(B * world * steps / (ms * 1e-3), 1),
