@@ -30,6 +30,8 @@ namespace {
 constexpr int kPlanThreads = 1024;
 constexpr int kMaxSlots = 8192;
 constexpr int kMaxRequests = 64;
+constexpr int kStageBatch = 4096;  // sequences whose lengths are staged in shared memory
+constexpr int kAdmLog = 2048;      // slots admitted by one launch, remembered for lookups
 
 struct PlanParams {
   int32_t* slot_owner;  // [n_slots] seq * 65536 + chunk, -1 = free
@@ -47,37 +49,90 @@ struct PlanParams {
   int32_t* err;
 };
 
+__host__ __device__ inline int plan_sort_n(int n_slots) {
+  int n = 1;
+  while (n < n_slots) n <<= 1;
+  return n;
+}
+
+// Shared memory of one plan launch: candidate keys [sort_n] (8 B), slot owner and
+// last use [n_slots] each, then (for batches up to kStageBatch) lengths and the
+// prefetched slot of each sequence's just-completed chunk [batch] each, the
+// prefetched slot of each request's chunk [kMaxRequests] and the admission log.
+__host__ __device__ inline size_t plan_smem_bytes(int n_slots, int batch) {
+  const size_t staged = batch <= kStageBatch ? 2 * (size_t)batch : 0;
+  return 8 * (size_t)plan_sort_n(n_slots) + 4 * (2 * (size_t)n_slots + staged + kMaxRequests + kAdmLog);
+}
+
 __device__ __forceinline__ bool chunk_pinned(int c, int len, int chunk, int sink, int window) {
   if (sink > 0 && c == 0) return true;                      // attention sink
   if ((int64_t)(c + 1) * chunk > (int64_t)len - window) return true;  // overlaps the recent window
   return (int64_t)(c + 1) * chunk >= len;                   // active (last, possibly partial) chunk
 }
 
+// The decisions are taken by one thread in a fixed order (the policy is sequential),
+// so every value that thread reads is staged in shared memory first by the whole
+// block: slot owners and last uses, sequence lengths, and the slots of the chunks
+// it will look up.  A prefetched chunk -> slot entry may have changed during the
+// launch; it is trusted only while the slot's owner still names the chunk, else the
+// slots admitted by this launch are searched (an admitted slot is never evicted in
+// the same step).  Global chunk_slot is written by that thread as it decides, so
+// when the log overflows it reads its own writes back.
 __global__ void __launch_bounds__(kPlanThreads) tiered_plan_kernel(PlanParams p) {
-  extern __shared__ unsigned long long cand[];  // candidate keys (power-of-two count), sorted ascending
-  __shared__ int s_ncand, s_next, s_nplan;
-  __shared__ int s_bad;
+  extern __shared__ unsigned long long plan_smem[];
+  const int sort_n = plan_sort_n(p.n_slots);
+  const bool staged = p.batch <= kStageBatch;
+  unsigned long long* cand = plan_smem;  // candidate keys, sorted ascending
+  int32_t* s_owner = reinterpret_cast<int32_t*>(cand + sort_n);
+  int32_t* s_last = s_owner + p.n_slots;
+  int32_t* s_len = s_last + p.n_slots;                     // [batch] when staged
+  int32_t* s_done = s_len + (staged ? p.batch : 0);        // [batch] when staged
+  int32_t* s_req = s_done + (staged ? p.batch : 0);        // [kMaxRequests]
+  int32_t* s_adm = s_req + kMaxRequests;                   // [kAdmLog]
+  __shared__ int s_ncand, s_bad;
   const int tid = threadIdx.x;
+  const int64_t mc = p.max_chunks;
+
+  // ---- stage the state (coalesced, all threads)
+  for (int i = tid; i < p.n_slots; i += kPlanThreads) {
+    s_owner[i] = p.slot_owner[i];
+    s_last[i] = p.slot_last[i];
+  }
+  if (staged) {
+    for (int b = tid; b < p.batch; b += kPlanThreads) {
+      const int old = p.seq_lens[b];
+      s_len[b] = old;
+      int g = -1;
+      if (old > 0 && old % p.chunk == 0 && p.n_new > 0) {
+        const int done = old / p.chunk - 1;
+        if (done < p.max_chunks) g = p.chunk_slot[b * mc + done];
+      }
+      s_done[b] = g;
+    }
+  }
+  if (tid < p.n_req) {
+    const int b = p.req_seq[tid], c = p.req_chunk[tid];
+    s_req[tid] = (b >= 0 && b < p.batch && c >= 0 && c < p.max_chunks) ? p.chunk_slot[b * mc + c] : -1;
+  }
   if (tid == 0) {
-    s_next = 0;
-    s_nplan = 0;
     s_bad = 0;
   }
-  int sort_n = 1;
-  while (sort_n < p.n_slots) sort_n <<= 1;
-  // candidate key: free slots (0, id), evictable (1 + last_use, id), others +inf.
+  __syncthreads();
+  const int32_t* lens0 = staged ? s_len : p.seq_lens;
+
+  // ---- candidate key: free slots (0, id), evictable (1 + last_use, id), others +inf.
   // Pinning is judged with the lengths after this step's growth.
   for (int s = tid; s < sort_n; s += kPlanThreads) {
     unsigned long long key = ~0ull;
     if (s < p.n_slots) {
-      const int owner = p.slot_owner[s];
+      const int owner = s_owner[s];
       if (owner < 0) {
         key = (unsigned long long)s;
       } else {
         const int seq = owner >> 16, c = owner & 0xFFFF;
-        const int len = p.seq_lens[seq] + p.n_new;
+        const int len = lens0[seq] + p.n_new;
         if (!chunk_pinned(c, len, p.chunk, p.sink, p.window))
-          key = ((unsigned long long)(1u + (uint32_t)p.slot_last[s]) << 32) | (uint32_t)s;
+          key = ((unsigned long long)(1u + (uint32_t)s_last[s]) << 32) | (uint32_t)s;
       }
     }
     cand[s] = key;
@@ -99,27 +154,41 @@ __global__ void __launch_bounds__(kPlanThreads) tiered_plan_kernel(PlanParams p)
       __syncthreads();
     }
   }
-  if (tid == 0) {
-    int n = 0;
-    while (n < p.n_slots && cand[n] != ~0ull) ++n;
-    s_ncand = n;
+  // candidates = keys below +inf: the first index holding +inf (the keys are sorted)
+  for (int i = tid; i < sort_n; i += kPlanThreads) {
+    const bool here = cand[i] == ~0ull && (i == 0 || cand[i - 1] != ~0ull);
+    if (here) s_ncand = i;
+    if (i == sort_n - 1 && cand[i] != ~0ull) s_ncand = sort_n;
   }
   __syncthreads();
 
-  // sequential decisions (one thread): deterministic order
+  // ---- sequential decisions (one thread, shared memory): deterministic order
   if (tid == 0) {
+    int next = 0, nadm = 0, nplan = 0, bad = 0;
+    bool adm_overflow = false;
+    const int ncand = min(s_ncand, p.n_slots);
+    // slot holding chunk c of sequence seq, or -1; g0 = its entry before this launch
+    auto resident_slot = [&](int seq, int c, int g0) -> int {
+      const int key = (seq << 16) | c;
+      if (g0 >= 0 && g0 < p.n_slots && s_owner[g0] == key) return g0;
+      if (adm_overflow) return p.chunk_slot[seq * mc + c];
+      for (int a = 0; a < nadm; ++a)
+        if (s_owner[s_adm[a]] == key) return s_adm[a];
+      return -1;
+    };
     auto take_slot = [&](int seq, int c) -> int {
-      while (s_next < s_ncand) {
-        const int s = (int)(cand[s_next++] & 0xFFFFFFFFull);
-        const int owner = p.slot_owner[s];
+      while (next < ncand) {
+        const int s = (int)(cand[next++] & 0xFFFFFFFFull);
+        const int owner = s_owner[s];
         if (owner >= 0) {
-          if (p.slot_last[s] == p.step) continue;  // touched or admitted in this step
-          const int oseq = owner >> 16, oc = owner & 0xFFFF;
-          p.chunk_slot[(int64_t)oseq * p.max_chunks + oc] = -1;
+          if (s_last[s] == p.step) continue;  // touched or admitted in this step
+          p.chunk_slot[(int64_t)(owner >> 16) * mc + (owner & 0xFFFF)] = -1;
         }
-        p.slot_owner[s] = (seq << 16) | c;
-        p.slot_last[s] = p.step;
-        p.chunk_slot[(int64_t)seq * p.max_chunks + c] = s;
+        s_owner[s] = (seq << 16) | c;
+        s_last[s] = p.step;
+        p.chunk_slot[seq * mc + c] = s;
+        if (nadm < kAdmLog) s_adm[nadm++] = s;
+        else adm_overflow = true;
         return s;
       }
       return -1;
@@ -127,74 +196,92 @@ __global__ void __launch_bounds__(kPlanThreads) tiered_plan_kernel(PlanParams p)
     // 1. growth: a sequence entering a new chunk needs a slot; the chunk it
     //    completed goes to its outbound staging slot
     for (int b = 0; b < p.batch; ++b) {
-      const int old = p.seq_lens[b];
+      const int old = staged ? s_len[b] : p.seq_lens[b];
       const int len = old + p.n_new;
       const int c_first = (old + p.chunk - 1) / p.chunk;   // first chunk not yet allocated
       const int c_last = (len + p.chunk - 1) / p.chunk;    // chunks needed after growth
       if (old > 0 && old % p.chunk == 0 && p.n_new > 0) {
         const int done = old / p.chunk - 1;
-        const int src = p.chunk_slot[(int64_t)b * p.max_chunks + done];
-        if (src >= 0 && s_nplan < p.max_plan) {
-          p.plan[2 * s_nplan] = src;
-          p.plan[2 * s_nplan + 1] = p.stage_out_base + b;
-          ++s_nplan;
+        if (done < p.max_chunks) {
+          const int src = resident_slot(b, done, staged ? s_done[b] : p.chunk_slot[b * mc + done]);
+          if (src >= 0 && nplan < p.max_plan) {
+            p.plan[2 * nplan] = src;
+            p.plan[2 * nplan + 1] = p.stage_out_base + b;
+            ++nplan;
+          }
         }
       }
       for (int c = c_first; c < c_last; ++c) {
         if (c >= p.max_chunks || c > 0xFFFF) {
-          s_bad |= SNAPMIND_DEVERR_TABLE;
+          bad |= SNAPMIND_DEVERR_TABLE;
           break;
         }
-        if (take_slot(b, c) < 0) s_bad |= SNAPMIND_DEVERR_OUT_OF_BLOCKS;
+        if (take_slot(b, c) < 0) bad |= SNAPMIND_DEVERR_OUT_OF_BLOCKS;
       }
       p.seq_lens[b] = len;
+      if (staged) s_len[b] = len;
     }
     // 2. requests
     for (int i = 0; i < p.n_req; ++i) {
       const int b = p.req_seq[i], c = p.req_chunk[i];
       if (b < 0 || b >= p.batch) continue;
-      const int len = p.seq_lens[b];
+      const int len = staged ? s_len[b] : p.seq_lens[b];
       if (c < 0 || c >= p.max_chunks || (int64_t)c * p.chunk >= len) continue;
-      const int cur = p.chunk_slot[(int64_t)b * p.max_chunks + c];
+      const int cur = resident_slot(b, c, s_req[i]);
       if (cur >= 0) {
-        p.slot_last[cur] = p.step;  // already resident: touch
+        s_last[cur] = p.step;  // already resident: touch
         continue;
       }
       const int s = take_slot(b, c);
       if (s < 0) {
-        s_bad |= SNAPMIND_DEVERR_OUT_OF_BLOCKS;
+        bad |= SNAPMIND_DEVERR_OUT_OF_BLOCKS;
         continue;
       }
-      if (s_nplan < p.max_plan) {
-        p.plan[2 * s_nplan] = p.stage_in_base + i;
-        p.plan[2 * s_nplan + 1] = s;
-        ++s_nplan;
+      if (nplan < p.max_plan) {
+        p.plan[2 * nplan] = p.stage_in_base + i;
+        p.plan[2 * nplan + 1] = s;
+        ++nplan;
       }
     }
-    *p.plan_count = s_nplan;
+    *p.plan_count = nplan;
+    s_bad = bad;
   }
   __syncthreads();
 
-  // 3. attention tables: one warp per sequence, ballot compaction in chunk order
+  // ---- write the slot state back
+  for (int i = tid; i < p.n_slots; i += kPlanThreads) {
+    p.slot_owner[i] = s_owner[i];
+    p.slot_last[i] = s_last[i];
+  }
+
+  // ---- 3. attention tables: one warp per sequence, ballot compaction in chunk order;
+  // each lane loads its 4 entries of a 128-chunk group before using any of them
   const int warp = tid >> 5, lane = tid & 31;
   for (int b = warp; b < p.batch; b += kPlanThreads / 32) {
-    const int len = p.seq_lens[b];
+    const int len = staged ? s_len[b] : p.seq_lens[b];
     const int nchunks = min(p.max_chunks, (len + p.chunk - 1) / p.chunk);
+    const int32_t* row = p.chunk_slot + b * mc;
     int n = 0, tokens = 0;
-    for (int c0 = 0; c0 < nchunks; c0 += 32) {
-      const int c = c0 + lane;
-      const int s = c < nchunks ? p.chunk_slot[(int64_t)b * p.max_chunks + c] : -1;
-      const unsigned mask = __ballot_sync(0xffffffffu, s >= 0);
-      if (s >= 0) {
-        const int pos = n + __popc(mask & ((1u << lane) - 1));
-        p.tables[(int64_t)b * p.max_chunks + pos] = s;
-      }
-      int tk = s >= 0 ? min(p.chunk, len - c * p.chunk) : 0;
+    for (int c0 = 0; c0 < nchunks; c0 += 128) {
+      int sv[4];
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) tk += __shfl_xor_sync(0xffffffffu, tk, off);
-      tokens += tk;
-      n += __popc(mask);
+      for (int k = 0; k < 4; ++k) {
+        const int c = c0 + 32 * k + lane;
+        sv[k] = c < nchunks ? row[c] : -1;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int c = c0 + 32 * k + lane;
+        const unsigned mask = __ballot_sync(0xffffffffu, sv[k] >= 0);
+        if (sv[k] >= 0) {
+          p.tables[b * mc + n + __popc(mask & ((1u << lane) - 1))] = sv[k];
+          tokens += min(p.chunk, len - c * p.chunk);
+        }
+        n += __popc(mask);
+      }
     }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) tokens += __shfl_xor_sync(0xffffffffu, tokens, off);
     if (lane == 0) p.table_lens[b] = tokens;
   }
   if (tid == 0 && s_bad) flag_error(p.err, s_bad);
@@ -215,7 +302,7 @@ __global__ void __launch_bounds__(256) tiered_move_kernel(MoveParams p) {
   const int e = blockIdx.x, layer = blockIdx.y, kv = blockIdx.z;
   if (e >= *p.plan_count) return;
   const int src = p.plan[2 * e], dst = p.plan[2 * e + 1];
-  const char* base = p.pool[kv] + layer * p.layer_stride;
+  const char* base = (kv ? p.pool[1] : p.pool[0]) + layer * p.layer_stride;  // no local copy of the array
   const Vec16* s = reinterpret_cast<const Vec16*>(base + src * p.slot_bytes);
   Vec16* d = reinterpret_cast<Vec16*>(const_cast<char*>(base) + dst * p.slot_bytes);
   const int n = (int)(p.slot_bytes / 16);
@@ -268,9 +355,7 @@ int snapmind_tiered_plan(int32_t* slot_owner, int32_t* slot_last, int32_t* chunk
     p.req_chunk[i] = req_chunk[i];
   }
   p.err = err_word;
-  int sort_n = 1;
-  while (sort_n < n_slots) sort_n <<= 1;
-  const size_t smem = sizeof(unsigned long long) * sort_n;
+  const size_t smem = plan_smem_bytes(n_slots, batch);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(tiered_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_status(e, "tiered_plan smem attribute");
