@@ -4,46 +4,46 @@
 // A decode step of DeepSeek-style absorbed MLA is, per sequence, a 128-row
 // attention: Q [128 heads x 576] against the attended latent rows
 // [n x 576] (latent 512 | rope 64), output [128 x 512] over the first 512
-// columns of the same rows.  A full-width output accumulator (128 x 512 f32)
-// would fill a whole SM's tensor memory and a full Q (144 KB) most of its
-// shared memory, so four independent CTAs share each (split, sequence):
-//   CTA q = 2 hh + dh owns heads [64 hh, 64 hh + 64) and output dims
-//   [256 dh, 256 dh + 256).  Each scores its 64 heads over the full
-//   576-wide contraction (tcgen05.mma with M = 64), so no partial result ever
-//   crosses between CTAs; the two dh CTAs of a head half compute the same
-//   scores (bit for bit: same inputs, same instruction sequence) and each
-//   applies them to its own half of V.
-// CTA = 6 warps: warps 0-3 softmax, warp 4 TMA producer, warp 5 MMA issuer.
-//   Shared memory (1024-aligned, 128-byte swizzle, written by TMA):
-//     Q: 9 k-blocks x [64 rows x 64] = 72 KB, resident;
-//     2 stages of one attended chunk of 64 rows, 9 k-blocks x [64 x 64]
-//       (72 KB: one 3-D TMA box for the 8 latent k-blocks, one 2-D box for
-//       the rope k-block);
-//     P: [64 heads x 64 tokens] bf16 = 8 KB, written by the softmax threads.
-//   TMEM (M = 64 accumulators keep row m in lane 32 (m / 16) + m % 16):
-//     O [64 x 256] f32 at column 0; two score buffers [64 x 64] at columns 256
-//     and 320.
-//   Per chunk of 64 tokens:
-//     S = Q K^T: 36 MMAs (M 64, N 64, K 16), K-major operands;
-//     softmax: warp w owns head rows 16 w .. 16 w + 15, four threads per row
-//       (tcgen05.ld.16x256b: thread t holds rows t / 4 and t / 4 + 8, 16 of
-//       the 64 tokens each; row maxima and sums take two shuffles); tokens
-//       outside the selection are masked; a reference maximum is raised only
-//       when a score exceeds it by 2^8 (then O's rows are rescaled in TMEM);
-//       P = exp2(s - m) is written as bf16;
-//     O += P V: 4 MMAs (M 64, N 256, K 16), V = this CTA's 4 latent k-blocks
-//       of the staged rows, read MN-major.
-//   The MMA warp issues whatever is ready (PV of the oldest chunk whose P is
-//   written, else the scores of the next staged chunk), so the scores of the
-//   next chunk overlap the softmax of the current one.  The producer keeps one
-//   chunk loading and the next kPrefetch chunks prefetched into L2 (TMA
-//   prefetch, no shared memory), so a stage that frees up is refilled from L2.
+// columns of the same rows.
+//
+// Orientation.  A tcgen05.mma of M = 64 rows takes as long as one of M = 128
+// (its time follows N), so the M side of every product here is 128 attended
+// tokens (two 64-token chunks), and the heads are the N side:
+//   S^T [128 tokens x 64 heads] = K [128 x 576] . Q^T: 36 MMAs (M 128, N 64, K 16);
+//   O^T [512 dims x 64 heads] += V^T [512 x 128] . P^T [128 x 64]: 32 MMAs
+//     (4 blocks of 128 dims x 8 steps of 16 tokens).
+// CTA = (head half hh, split, sequence): heads [64 hh, 64 hh + 64), every
+// output dim, the split's attended chunks two at a time ("pairs").  No
+// product is computed twice and nothing crosses between CTAs.
+// CTA = 6 warps: warps 0-3 softmax (thread = token of the pair = TMEM lane),
+// warp 4 TMA producer, warp 5 MMA issuer.
+//   Shared memory (1024-aligned, 128-byte swizzle):
+//     Q^T: 9 k-blocks x [64 heads x 64] = 72 KB, resident;
+//     one pair stage: 9 k-blocks x [128 tokens x 64] = 144 KB (chunk 2q in
+//       rows 0-63 of every k-block, chunk 2q + 1 in rows 64-127; one 2-D TMA
+//       box per (chunk, k-block)).  Once the scores are done the rope k-block
+//       is free and holds P^T [128 tokens x 64 heads] for P V.
+//   TMEM (M = 128: row m in lane m): O^T as 4 blocks [128 dims x 64 heads] at
+//     columns 0-255, S^T [128 tokens x 64 heads] at column 256.
+//   Per pair: S^T over the 9 k-blocks (K-major operands); softmax: thread t
+//     loads its token's 64 scores (tcgen05.ld 32x32b) and masks the token if
+//     it is not attended; the scores are checked against a per-head reference
+//     maximum that is raised only when a score exceeds it by 2^8 (then the
+//     exact per-head maximum of the pair is reduced across the 128 threads and
+//     O's columns are rescaled in TMEM); P = exp2(s - m) is written as a bf16
+//     row of P^T; a row that holds no token is zeroed in the latent k-blocks
+//     (0 x garbage must not reach O); O^T += V^T P^T (V^T read MN-major from
+//     the staged rows, P^T MN-major); meanwhile the per-head sums of P are
+//     reduced across each warp by a transposing butterfly.
+//   The producer refills the stage once O^T += V^T P^T of the pair is done and
+//   keeps the next kPrefetch chunks prefetched into L2 (TMA prefetch, no
+//   shared memory), so the refill is served from L2.
 //   Handshakes are mbarriers (tcgen05.commit for the tensor core), every wait
 //   is bounded (about a second) and ends early once another role gave up, and
 //   TMEM is released on every path.
-// Splits write fp32 partials (unnormalised output [sequence][split][dim][head],
-// max and sum [sequence][split][2][head]) into the workspace region the paged
-// GQA decode layout sizes for them; a second kernel merges them.
+// Splits write fp32 partials (unnormalised output [sequence][split][head][dim],
+// then max and sum [sequence][split][2][head]) into the workspace region the
+// paged GQA decode layout sizes for them; a second kernel merges them.
 //
 // The attended positions are those of the mma.sync kernel (sparse_mla.cu):
 // the selected chunks of the lookahead indexer
@@ -63,20 +63,21 @@ namespace {
 using namespace tc;
 
 constexpr int kH = 128;                                 // heads of a sequence
-constexpr int kHC = 64;                                 // heads per CTA = MMA M
+constexpr int kHC = 64;                                 // heads per CTA = MMA N
 constexpr int kR = 512, kP = 64;
 constexpr int kKB = (kR + kP) / 64;                     // 9 k-blocks of 64 elements
-constexpr int kBs = 64;                                 // block (chunk) size = tokens per score tile
-constexpr int kDH = kR / 2;                             // output dims per CTA
+constexpr int kBs = 64;                                 // block (chunk) size
+constexpr int kPair = 2 * kBs;                          // tokens per pair = MMA M
 constexpr int kSoftmaxThreads = 128;
 constexpr int kProducerWarp = 4, kMmaWarp = 5;
 constexpr int kThreads = 192;
-constexpr uint32_t kQBlock = kHC * 128;                 // one k-block of Q: 8 KB
+constexpr uint32_t kQBlock = kHC * 128;                 // one k-block of Q^T: 8 KB
 constexpr uint32_t kQBytes = kKB * kQBlock;             // 72 KB
-constexpr uint32_t kStBlock = kBs * 128;                // one k-block of a chunk: 8 KB
-constexpr uint32_t kStageBytes = kKB * kStBlock;        // 72 KB
-constexpr int kStages = 2;
-constexpr uint32_t kPBytes = kHC * kBs * 2;             // 8 KB
+constexpr uint32_t kHalfBlock = kBs * 128;              // one chunk's rows of a k-block: 8 KB
+constexpr uint32_t kStBlock = kPair * 128;              // one k-block of the pair: 16 KB
+constexpr uint32_t kStageBytes = kKB * kStBlock;        // 144 KB
+constexpr uint32_t kChunkBytes = kKB * kHalfBlock;      // bytes one chunk brings: 72 KB
+constexpr uint32_t kPOff = (kKB - 1) * kStBlock;        // P^T in the rope k-block
 constexpr int kBits = 3072;                             // chunks per sequence (bitmaps; longer tables take the mma.sync kernel)
 constexpr uint32_t kTmemCols = 512, kColO = 0, kColS = 256;
 constexpr float kRescale = 8.f;                         // log2 headroom of the reference maximum
@@ -84,26 +85,27 @@ constexpr int kPrefetch = 4;                            // chunks prefetched int
 constexpr int kRing = 64;                               // resolved (chunk, block) pairs kept ahead
 
 struct Ctrl {
-  uint64_t full[kStages];    // producer -> MMA, softmax: chunk staged
-  uint64_t empty[kStages];   // MMA commit after O += P V of the chunk: stage free
-  uint64_t s_full[2];        // MMA commit after S = Q K^T: buffer ready
-  uint64_t s_empty[2];       // softmax threads: buffer read
+  uint64_t full;    // producer -> MMA, softmax: pair staged
+  uint64_t empty;   // MMA commit after O^T += V^T P^T: stage free
+  uint64_t s_full;  // MMA commit after S^T: scores ready
+  uint64_t p_full;  // softmax threads: P^T written, empty rows zeroed (and O rescaled)
+  uint64_t o_done;  // MMA commit after O^T += V^T P^T
   uint64_t q_full;
-  uint64_t p_full;           // softmax threads: P written (and O rescaled)
-  uint64_t o_done;           // MMA commit after O += P V
   uint32_t tmem_base;
   int32_t abort;
   int32_t count;
-  int32_t chunk_phys[kStages];  // block and chunk id of each staged chunk
-  int32_t chunk_id[kStages];
+  int32_t rescale;              // a raise step must rescale some head's O columns
   int32_t ring_c[kRing];        // chunk id and block of chunk j of the split at j % kRing
   int32_t ring_p[kRing];
   uint32_t sel_bits[kBits / 32];
   uint32_t inc_bits[kBits / 32];
   int32_t word_pre[kBits / 32 + 1];
+  float m_ref[kHC];             // per-head reference maximum (log2 units of score * scale)
+  float alpha[kHC];             // per-head rescale factor of a raise step; 1 / sum in the epilogue
+  float red[4][kHC];            // per-warp partial maxima / sums
 };
 
-constexpr size_t kSmemBytes = 1024 + kQBytes + kStages * kStageBytes + kPBytes + sizeof(Ctrl);
+constexpr size_t kSmemBytes = 1024 + kQBytes + kStageBytes + sizeof(Ctrl);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 __device__ __forceinline__ int chunk_of_rank(const Ctrl& C, int words, int rank) {
@@ -134,6 +136,9 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi
   __half2 v = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+template <typename T> __device__ __forceinline__ T to_elem(float x);
+template <> __device__ __forceinline__ __nv_bfloat16 to_elem<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half to_elem<__half>(float x) { return __float2half_rn(x); }
 
 // Waits of the pipeline roles: bounded, and cut short once another role gave up.
 __device__ __forceinline__ bool role_wait(const Ctrl& C, uint32_t bar, uint32_t parity) {
@@ -151,51 +156,69 @@ __device__ __forceinline__ void give_up(Ctrl& C, int32_t* err) {
   flag_error(err, SNAPMIND_DEVERR_TIMEOUT);
 }
 
-// Maximum over the four threads that share a row (lanes 4 r .. 4 r + 3).
-__device__ __forceinline__ float quad_max(float x) {
-  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
-  return fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+// Named barrier 1 over the 128 softmax threads (the producer and MMA warps do not take part).
+__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// The same barrier, returning whether `v` holds in any of the 128 threads.
+__device__ __forceinline__ bool softmax_any(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.or.pred q, 1, 128, p; selp.u32 %0, 1, 0, q; }"
+      : "=r"(r)
+      : "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
 }
-__device__ __forceinline__ float quad_sum(float x) {
-  x += __shfl_xor_sync(0xffffffffu, x, 1);
-  return x + __shfl_xor_sync(0xffffffffu, x, 2);
+
+// Reduces 64 values per lane over the warp's 32 lanes by a transposing butterfly
+// (62 shuffles): afterwards lane l holds, in v[0] and v[1], the sum (or maximum)
+// over the warp of values 2 l and 2 l + 1.
+template <bool kMax>
+__device__ __forceinline__ void warp_transpose_reduce(float (&v)[64], int lane) {
+#pragma unroll
+  for (int step = 0; step < 5; ++step) {
+    const int mask = 16 >> step;  // partner distance
+    const int n = 32 >> step;     // this lane keeps n of its current 2 n values
+    const bool upper = (lane & mask) != 0;
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      const float send = upper ? v[i] : v[i + n];
+      const float keep = upper ? v[i + n] : v[i];
+      const float got = __shfl_xor_sync(0xffffffffu, send, mask);
+      v[i] = kMax ? fmaxf(keep, got) : keep + got;
+    }
+  }
 }
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     sparse_mla_umma_kernel(const __grid_constant__ CUtensorMap qlat_map, const __grid_constant__ CUtensorMap qpe_map,
-                           const __grid_constant__ CUtensorMap lat_map, const __grid_constant__ CUtensorMap rope_map,
-                           SparseParams p) {
+                           const __grid_constant__ CUtensorMap lat_map, const __grid_constant__ CUtensorMap lat3_map,
+                           const __grid_constant__ CUtensorMap rope_map, SparseParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_s = base;
   uint8_t* st_s = q_s + kQBytes;
-  uint8_t* p_s = st_s + kStages * kStageBytes;
-  Ctrl& C = *reinterpret_cast<Ctrl*>(p_s + kPBytes);
+  Ctrl& C = *reinterpret_cast<Ctrl*>(st_s + kStageBytes);
 
-  const int hh = blockIdx.x >> 1, dh = blockIdx.x & 1;  // head half, output-dim half
+  const int hh = blockIdx.x;  // head half
   const int s = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kIdescS = idesc_f16(kBf16, kHC, kBs, false, false);
-  constexpr uint32_t kIdescPV = idesc_f16(kBf16, kHC, kDH, false, true);
+  constexpr uint32_t kIdescS = idesc_f16(kBf16, kPair, kHC, false, false);
+  constexpr uint32_t kIdescPV = idesc_f16(kBf16, kPair, kHC, true, true);
   const DecodeParams& dp = p.dp;
   const int q_row0 = b * kH + hh * kHC;  // first row of this CTA's heads in q_lat / q_pe
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(smem_u32(&C.full[i]), 1);
-      mbar_init(smem_u32(&C.empty[i]), 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&C.s_full[i]), 1);
-      mbar_init(smem_u32(&C.s_empty[i]), kSoftmaxThreads);
-    }
-    mbar_init(smem_u32(&C.q_full), 1);
+    mbar_init(smem_u32(&C.full), 1);
+    mbar_init(smem_u32(&C.empty), 1);
+    mbar_init(smem_u32(&C.s_full), 1);
     mbar_init(smem_u32(&C.p_full), kSoftmaxThreads);
     mbar_init(smem_u32(&C.o_done), 1);
+    mbar_init(smem_u32(&C.q_full), 1);
     C.abort = 0;
+    C.rescale = 0;
     mbar_init_fence();
     // Q depends only on the sequence: its copy overlaps the selection set-up below
     const uint32_t qb = smem_u32(&C.q_full);
@@ -207,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(smem_u32(&C.tmem_base), kTmemCols);
     tmem_relinquish();
   }
+  if (tid < kHC) C.m_ref[tid] = -INFINITY;
 
   // ---- attended chunks of sequence b: bitmaps and the prefix of their counts
   // (the length and the first selected ids are loaded together)
@@ -262,23 +286,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = C.tmem_base;
   const int count = C.count;
 
-  // chunks of this split (the same for the four CTAs of a (split, sequence))
-  const int per = (count + p.n_splits - 1) / max(p.n_splits, 1);
+  // chunks of this split (the same for both head halves): an even count per split, so
+  // only the last split can end in a half-empty pair
+  int per = (count + p.n_splits - 1) / max(p.n_splits, 1);
+  per += per & 1;
   const int c_lo = min(count, s * per), c_hi = min(count, c_lo + per);
   const int n_ck = c_hi - c_lo;
+  const int n_pairs = (n_ck + 1) / 2;
   const bool direct = (p.n_splits == 1);
 
   if (n_ck > 0) {
     if (warp == kProducerWarp) {
       // ---------------------------------------------------------------- TMA producer
       // The warp resolves the blocks of 32 chunks at a time (one table read per lane)
-      // into a ring; lane 0 loads chunk i into stage i % 2 once PV(i - 2) freed it,
-      // and keeps chunks up to i + kPrefetch prefetched into L2, so a load that
-      // waited for its stage finds its rows there.
-      int located = 0, prefetched = min(n_ck, kStages), issued = 0;
+      // into a ring; lane 0 loads pair q into the stage once O^T += V^T P^T of pair
+      // q - 1 is done, and keeps the chunks up to 2 q + 2 + kPrefetch prefetched into
+      // L2, so the refill finds its rows there.
+      int located = 0, prefetched = min(n_ck, 2), issued = -1;
       bool ok = true;
-      for (int i = 0; i < n_ck && ok; ++i) {
-        if (min(n_ck, i + kPrefetch + 1) > located) {  // warp-uniform
+      for (int q = 0; q < n_pairs && ok; ++q) {
+        while (min(n_ck, 2 * q + 2 + kPrefetch) > located) {  // warp-uniform
           const int j = located + lane;
           if (j < n_ck) {
             const int c = chunk_of_rank(C, words, c_lo + j);
@@ -291,31 +318,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           located += 32;
         }
         if (lane == 0) {
-          const int st = i % kStages;
-          if (i >= kStages && !role_wait(C, smem_u32(&C.empty[st]), ((i / kStages) - 1) & 1)) {
+          if (q > 0 && !role_wait(C, smem_u32(&C.empty), (q - 1) & 1)) {
             give_up(C, dp.err);
             ok = false;
           } else {
-            const int32_t phys = C.ring_p[i % kRing];
-            C.chunk_phys[st] = phys;
-            C.chunk_id[st] = C.ring_c[i % kRing];
-            const uint32_t bar = smem_u32(&C.full[st]);
-            if (phys < 0) {
-              flag_error(dp.err, SNAPMIND_DEVERR_BLOCK_ID);
+            const uint32_t bar = smem_u32(&C.full);
+            uint32_t bytes = 0;
+            for (int h = 0; h < 2; ++h) {
+              const int i = 2 * q + h;
+              if (i >= n_ck) continue;
+              if (C.ring_p[i % kRing] >= 0) bytes += kChunkBytes;
+              else flag_error(dp.err, SNAPMIND_DEVERR_BLOCK_ID);
+            }
+            if (bytes == 0) {
               mbar_arrive(bar);
             } else {
-              uint8_t* stage = st_s + st * kStageBytes;
-              mbar_arrive_expect_tx(bar, kStageBytes);
-              const int y = phys * kBs;
-              tma_load_3d(smem_u32(stage), &lat_map, 0, y, 0, bar);  // the 8 latent k-blocks
-              tma_load_2d(smem_u32(stage + (kKB - 1) * kStBlock), &rope_map, 0, y, bar);
+              mbar_arrive_expect_tx(bar, bytes);
+              for (int h = 0; h < 2; ++h) {
+                const int i = 2 * q + h;
+                const int32_t phys = i < n_ck ? C.ring_p[i % kRing] : -1;
+                if (phys < 0) continue;
+                const int y = phys * kBs;
+                for (int kb = 0; kb < kKB - 1; ++kb)
+                  tma_load_2d(smem_u32(st_s + kb * kStBlock + h * kHalfBlock), &lat_map, kb * 64, y, bar);
+                tma_load_2d(smem_u32(st_s + (kKB - 1) * kStBlock + h * kHalfBlock), &rope_map, 0, y, bar);
+              }
             }
-            issued = i + 1;
-            for (; prefetched < min(n_ck, i + kPrefetch + 1); ++prefetched) {
-              const int32_t pp = C.ring_p[prefetched % kRing];
-              if (pp >= 0) {
-                tma_prefetch_3d(&lat_map, 0, pp * kBs, 0);
-                tma_prefetch_2d(&rope_map, 0, pp * kBs);
+            issued = q;
+            for (; prefetched < min(n_ck, 2 * q + 2 + kPrefetch); ++prefetched) {
+              const int32_t pb = C.ring_p[prefetched % kRing];
+              if (pb >= 0) {
+                tma_prefetch_3d(&lat3_map, 0, pb * kBs, 0);
+                tma_prefetch_2d(&rope_map, 0, pb * kBs);
               }
             }
           }
@@ -324,8 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (lane == 0) {
         // before the shared memory is released: every copy issued has landed (bounded)
-        for (int j = max(0, issued - kStages); j < issued; ++j)
-          mbar_wait(smem_u32(&C.full[j % kStages]), (j / kStages) & 1);
+        if (issued >= 0) mbar_wait(smem_u32(&C.full), issued & 1);
         mbar_wait(smem_u32(&C.q_full), 0);
       }
     } else if (warp == kMmaWarp) {
@@ -333,60 +366,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         bool ok = role_wait(C, smem_u32(&C.q_full), 0);
         uint32_t last_bar = 0, last_parity = 0;  // the latest commit: covers every MMA issued
-        auto issue_s = [&](int i) {  // S = Q K^T of chunk i over the full 576 columns
-          const uint8_t* stage = st_s + (i % kStages) * kStageBytes;
-          const uint32_t d = tmem + kColS + (i & 1) * kBs;
+        for (int q = 0; q < n_pairs && ok; ++q) {
+          if (!role_wait(C, smem_u32(&C.full), q & 1)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
+          // S^T = K Q^T over the 576 columns: the stage's token rows (A) against Q^T (B)
 #pragma unroll 1
           for (int kb = 0; kb < kKB; ++kb) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = smem_desc(smem_u32(q_s + kb * kQBlock + kk * 32), 16, 1024, kSwizzle128B);
-              const uint64_t bd = smem_desc(smem_u32(stage + kb * kStBlock + kk * 32), 16, 1024, kSwizzle128B);
-              umma_f16(d, ad, bd, kIdescS, (kb > 0 || kk > 0) ? 1u : 0u);
+              const uint64_t ad = smem_desc(smem_u32(st_s + kb * kStBlock + kk * 32), 16, 1024, kSwizzle128B);
+              const uint64_t bd = smem_desc(smem_u32(q_s + kb * kQBlock + kk * 32), 16, 1024, kSwizzle128B);
+              umma_f16(tmem + kColS, ad, bd, kIdescS, (kb > 0 || kk > 0) ? 1u : 0u);
             }
           }
-          umma_commit(smem_u32(&C.s_full[i & 1]));
-          last_bar = smem_u32(&C.s_full[i & 1]);
-          last_parity = (i >> 1) & 1;
-        };
-        auto issue_pv = [&](int i) {  // O += P V of chunk i (this CTA's 256 output dims)
-          const uint8_t* v = st_s + (i % kStages) * kStageBytes + dh * 4 * kStBlock;
-          tc_fence_after();
-#pragma unroll
-          for (int ks = 0; ks < kBs / 16; ++ks) {
-            const uint64_t ad = smem_desc(smem_u32(p_s + ks * 32), 16, 1024, kSwizzle128B);
-            const uint64_t bd = smem_desc(smem_u32(v + ks * 16 * 128), kStBlock, 1024, kSwizzle128B);
-            umma_f16(tmem + kColO, ad, bd, kIdescPV, (i > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(smem_u32(&C.s_full));
+          last_bar = smem_u32(&C.s_full);
+          last_parity = q & 1;
+          if (!role_wait(C, smem_u32(&C.p_full), q & 1)) {
+            ok = false;
+            break;
           }
-          umma_commit(smem_u32(&C.empty[i % kStages]));
+          tc_fence_after();
+          // O^T += V^T P^T: dim block j = latent k-blocks 2 j, 2 j + 1 (MN-major), P^T
+          // (MN-major), 16 tokens a step
+#pragma unroll 1
+          for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int ks = 0; ks < kPair / 16; ++ks) {
+              const uint64_t ad =
+                  smem_desc(smem_u32(st_s + 2 * j * kStBlock + ks * 16 * 128), kStBlock, 1024, kSwizzle128B);
+              const uint64_t bd = smem_desc(smem_u32(st_s + kPOff + ks * 16 * 128), kStBlock, 1024, kSwizzle128B);
+              umma_f16(tmem + kColO + j * kHC, ad, bd, kIdescPV, (q > 0 || ks > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(smem_u32(&C.empty));
           umma_commit(smem_u32(&C.o_done));
           last_bar = smem_u32(&C.o_done);
-          last_parity = i & 1;
-        };
-        // Issue whichever is ready: O += P V of the oldest chunk whose P is written (it
-        // frees a stage), else the scores of the next staged chunk (at most two score
-        // buffers ahead).  Between polls the thread backs off briefly, leaving the
-        // issue slots of its SM sub-partition to the softmax warp there.
-        int ns = 0, np = 0;  // next chunk to score, next chunk for O += P V
-        long long idle_since = clock64();
-        while (ok && np < n_ck) {
-          bool progressed = false;
-          if (np < ns && mbar_test_wait(smem_u32(&C.p_full), np & 1)) {
-            issue_pv(np++);
-            progressed = true;
-          } else if (ns < n_ck && mbar_test_wait(smem_u32(&C.full[ns % kStages]), (ns / kStages) & 1) &&
-                     (ns < 2 || mbar_test_wait(smem_u32(&C.s_empty[ns & 1]), ((ns >> 1) - 1) & 1))) {
-            issue_s(ns++);
-            progressed = true;
-          }
-          if (progressed) {
-            idle_since = clock64();
-          } else if (*reinterpret_cast<const volatile int32_t*>(&C.abort) || clock64() - idle_since > kWaitTicks) {
-            ok = false;
-          } else {
-            __nanosleep(32);
-          }
+          last_parity = q & 1;
         }
         if (!ok) {
           give_up(C, dp.err);
@@ -395,179 +414,159 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else {
       // ---------------------------------------------------------------- softmax warps 0-3
-      // thread: rows ra = 16 warp + lane / 4 and rb = ra + 8 of this CTA's 64 heads,
-      // tokens 8 j + 2 cq + {0, 1} of every chunk (j = 0..7)
-      const int cq = lane & 3;
-      const int ra = warp * 16 + (lane >> 2), rb = ra + 8;
+      // thread t = token t of the pair (TMEM lane t): chunk 2 q + t / 64, row t % 64
+      const int t = tid;
       const uint32_t t_w = tmem + ((uint32_t)(warp * 32) << 16);
       const float c2 = p.scale * 1.4426950408889634f;
-      float ma_ref = -INFINITY, mb_ref = -INFINITY, la = 0.f, lb = 0.f;  // log2 units of score * scale
-      uint8_t* prow_a = p_s + ra * 128;
-      uint8_t* prow_b = p_s + rb * 128;
-      const uint32_t psw = (uint32_t)(ra & 7);  // rb & 7 is the same
+      uint8_t* prow = st_s + kPOff + t * 128;
+      const uint32_t psw = (uint32_t)(t & 7);
+      float l0 = 0.f, l1 = 0.f;  // sums of P over this warp's tokens for heads 2 lane, 2 lane + 1
       bool ok = true;
-      for (int i = 0; i < n_ck; ++i) {
-        const int st = i % kStages, sb = i & 1;
-        ok = role_wait(C, smem_u32(&C.full[st]), (i / kStages) & 1) &&
-             role_wait(C, smem_u32(&C.s_full[sb]), (i >> 1) & 1);
-        if (__any_sync(0xffffffffu, !ok)) {
+      for (int q = 0; q < n_pairs; ++q) {
+        ok = role_wait(C, smem_u32(&C.full), q & 1) && role_wait(C, smem_u32(&C.s_full), q & 1);
+        if (softmax_any(!ok)) {
           ok = false;
           break;
         }
-        const int phys = C.chunk_phys[st], c = C.chunk_id[st];
-        const int pos0 = c * kBs;
-        const int good = phys < 0 ? 0 : max(0, min(kBs, len - pos0));  // rows holding a token
-        // attended tokens of the chunk as a bit mask: [0, good) for a selected chunk,
-        // else [0, min(good, sink - pos0)) and [max(0, wstart - pos0), good)
-        uint64_t vmask;
-        {
-          const uint64_t below_good = good >= 64 ? ~0ull : ((1ull << good) - 1ull);
-          const bool selected = phys >= 0 && ((C.sel_bits[c >> 5] >> (c & 31)) & 1u);
-          if (selected) {
-            vmask = below_good;
-          } else {
-            const int a = max(0, min(64, sink - pos0));
-            const int w = max(0, min(64, wstart - pos0));
-            const uint64_t sink_bits = a >= 64 ? ~0ull : ((1ull << a) - 1ull);
-            const uint64_t win_bits = w >= 64 ? 0ull : ~((1ull << w) - 1ull);
-            vmask = (sink_bits | win_bits) & below_good;
-          }
+        const int i = 2 * q + (t >> 6);
+        int c = 0, phys = -1;
+        if (i < n_ck) {
+          c = C.ring_c[i % kRing];  // kept until chunk i + 64 is resolved
+          phys = C.ring_p[i % kRing];
         }
-        const uint64_t tmask = vmask >> (2 * cq);  // bit 8 j + e: token 8 j + 2 cq + e
+        const int pos = c * kBs + (t & 63);
+        const bool real = phys >= 0 && pos < len;  // the row holds a token
+        const bool att =
+            real && ((((C.sel_bits[c >> 5] >> (c & 31)) & 1u) != 0u) || pos < sink || pos >= wstart);
         tc_fence_after();
-        float sv[32];
-        tmem_ld16x256b_x8(t_w + kColS + sb * kBs, sv);
+        float v[64];
+        tmem_ld32(t_w + kColS, v);
+        tmem_ld32(t_w + kColS + 32, v + 32);
         tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(smem_u32(&C.s_empty[sb]));
-        // masked row maxima (raw scores; scale > 0)
-        float mxa = -INFINITY, mxb = -INFINITY;
+        // raise step: an attended score exceeds its head's reference maximum by 2^8
+        bool need = false;
+        if (att) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const bool on = (tmask >> (8 * j + e)) & 1ull;
-            mxa = fmaxf(mxa, on ? sv[4 * j + e] : -INFINITY);
-            mxb = fmaxf(mxb, on ? sv[4 * j + 2 + e] : -INFINITY);
-          }
+          for (int h = 0; h < kHC; ++h) need |= v[h] * c2 > C.m_ref[h] + kRescale;
         }
-        const float mta = quad_max(mxa) * c2, mtb = quad_max(mxb) * c2;
-        const bool raise_a = mta > ma_ref + kRescale, raise_b = mtb > mb_ref + kRescale;
-        const float ma_old = ma_ref, mb_old = mb_ref;
-        ma_ref = raise_a ? mta : ma_ref;
-        mb_ref = raise_b ? mtb : mb_ref;
-        // P = 2^(s c2 - m) for attended tokens, 0 elsewhere
-        uint32_t pa[8], pb[8];
-        float sa = 0.f, sb_ = 0.f;  // this chunk's terms (added after any rescale of la, lb)
+        if (softmax_any(need)) {
+          float mx[64];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const bool on0 = (tmask >> (8 * j)) & 1ull, on1 = (tmask >> (8 * j + 1)) & 1ull;
-          const float a0 = on0 ? ex2_approx(fmaf(sv[4 * j], c2, -ma_ref)) : 0.f;
-          const float a1 = on1 ? ex2_approx(fmaf(sv[4 * j + 1], c2, -ma_ref)) : 0.f;
-          const float b0 = on0 ? ex2_approx(fmaf(sv[4 * j + 2], c2, -mb_ref)) : 0.f;
-          const float b1 = on1 ? ex2_approx(fmaf(sv[4 * j + 3], c2, -mb_ref)) : 0.f;
-          sa += a0 + a1;
-          sb_ += b0 + b1;
-          pa[j] = pack2<T>(a0, a1);
-          pb[j] = pack2<T>(b0, b1);
-        }
-        // O += P V of the previous chunk has finished: P is free and O holds it
-        if (i >= 1) {
-          ok = role_wait(C, smem_u32(&C.o_done), (i - 1) & 1);
-          if (__any_sync(0xffffffffu, !ok)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-        }
-        const bool resc_a = raise_a && ma_old != -INFINITY, resc_b = raise_b && mb_old != -INFINITY;
-        if (__any_sync(0xffffffffu, resc_a || resc_b)) {
-          // O rows of this warp at the old reference maxima: rescale in TMEM
-          const float alpha_a = resc_a ? exp2f(ma_old - ma_ref) : 1.f;
-          const float alpha_b = resc_b ? exp2f(mb_old - mb_ref) : 1.f;
-#pragma unroll 1
-          for (int cc = 0; cc < kDH; cc += 64) {
-            float o[32];
-            tmem_ld16x256b_x8(t_w + kColO + cc, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              o[4 * j] *= alpha_a;
-              o[4 * j + 1] *= alpha_a;
-              o[4 * j + 2] *= alpha_b;
-              o[4 * j + 3] *= alpha_b;
+          for (int h = 0; h < kHC; ++h) mx[h] = att ? v[h] * c2 : -INFINITY;
+          warp_transpose_reduce<true>(mx, lane);
+          C.red[warp][2 * lane] = mx[0];
+          C.red[warp][2 * lane + 1] = mx[1];
+          softmax_sync();
+          if (t < kHC) {
+            const float m = fmaxf(fmaxf(C.red[0][t], C.red[1][t]), fmaxf(C.red[2][t], C.red[3][t]));
+            const float old = C.m_ref[t];
+            float a = 1.f;
+            if (m > old + kRescale) {
+              C.m_ref[t] = m;
+              if (old != -INFINITY) {
+                a = exp2f(old - m);
+                C.rescale = 1;
+              }
             }
-            tmem_st16x256b_x8(t_w + kColO + cc, o);
+            C.alpha[t] = a;
           }
-          tmem_wait_st();
-          la *= alpha_a;
-          lb *= alpha_b;
+          softmax_sync();
+          if (C.rescale) {  // O^T columns of the raised heads (O^T += V^T P^T of pair q - 1 is done)
+            ok = role_wait(C, smem_u32(&C.o_done), (q - 1) & 1);
+            if (softmax_any(!ok)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j) {
+#pragma unroll 1
+              for (int hc = 0; hc < kHC; hc += 32) {
+                float o[32];
+                tmem_ld32(t_w + kColO + j * kHC + hc, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) o[e] *= C.alpha[hc + e];
+                tmem_st32(t_w + kColO + j * kHC + hc, o);
+              }
+            }
+            tmem_wait_st();
+            l0 *= C.alpha[2 * lane];
+            l1 *= C.alpha[2 * lane + 1];
+            softmax_sync();  // every thread has read the factors before the flag is cleared
+            if (t == 0) C.rescale = 0;
+          }
         }
-        la += sa;
-        lb += sb_;
-        // rows ra, rb of P: 128 bytes each, 128-byte swizzle (16-byte piece j at j ^ (row & 7))
+        // P = 2^(s c2 - m) for an attended token, 0 otherwise; row t of P^T (128-byte
+        // swizzle: 16-byte piece j of the row at j ^ (t & 7))
+#pragma unroll
+        for (int h = 0; h < kHC; ++h) v[h] = att ? ex2_approx(fmaf(v[h], c2, -C.m_ref[h])) : 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const uint32_t off = (((uint32_t)j ^ psw) << 4) + 4 * cq;
-          *reinterpret_cast<uint32_t*>(prow_a + off) = pa[j];
-          *reinterpret_cast<uint32_t*>(prow_b + off) = pb[j];
+          const uint4 w4 = make_uint4(pack2<T>(v[8 * j], v[8 * j + 1]), pack2<T>(v[8 * j + 2], v[8 * j + 3]),
+                                      pack2<T>(v[8 * j + 4], v[8 * j + 5]), pack2<T>(v[8 * j + 6], v[8 * j + 7]));
+          *reinterpret_cast<uint4*>(prow + (((uint32_t)j ^ psw) << 4)) = w4;
         }
-        if (good < kBs) {  // rows holding no token: zero this CTA's V columns (the scores are done)
-          uint8_t* v = st_s + st * kStageBytes + dh * 4 * kStBlock;
-          const int rows = kBs - good;
-          for (int e = tid; e < 4 * rows * 8; e += kSoftmaxThreads) {
-            const int kb = e / (rows * 8);
-            const int row = good + (e / 8) % rows;
-            *reinterpret_cast<uint4*>(v + kb * kStBlock + row * 128 + (e & 7) * 16) = make_uint4(0, 0, 0, 0);
+        if (!real) {  // a row without a token: zero it in the latent k-blocks (V^T of P V)
+#pragma unroll
+          for (int kb = 0; kb < kKB - 1; ++kb) {
+            uint4* row = reinterpret_cast<uint4*>(st_s + kb * kStBlock + t * 128);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) row[e] = make_uint4(0, 0, 0, 0);
           }
         }
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(smem_u32(&C.p_full));
+        // the per-head sums of P over this warp's tokens, while O^T += V^T P^T runs
+        warp_transpose_reduce<false>(v, lane);
+        l0 += v[0];
+        l1 += v[1];
       }
       if (ok) {
-        ok = role_wait(C, smem_u32(&C.o_done), (n_ck - 1) & 1);
-        ok = !__any_sync(0xffffffffu, !ok);
+        ok = role_wait(C, smem_u32(&C.o_done), (n_pairs - 1) & 1);
+        ok = !softmax_any(!ok);
       }
       if (!ok) {
         give_up(C, dp.err);
       } else {
-        // ---- epilogue: rows ra, rb of O (256 columns)
+        // ---- epilogue: per-head totals, then O^T rows d = 128 j + t
         tc_fence_after();
-        const float lta = quad_sum(la), ltb = quad_sum(lb);
-        const float inv_a = lta > 0.f ? 1.f / lta : 0.f, inv_b = ltb > 0.f ? 1.f / ltb : 0.f;
-        const int ha = hh * kHC + ra, hb = hh * kHC + rb;
-        // partials [sequence][split][dim][head], then max and sum [sequence][split][2][head]
+        C.red[warp][2 * lane] = l0;
+        C.red[warp][2 * lane + 1] = l1;
+        softmax_sync();
         const int64_t bs_ = (int64_t)b * p.n_splits + s;
-        float* part = dp.partials + (bs_ * kR + dh * kDH) * kH;
-        float* ml = dp.partials + (int64_t)p.batch * p.n_splits * kR * kH + bs_ * 2 * kH;
-        T* out_a = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)ha * dp.out_stride_head +
-                   dh * kDH;
-        T* out_b = out_a + 8 * dp.out_stride_head;
-#pragma unroll 1
-        for (int cc = 0; cc < kDH; cc += 64) {
-          float o[32];
-          tmem_ld16x256b_x8(t_w + kColO + cc, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int d = cc + 8 * j + 2 * cq;
-            if (direct) {
-              *reinterpret_cast<uint32_t*>(out_a + d) = pack2<T>(o[4 * j] * inv_a, o[4 * j + 1] * inv_a);
-              *reinterpret_cast<uint32_t*>(out_b + d) = pack2<T>(o[4 * j + 2] * inv_b, o[4 * j + 3] * inv_b);
-            } else {
-              part[(int64_t)d * kH + ha] = o[4 * j];
-              part[(int64_t)(d + 1) * kH + ha] = o[4 * j + 1];
-              part[(int64_t)d * kH + hb] = o[4 * j + 2];
-              part[(int64_t)(d + 1) * kH + hb] = o[4 * j + 3];
-            }
+        if (t < kHC) {
+          const float l = C.red[0][t] + C.red[1][t] + C.red[2][t] + C.red[3][t];
+          C.alpha[t] = l > 0.f ? 1.f / l : 0.f;
+          if (!direct) {
+            // max and sum [sequence][split][2][head]
+            float* ml = dp.partials + (int64_t)p.batch * p.n_splits * kR * kH + bs_ * 2 * kH + hh * kHC;
+            const float m = C.m_ref[t];
+            ml[t] = m == -INFINITY ? -INFINITY : m * 0.6931471805599453f;  // natural-log units
+            ml[kH + t] = l;
           }
         }
-        if (!direct && dh == 0 && cq == 0) {
-          ml[ha] = ma_ref == -INFINITY ? -INFINITY : ma_ref * 0.6931471805599453f;  // natural-log units
-          ml[hb] = mb_ref == -INFINITY ? -INFINITY : mb_ref * 0.6931471805599453f;
-          ml[kH + ha] = lta;
-          ml[kH + hb] = ltb;
+        softmax_sync();
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+          const int d = j * kPair + t;
+          float o[64];
+          tmem_ld32(t_w + kColO + j * kHC, o);
+          tmem_ld32(t_w + kColO + j * kHC + 32, o + 32);
+          tmem_wait_ld();
+          if (direct) {
+            T* out = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq +
+                     (int64_t)hh * kHC * dp.out_stride_head + d;
+#pragma unroll
+            for (int h = 0; h < kHC; ++h) out[(int64_t)h * dp.out_stride_head] = to_elem<T>(o[h] * C.alpha[h]);
+          } else {
+            // partials [sequence][split][head][dim]: the warp's 32 dims of each head are one
+            // 128-byte line
+            float* part = dp.partials + (bs_ * kH + hh * kHC) * kR + d;
+#pragma unroll
+            for (int h = 0; h < kHC; ++h) part[(int64_t)h * kR] = o[h];
+          }
         }
       }
     }
@@ -576,10 +575,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int h = hh * kHC + tid;
     if (tid == 0) mbar_wait(smem_u32(&C.q_full), 0);  // the Q copy lands before the CTA exits (bounded)
     if (direct) {
-      T* o = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)h * dp.out_stride_head +
-             dh * kDH;
-      for (int d = 0; d < kDH; d += 8) *reinterpret_cast<uint4*>(o + d) = make_uint4(0, 0, 0, 0);
-    } else if (dh == 0) {
+      T* o = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)h * dp.out_stride_head;
+      for (int d = 0; d < kR; d += 8) *reinterpret_cast<uint4*>(o + d) = make_uint4(0, 0, 0, 0);
+    } else {
       float* ml = dp.partials + (int64_t)p.batch * p.n_splits * kR * kH + ((int64_t)b * p.n_splits + s) * 2 * kH;
       ml[h] = -INFINITY;
       ml[kH + h] = 0.f;
@@ -595,49 +593,46 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Merge of the split partials: CTA = (sequence, 16 output dims), thread = head.
-// Every load of a warp reads 32 heads of one (split, dim): one 128-byte line.
-// Splits without attended tokens (weight 0) may hold stale values: their
+// Merge of the split partials: CTA = (sequence, head), thread = 4 output dims, so
+// every load of a warp is 512 contiguous bytes of one (split, head).  The split
+// statistics are read first (all at once, up to 16 splits a pass), then the partial
+// rows.  Splits without attended tokens (weight 0) may hold stale values: their
 // terms are skipped, never multiplied.
-constexpr int kMergeDims = 16;
-
 template <typename T>
-__global__ void __launch_bounds__(kH) sparse_mla_merge_kernel(DecodeParams dp, int n_splits) {
-  const int b = blockIdx.x / (kR / kMergeDims), d0 = (blockIdx.x % (kR / kMergeDims)) * kMergeDims;
-  const int h = threadIdx.x;
+__global__ void __launch_bounds__(kR / 4) sparse_mla_merge_kernel(DecodeParams dp, int n_splits) {
+  const int b = blockIdx.x / kH, h = blockIdx.x % kH;
+  const int d = threadIdx.x * 4;
   if (b >= dp.batch) return;
   const float* ml = dp.partials + (int64_t)dp.batch * n_splits * kR * kH + (int64_t)b * n_splits * 2 * kH + h;
+  const float* part = dp.partials + ((int64_t)b * n_splits * kH + h) * kR + d;
   float M = -INFINITY;
+#pragma unroll 16
   for (int sp = 0; sp < n_splits; ++sp) M = fmaxf(M, __ldcg(ml + sp * 2 * kH));
-  float L = 0.f, acc[kMergeDims];
-#pragma unroll
-  for (int j = 0; j < kMergeDims; ++j) acc[j] = 0.f;
-  const float* part = dp.partials + ((int64_t)b * n_splits * kR + d0) * kH + h;
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
   for (int sp = 0; sp < n_splits; ++sp) {
     const float m = __ldcg(ml + sp * 2 * kH);
-    if (m == -INFINITY) continue;
-    const float f = expf(m - M);
-    L = fmaf(__ldcg(ml + sp * 2 * kH + kH), f, L);
-    const float* ps = part + (int64_t)sp * kR * kH;
-    float v[kMergeDims];
-#pragma unroll
-    for (int j = 0; j < kMergeDims; ++j) v[j] = __ldcg(ps + j * kH);
-#pragma unroll
-    for (int j = 0; j < kMergeDims; ++j) acc[j] = fmaf(v[j], f, acc[j]);
+    const float l = __ldcg(ml + sp * 2 * kH + kH);
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(part + (int64_t)sp * kH * kR));
+    if (m != -INFINITY) {
+      const float f = expf(m - M);
+      L = fmaf(l, f, L);
+      acc.x = fmaf(v.x, f, acc.x);
+      acc.y = fmaf(v.y, f, acc.y);
+      acc.z = fmaf(v.z, f, acc.z);
+      acc.w = fmaf(v.w, f, acc.w);
+    }
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  T* o = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)h * dp.out_stride_head + d0;
-#pragma unroll
-  for (int j = 0; j < kMergeDims; j += 8)
-    *reinterpret_cast<uint4*>(o + j) =
-        make_uint4(pack2<T>(acc[j] * inv, acc[j + 1] * inv), pack2<T>(acc[j + 2] * inv, acc[j + 3] * inv),
-                   pack2<T>(acc[j + 4] * inv, acc[j + 5] * inv), pack2<T>(acc[j + 6] * inv, acc[j + 7] * inv));
+  T* o = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)h * dp.out_stride_head + d;
+  *reinterpret_cast<uint2*>(o) = make_uint2(pack2<T>(acc.x * inv, acc.y * inv), pack2<T>(acc.z * inv, acc.w * inv));
 }
 
 }  // namespace
 
 int sparse_mla_umma_splits(int batch) {
-  const int per_seq = num_sms() / (4 * (batch > 0 ? batch : 1));  // 4 CTAs per (split, sequence)
+  const int per_seq = num_sms() / (2 * (batch > 0 ? batch : 1));  // 2 CTAs (head halves) per (split, sequence)
   return per_seq < 1 ? 1 : (per_seq > 64 ? 64 : per_seq);
 }
 
@@ -650,12 +645,15 @@ bool sparse_mla_umma_supported(const SparseParams& p, int dtype) {
 
 int launch_sparse_mla_umma(const SparseParams& p, int dtype, cudaStream_t st) {
   const bool bf16 = dtype == SNAPMIND_DTYPE_BF16;
-  CUtensorMap qlat, qpe, lat, rope;
+  CUtensorMap qlat, qpe, lat, lat3, rope;
   const uint64_t rows = (uint64_t)p.num_blocks * kBs;
-  // Q rows of 64 heads and chunk rows of 64 tokens: all 8 latent k-blocks in one 3-D box, rope in a 2-D box
+  // Q^T rows of 64 heads: all 8 latent k-blocks in one 3-D box, rope in a 2-D box.  Chunk
+  // rows of 64 tokens: one 2-D box per latent k-block (the pair stage interleaves two
+  // chunks in every k-block) and one for rope; the 3-D map prefetches a chunk's latent rows.
   if (!tensor_map_col_blocks(&qlat, bf16, p.q_lat, (uint64_t)p.batch * kH, kR * 2, kR / 64, kHC) ||
       !tensor_map_2d(&qpe, bf16, p.q_pe, kP, (uint64_t)p.batch * kH, kP * 2, 64, kHC) ||
-      !tensor_map_col_blocks(&lat, bf16, p.latent, rows, kR * 2, kR / 64, kBs) ||
+      !tensor_map_2d(&lat, bf16, p.latent, kR, rows, kR * 2, 64, kBs) ||
+      !tensor_map_col_blocks(&lat3, bf16, p.latent, rows, kR * 2, kR / 64, kBs) ||
       !tensor_map_2d(&rope, bf16, p.rope, kP, rows, kP * 2, 64, kBs)) {
     set_last_error("sparse_mla_umma: tensor map encoding failed");
     return SNAPMIND_ERR_CUDA;
@@ -669,11 +667,11 @@ int launch_sparse_mla_umma(const SparseParams& p, int dtype, cudaStream_t st) {
       if (e != cudaSuccess) return cuda_status(e, "sparse_mla_umma smem attribute");
       attr = true;
     }
-    // x = 2 (head half) + (output-dim half)
-    kernel<<<dim3(4, p.n_splits, p.batch), kThreads, kSmemBytes, st>>>(qlat, qpe, lat, rope, p);
+    // x = head half
+    kernel<<<dim3(2, p.n_splits, p.batch), kThreads, kSmemBytes, st>>>(qlat, qpe, lat, lat3, rope, p);
     int rc = cuda_status(cudaGetLastError(), "sparse_mla_umma launch");
     if (rc != SNAPMIND_OK || p.n_splits == 1) return rc;
-    merge<<<dim3(p.batch * (kR / kMergeDims)), kH, 0, st>>>(p.dp, p.n_splits);
+    merge<<<dim3(p.batch * kH), kR / 4, 0, st>>>(p.dp, p.n_splits);
     return cuda_status(cudaGetLastError(), "sparse_mla_merge launch");
   };
   return bf16 ? go(sparse_mla_umma_kernel<__nv_bfloat16>, sparse_mla_merge_kernel<__nv_bfloat16>)
