@@ -108,6 +108,52 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ---- issue from a convergent warp ---------------------------------------------------
+// A role warp runs its loop with all 32 lanes and lets one elected lane issue each
+// single-thread instruction (TMA copy, MMA, commit, barrier arrive), predicated on
+// `leader`.  Issuing from a `lane == 0` branch instead, with barrier waits between the
+// instructions, measured about twice the cycles per tcgen05.mma on B200.
+__device__ __forceinline__ uint32_t elect_one_sync() {
+  uint32_t pred;
+  asm volatile("{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\tselp.u32 %0, 1, 0, e;\n\t}" : "=r"(pred));
+  return pred;
+}
+__device__ __forceinline__ void mbar_arrive_p(uint32_t leader, uint32_t bar) {
+  asm volatile("{ .reg .pred p; .reg .b64 st; setp.ne.b32 p, %0, 0; @p mbarrier.arrive.shared::cta.b64 st, [%1]; }" ::"r"(
+                   leader),
+               "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx_p(uint32_t leader, uint32_t bar, uint32_t bytes) {
+  asm volatile(
+      "{ .reg .pred p; .reg .b64 st; setp.ne.b32 p, %0, 0; @p mbarrier.arrive.expect_tx.shared::cta.b64 st, [%1], "
+      "%2; }" ::"r"(leader),
+      "r"(bar), "r"(bytes)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_p(uint32_t leader, uint32_t dst, const CUtensorMap* map, int x, int y,
+                                              uint32_t bar) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %0, 0; @p cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::"
+      "bytes [%1], [%2, {%3, %4}], [%5]; }" ::"r"(leader),
+      "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_3d_p(uint32_t leader, const CUtensorMap* map, int x, int y, int z) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %0, 0; @p cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%1, {%2, %3, %4}]; "
+      "}" ::"r"(leader),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_2d_p(uint32_t leader, const CUtensorMap* map, int x, int y) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %0, 0; @p cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%1, {%2, %3}]; }" ::"r"(
+          leader),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y)
+      : "memory");
+}
+
 // ---- tcgen05 ------------------------------------------------------------------
 // Allocation and release are warp-wide (.sync.aligned): call from one full warp.
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
@@ -130,6 +176,22 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// The same, issued by the lane whose `leader` is non-zero.
+__device__ __forceinline__ void umma_f16_p(uint32_t leader, uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %5, 0;\n\tsetp.ne.b32 e, %0, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], %2, %3, %4, p;\n\t}\n" ::"r"(leader),
+      "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_p(uint32_t leader, uint32_t bar) {
+  asm volatile(
+      "{ .reg .pred e; setp.ne.b32 e, %0, 0; @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+      "[%1]; }" ::"r"(leader),
+      "r"(bar)
       : "memory");
 }
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread has completed.

@@ -35,9 +35,12 @@
 //     (0 x garbage must not reach O); O^T += V^T P^T (V^T read MN-major from
 //     the staged rows, P^T MN-major); meanwhile the per-head sums of P are
 //     reduced across each warp by a transposing butterfly.
-//   The producer refills the stage once O^T += V^T P^T of the pair is done and
-//   keeps the next kPrefetch chunks prefetched into L2 (TMA prefetch, no
-//   shared memory), so the refill is served from L2.
+//   The producer refills the stage in five groups (latent k-blocks 2 g, 2 g + 1
+//   for g < 4, then rope): group g of the next pair loads as soon as O^T block
+//   g += V^T P^T of this pair is done, so the refill runs under the rest of
+//   P V and the next scores start on the groups already landed.  It keeps the
+//   next kPrefetch chunks prefetched into L2 (TMA prefetch, no shared memory),
+//   so the refill is served from L2.
 //   Handshakes are mbarriers (tcgen05.commit for the tensor core), every wait
 //   is bounded (about a second) and ends early once another role gave up, and
 //   TMEM is released on every path.
@@ -83,10 +86,15 @@ constexpr uint32_t kTmemCols = 512, kColO = 0, kColS = 256;
 constexpr float kRescale = 8.f;                         // log2 headroom of the reference maximum
 constexpr int kPrefetch = 4;                            // chunks prefetched into L2 ahead of the load
 constexpr int kRing = 64;                               // resolved (chunk, block) pairs kept ahead
+// The stage is refilled in groups: group g < 4 = latent k-blocks 2 g, 2 g + 1 (the V rows
+// of output block g), group 4 = the rope k-block (P^T during P V).  Group g of the next pair
+// loads as soon as O^T block g += V^T P^T is done, so the refill overlaps the rest of P V.
+constexpr int kGroups = 5;
+__host__ __device__ constexpr uint32_t group_bytes(int g) { return g < kGroups - 1 ? 2 * kHalfBlock : kHalfBlock; }
 
 struct Ctrl {
-  uint64_t full;    // producer -> MMA, softmax: pair staged
-  uint64_t empty;   // MMA commit after O^T += V^T P^T: stage free
+  uint64_t full[kGroups];       // producer -> MMA: group g of the pair staged
+  uint64_t empty[kGroups - 1];  // MMA commit after O^T block g += V^T P^T: latent group g free
   uint64_t s_full;  // MMA commit after S^T: scores ready
   uint64_t p_full;  // softmax threads: P^T written, empty rows zeroed (and O rescaled)
   uint64_t o_done;  // MMA commit after O^T += V^T P^T
@@ -211,8 +219,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q_row0 = b * kH + hh * kHC;  // first row of this CTA's heads in q_lat / q_pe
 
   if (tid == 0) {
-    mbar_init(smem_u32(&C.full), 1);
-    mbar_init(smem_u32(&C.empty), 1);
+    for (int g = 0; g < kGroups; ++g) mbar_init(smem_u32(&C.full[g]), 1);
+    for (int g = 0; g < kGroups - 1; ++g) mbar_init(smem_u32(&C.empty[g]), 1);
     mbar_init(smem_u32(&C.s_full), 1);
     mbar_init(smem_u32(&C.p_full), kSoftmaxThreads);
     mbar_init(smem_u32(&C.o_done), 1);
@@ -299,10 +307,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kProducerWarp) {
       // ---------------------------------------------------------------- TMA producer
       // The warp resolves the blocks of 32 chunks at a time (one table read per lane)
-      // into a ring; lane 0 loads pair q into the stage once O^T += V^T P^T of pair
-      // q - 1 is done, and keeps the chunks up to 2 q + 2 + kPrefetch prefetched into
-      // L2, so the refill finds its rows there.
-      int located = 0, prefetched = min(n_ck, 2), issued = -1;
+      // into a ring.  Then, with every lane running the loop and one elected lane
+      // issuing, it loads group g of pair q into the stage once O^T block g += V^T P^T
+      // of pair q - 1 is done (the rope group once all of P V is done), and keeps the
+      // chunks up to 2 q + 2 + kPrefetch prefetched into L2, so the refill finds its
+      // rows there.
+      const uint32_t leader = elect_one_sync();
+      int located = 0, prefetched = min(n_ck, 2);
+      int armed[kGroups];  // the last pair whose copies group g's full barrier counts (-1: none)
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g) armed[g] = -1;
       bool ok = true;
       for (int q = 0; q < n_pairs && ok; ++q) {
         while (min(n_ck, 2 * q + 2 + kPrefetch) > located) {  // warp-uniform
@@ -317,100 +331,120 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           located += 32;
         }
-        if (lane == 0) {
-          if (q > 0 && !role_wait(C, smem_u32(&C.empty), (q - 1) & 1)) {
-            give_up(C, dp.err);
-            ok = false;
+        int32_t phys[2];
+        int n_valid = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int i = 2 * q + h;
+          phys[h] = i < n_ck ? C.ring_p[i % kRing] : -1;
+          if (phys[h] >= 0) ++n_valid;
+          else if (i < n_ck && lane == 0) flag_error(dp.err, SNAPMIND_DEVERR_BLOCK_ID);
+        }
+#pragma unroll 1
+        for (int g = 0; g < kGroups; ++g) {
+          if (q > 0) {
+            const uint32_t freed = g < kGroups - 1 ? smem_u32(&C.empty[g]) : smem_u32(&C.o_done);
+            ok = __all_sync(0xffffffffu, role_wait(C, freed, (q - 1) & 1));
+            if (!ok) {
+              if (lane == 0) give_up(C, dp.err);
+              break;
+            }
+          }
+          const uint32_t bar = smem_u32(&C.full[g]);
+          if (n_valid == 0) {
+            mbar_arrive_p(leader, bar);
           } else {
-            const uint32_t bar = smem_u32(&C.full);
-            uint32_t bytes = 0;
+            mbar_arrive_expect_tx_p(leader, bar, n_valid * group_bytes(g));
+#pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int i = 2 * q + h;
-              if (i >= n_ck) continue;
-              if (C.ring_p[i % kRing] >= 0) bytes += kChunkBytes;
-              else flag_error(dp.err, SNAPMIND_DEVERR_BLOCK_ID);
-            }
-            if (bytes == 0) {
-              mbar_arrive(bar);
-            } else {
-              mbar_arrive_expect_tx(bar, bytes);
-              for (int h = 0; h < 2; ++h) {
-                const int i = 2 * q + h;
-                const int32_t phys = i < n_ck ? C.ring_p[i % kRing] : -1;
-                if (phys < 0) continue;
-                const int y = phys * kBs;
-                for (int kb = 0; kb < kKB - 1; ++kb)
-                  tma_load_2d(smem_u32(st_s + kb * kStBlock + h * kHalfBlock), &lat_map, kb * 64, y, bar);
-                tma_load_2d(smem_u32(st_s + (kKB - 1) * kStBlock + h * kHalfBlock), &rope_map, 0, y, bar);
-              }
-            }
-            issued = q;
-            for (; prefetched < min(n_ck, 2 * q + 2 + kPrefetch); ++prefetched) {
-              const int32_t pb = C.ring_p[prefetched % kRing];
-              if (pb >= 0) {
-                tma_prefetch_3d(&lat3_map, 0, pb * kBs, 0);
-                tma_prefetch_2d(&rope_map, 0, pb * kBs);
+              if (phys[h] < 0) continue;
+              const int y = phys[h] * kBs;
+              if (g < kGroups - 1) {
+                tma_load_2d_p(leader, smem_u32(st_s + 2 * g * kStBlock + h * kHalfBlock), &lat_map, 2 * g * 64, y,
+                              bar);
+                tma_load_2d_p(leader, smem_u32(st_s + (2 * g + 1) * kStBlock + h * kHalfBlock), &lat_map,
+                              (2 * g + 1) * 64, y, bar);
+              } else {
+                tma_load_2d_p(leader, smem_u32(st_s + (kKB - 1) * kStBlock + h * kHalfBlock), &rope_map, 0, y, bar);
               }
             }
           }
+          armed[g] = q;
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
+        // L2 prefetch of the chunks after this pair, queued behind the pair's own copies
+        for (; ok && prefetched < min(n_ck, 2 * q + 2 + kPrefetch); ++prefetched) {
+          const int32_t pb = C.ring_p[prefetched % kRing];
+          if (pb >= 0) {
+            tma_prefetch_3d_p(leader, &lat3_map, 0, pb * kBs, 0);
+            tma_prefetch_2d_p(leader, &rope_map, 0, pb * kBs);
+          }
+        }
       }
-      if (lane == 0) {
-        // before the shared memory is released: every copy issued has landed (bounded)
-        if (issued >= 0) mbar_wait(smem_u32(&C.full), issued & 1);
-        mbar_wait(smem_u32(&C.q_full), 0);
-      }
+      // before the shared memory is released: every copy issued has landed (bounded)
+#pragma unroll 1
+      for (int g = 0; g < kGroups; ++g)
+        if (armed[g] >= 0) mbar_wait(smem_u32(&C.full[g]), armed[g] & 1);
+      mbar_wait(smem_u32(&C.q_full), 0);
     } else if (warp == kMmaWarp) {
       // ---------------------------------------------------------------- MMA issuer
-      if (lane == 0) {
-        bool ok = role_wait(C, smem_u32(&C.q_full), 0);
-        uint32_t last_bar = 0, last_parity = 0;  // the latest commit: covers every MMA issued
-        for (int q = 0; q < n_pairs && ok; ++q) {
-          if (!role_wait(C, smem_u32(&C.full), q & 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // S^T = K Q^T over the 576 columns: the stage's token rows (A) against Q^T (B)
+      // Every lane runs the loop and its waits; one elected lane issues the MMAs and
+      // commits.
+      const uint32_t leader = elect_one_sync();
+      bool ok = __all_sync(0xffffffffu, role_wait(C, smem_u32(&C.q_full), 0));
+      uint32_t last_bar = 0, last_parity = 0;  // the latest commit: covers every MMA issued
+      for (int q = 0; q < n_pairs && ok; ++q) {
+        // S^T = K Q^T over the 576 columns: the stage's token rows (A) against Q^T (B),
+        // each group as soon as it has landed
+        bool kb_issued = false;
 #pragma unroll 1
-          for (int kb = 0; kb < kKB; ++kb) {
+        for (int kb = 0; kb < kKB; ++kb) {
+          if (kb % 2 == 0) {  // first k-block of group kb / 2 (the rope k-block is group 4)
+            ok = __all_sync(0xffffffffu, role_wait(C, smem_u32(&C.full[kb / 2]), q & 1));
+            if (!ok) break;
+            tc_fence_after();
+          }
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = smem_desc(smem_u32(st_s + kb * kStBlock + kk * 32), 16, 1024, kSwizzle128B);
-              const uint64_t bd = smem_desc(smem_u32(q_s + kb * kQBlock + kk * 32), 16, 1024, kSwizzle128B);
-              umma_f16(tmem + kColS, ad, bd, kIdescS, (kb > 0 || kk > 0) ? 1u : 0u);
-            }
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = smem_desc(smem_u32(st_s + kb * kStBlock + kk * 32), 16, 1024, kSwizzle128B);
+            const uint64_t bd = smem_desc(smem_u32(q_s + kb * kQBlock + kk * 32), 16, 1024, kSwizzle128B);
+            umma_f16_p(leader, tmem + kColS, ad, bd, kIdescS, (kb > 0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(smem_u32(&C.s_full));
-          last_bar = smem_u32(&C.s_full);
-          last_parity = q & 1;
-          if (!role_wait(C, smem_u32(&C.p_full), q & 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // O^T += V^T P^T: dim block j = latent k-blocks 2 j, 2 j + 1 (MN-major), P^T
-          // (MN-major), 16 tokens a step
-#pragma unroll 1
-          for (int j = 0; j < 4; ++j) {
-#pragma unroll
-            for (int ks = 0; ks < kPair / 16; ++ks) {
-              const uint64_t ad =
-                  smem_desc(smem_u32(st_s + 2 * j * kStBlock + ks * 16 * 128), kStBlock, 1024, kSwizzle128B);
-              const uint64_t bd = smem_desc(smem_u32(st_s + kPOff + ks * 16 * 128), kStBlock, 1024, kSwizzle128B);
-              umma_f16(tmem + kColO + j * kHC, ad, bd, kIdescPV, (q > 0 || ks > 0) ? 1u : 0u);
-            }
-          }
-          umma_commit(smem_u32(&C.empty));
-          umma_commit(smem_u32(&C.o_done));
-          last_bar = smem_u32(&C.o_done);
-          last_parity = q & 1;
+          kb_issued = true;
         }
         if (!ok) {
-          give_up(C, dp.err);
-          if (last_bar) mbar_wait(last_bar, last_parity);  // MMAs in flight finish (bounded) before TMEM goes
+          if (kb_issued) {  // cover the score MMAs already issued for this pair
+            umma_commit_p(leader, smem_u32(&C.s_full));
+            last_bar = smem_u32(&C.s_full);
+            last_parity = q & 1;
+          }
+          break;
         }
+        umma_commit_p(leader, smem_u32(&C.s_full));
+        last_bar = smem_u32(&C.s_full);
+        last_parity = q & 1;
+        ok = __all_sync(0xffffffffu, role_wait(C, smem_u32(&C.p_full), q & 1));
+        if (!ok) break;
+        tc_fence_after();
+        // O^T += V^T P^T: dim block j = latent k-blocks 2 j, 2 j + 1 (MN-major), P^T
+        // (MN-major), 16 tokens a step
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+          for (int ks = 0; ks < kPair / 16; ++ks) {
+            const uint64_t ad =
+                smem_desc(smem_u32(st_s + 2 * j * kStBlock + ks * 16 * 128), kStBlock, 1024, kSwizzle128B);
+            const uint64_t bd = smem_desc(smem_u32(st_s + kPOff + ks * 16 * 128), kStBlock, 1024, kSwizzle128B);
+            umma_f16_p(leader, tmem + kColO + j * kHC, ad, bd, kIdescPV, (q > 0 || ks > 0) ? 1u : 0u);
+          }
+          umma_commit_p(leader, smem_u32(&C.empty[j]));  // latent group j may refill for the next pair
+        }
+        umma_commit_p(leader, smem_u32(&C.o_done));
+        last_bar = smem_u32(&C.o_done);
+        last_parity = q & 1;
+      }
+      if (!ok) {
+        if (lane == 0) give_up(C, dp.err);
+        if (last_bar) mbar_wait(last_bar, last_parity);  // MMAs in flight finish (bounded) before TMEM goes
       }
     } else {
       // ---------------------------------------------------------------- softmax warps 0-3
@@ -423,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float l0 = 0.f, l1 = 0.f;  // sums of P over this warp's tokens for heads 2 lane, 2 lane + 1
       bool ok = true;
       for (int q = 0; q < n_pairs; ++q) {
-        ok = role_wait(C, smem_u32(&C.full), q & 1) && role_wait(C, smem_u32(&C.s_full), q & 1);
+        ok = role_wait(C, smem_u32(&C.s_full), q & 1);  // S^T done: every group of the pair landed
         if (softmax_any(!ok)) {
           ok = false;
           break;
@@ -594,10 +628,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Merge of the split partials: CTA = (sequence, head), thread = 4 output dims, so
-// every load of a warp is 512 contiguous bytes of one (split, head).  The split
-// statistics are read first (all at once, up to 16 splits a pass), then the partial
-// rows.  Splits without attended tokens (weight 0) may hold stale values: their
-// terms are skipped, never multiplied.
+// every load of a warp is 512 contiguous bytes of one (split, head).  The splits are
+// taken kMergeBatch at a time: each thread first issues the loads of every split of
+// the batch (its max, sum and four partial dims), all independent, so they are in
+// flight together; then it folds them in with a running maximum.  Splits without
+// attended tokens (max -inf, weight 0) may hold stale rows: their terms are
+// selected away, never multiplied.
+constexpr int kMergeBatch = 16;
+
 template <typename T>
 __global__ void __launch_bounds__(kR / 4) sparse_mla_merge_kernel(DecodeParams dp, int n_splits) {
   const int b = blockIdx.x / kH, h = blockIdx.x % kH;
@@ -605,23 +643,42 @@ __global__ void __launch_bounds__(kR / 4) sparse_mla_merge_kernel(DecodeParams d
   if (b >= dp.batch) return;
   const float* ml = dp.partials + (int64_t)dp.batch * n_splits * kR * kH + (int64_t)b * n_splits * 2 * kH + h;
   const float* part = dp.partials + ((int64_t)b * n_splits * kH + h) * kR + d;
-  float M = -INFINITY;
-#pragma unroll 16
-  for (int sp = 0; sp < n_splits; ++sp) M = fmaxf(M, __ldcg(ml + sp * 2 * kH));
-  float L = 0.f;
+  float M = -INFINITY, L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-  for (int sp = 0; sp < n_splits; ++sp) {
-    const float m = __ldcg(ml + sp * 2 * kH);
-    const float l = __ldcg(ml + sp * 2 * kH + kH);
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(part + (int64_t)sp * kH * kR));
-    if (m != -INFINITY) {
-      const float f = expf(m - M);
-      L = fmaf(l, f, L);
-      acc.x = fmaf(v.x, f, acc.x);
-      acc.y = fmaf(v.y, f, acc.y);
-      acc.z = fmaf(v.z, f, acc.z);
-      acc.w = fmaf(v.w, f, acc.w);
+  for (int s0 = 0; s0 < n_splits; s0 += kMergeBatch) {
+    float m[kMergeBatch], l[kMergeBatch];
+    float4 v[kMergeBatch];
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; ++i) {
+      const int sp = s0 + i;
+      m[i] = -INFINITY;
+      if (sp < n_splits) {
+        m[i] = __ldcg(ml + sp * 2 * kH);
+        l[i] = __ldcg(ml + sp * 2 * kH + kH);
+        v[i] = __ldcg(reinterpret_cast<const float4*>(part + (int64_t)sp * kH * kR));
+      }
+    }
+    float mb = M;
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; ++i) mb = fmaxf(mb, m[i]);
+    if (mb == -INFINITY) continue;  // nothing attended so far
+    const float r = M == -INFINITY ? 0.f : expf(M - mb);
+    L *= r;
+    acc.x *= r;
+    acc.y *= r;
+    acc.z *= r;
+    acc.w *= r;
+    M = mb;
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; ++i) {
+      if (m[i] != -INFINITY) {
+        const float f = expf(m[i] - M);
+        L = fmaf(l[i], f, L);
+        acc.x = fmaf(v[i].x, f, acc.x);
+        acc.y = fmaf(v[i].y, f, acc.y);
+        acc.z = fmaf(v[i].z, f, acc.z);
+        acc.w = fmaf(v[i].w, f, acc.w);
+      }
     }
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
