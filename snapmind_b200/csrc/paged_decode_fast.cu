@@ -85,6 +85,29 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Issue from a convergent warp: the producer warp runs its loop with every lane and
+// one elected lane (`leader` non-zero) issues each copy and barrier arrive.
+__device__ __forceinline__ uint32_t elect_one() {
+  uint32_t pred;
+  asm volatile("{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\tselp.u32 %0, 1, 0, e;\n\t}" : "=r"(pred));
+  return pred;
+}
+__device__ __forceinline__ void tma_load_2d_p(uint32_t leader, uint32_t dst, const CUtensorMap* map, int x, int y,
+                                              uint32_t bar) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %0, 0; @p cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::"
+      "bytes [%1], [%2, {%3, %4}], [%5]; }" ::"r"(leader),
+      "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx_p(uint32_t leader, uint32_t bar, uint32_t bytes) {
+  asm volatile(
+      "{ .reg .pred p; .reg .b64 st; setp.ne.b32 p, %0, 0; @p mbarrier.arrive.expect_tx.shared::cta.b64 st, [%1], "
+      "%2; }" ::"r"(leader),
+      "r"(bar), "r"(bytes)
+      : "memory");
+}
+
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
                                         uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -250,38 +273,40 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == kConsumers) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      for (int i = 0; i < n_tiles; ++i) {
-        const int st = i % kStages;
-        const uint32_t parity = ((i / kStages) & 1) ^ 1;
-        if (!mbar_wait(smem_u32(&S.empty[st]), parity)) {
+    // every lane runs the loop and its waits; one elected lane issues the copies
+    const uint32_t leader = elect_one();
+    for (int i = 0; i < n_tiles; ++i) {
+      const int st = i % kStages;
+      const uint32_t parity = ((i / kStages) & 1) ^ 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&S.empty[st]), parity))) {
+        if (lane == 0) {
           flag_error(p.err, SNAPMIND_DEVERR_TIMEOUT);
           atomicExch(&S.abort, 1);
-          break;
         }
-        if (read_abort(S)) break;
-        const int tile_t0 = t0 + i * kTile;
-        const int tile_n = min(kTile, t1 - tile_t0);
-        const int jb = (tile_t0 - t0) / BS;     // first block of the tile (split-relative)
-        const int nb = (tile_n + BS - 1) / BS;  // blocks holding valid keys
-        uint32_t bytes = 0;
-        for (int j = 0; j < nb; ++j)
-          if (S.table[jb + j] >= 0) bytes += 4u * BS * 128u;
-        const uint32_t fb = smem_u32(&S.full[st]);
-        mbar_arrive_expect_tx(fb, bytes);
-        uint8_t* stage = ring + st * kStageBytes;
-        for (int j = 0; j < nb; ++j) {
-          const int32_t phys = S.table[jb + j];
-          if (phys < 0) continue;
-          const int y = (phys * p.n_kv_heads + kvh) * BS;
-          const uint32_t row_off = j * BS * 128;
-          tma_load_2d(smem_u32(stage + 0 * kHalfBytes + row_off), &kmap, 0, y, fb);
-          tma_load_2d(smem_u32(stage + 1 * kHalfBytes + row_off), &kmap, 64, y, fb);
-          tma_load_2d(smem_u32(stage + 2 * kHalfBytes + row_off), &vmap, 0, y, fb);
-          tma_load_2d(smem_u32(stage + 3 * kHalfBytes + row_off), &vmap, 64, y, fb);
-        }
-        S.issued = i + 1;
+        break;
       }
+      if (__any_sync(0xffffffffu, read_abort(S) != 0)) break;
+      const int tile_t0 = t0 + i * kTile;
+      const int tile_n = min(kTile, t1 - tile_t0);
+      const int jb = (tile_t0 - t0) / BS;     // first block of the tile (split-relative)
+      const int nb = (tile_n + BS - 1) / BS;  // blocks holding valid keys
+      uint32_t bytes = 0;
+      for (int j = 0; j < nb; ++j)
+        if (S.table[jb + j] >= 0) bytes += 4u * BS * 128u;
+      const uint32_t fb = smem_u32(&S.full[st]);
+      mbar_arrive_expect_tx_p(leader, fb, bytes);
+      uint8_t* stage = ring + st * kStageBytes;
+      for (int j = 0; j < nb; ++j) {
+        const int32_t phys = S.table[jb + j];
+        if (phys < 0) continue;
+        const int y = (phys * p.n_kv_heads + kvh) * BS;
+        const uint32_t row_off = j * BS * 128;
+        tma_load_2d_p(leader, smem_u32(stage + 0 * kHalfBytes + row_off), &kmap, 0, y, fb);
+        tma_load_2d_p(leader, smem_u32(stage + 1 * kHalfBytes + row_off), &kmap, 64, y, fb);
+        tma_load_2d_p(leader, smem_u32(stage + 2 * kHalfBytes + row_off), &vmap, 0, y, fb);
+        tma_load_2d_p(leader, smem_u32(stage + 3 * kHalfBytes + row_off), &vmap, 64, y, fb);
+      }
+      if (lane == 0) S.issued = i + 1;
     }
   } else {
     // ------------------------------------------------------------ consumers
