@@ -63,17 +63,22 @@ __device__ __forceinline__ int64_t append_dst_row(const AppendParams& p, int lay
   return (((int64_t)phys * p.n_heads + h) * p.block_size + off);
 }
 
-// Same dtype on both sides: a byte copy in W-byte vectors.
+// Same dtype on both sides: a byte copy in W-byte vectors.  A team of lanes copies one
+// row (one token of one head of one layer): vpr lanes when a row's vpr vectors divide
+// the warp (two 256-byte rows per warp at head_dim 128 in 16-bit), else the whole warp.
+// The row's coordinates and destination are resolved once per row, not per vector.
 template <int W>
 __global__ void __launch_bounds__(256) kv_append_copy_kernel(AppendParams p) {
   using V = typename VecT<W>::type;
   const int vpr = p.row_bytes_out / W;  // vectors per row
+  const int team = (vpr < 32 && 32 % vpr == 0) ? vpr : 32;
+  const int per_warp = 32 / team;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane / team, sl = lane - sub * team;
   const int64_t rows = (int64_t)p.n_layers * p.batch * p.n_tokens * p.nkv * p.n_heads;
-  const int64_t total = rows * vpr;
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = idx / vpr;
-    const int v = (int)(idx - r * vpr);
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * per_warp + sub; r < rows;
+       r += warps * per_warp) {
     int64_t q = r;
     const int h = (int)(q % p.n_heads); q /= p.n_heads;
     const int kv = (int)(q % p.nkv); q /= p.nkv;
@@ -82,10 +87,10 @@ __global__ void __launch_bounds__(256) kv_append_copy_kernel(AppendParams p) {
     const int layer = (int)(q / p.batch);
     const int64_t row = append_dst_row(p, layer, b, t, h);
     if (row < 0) continue;
-    const char* src = p.in[kv] + layer * p.in_stride_layer + b * p.in_stride_seq +
-                      h * p.in_stride_head + t * p.in_stride_tok;
-    char* dst = p.pool[kv] + layer * p.pool_layer_stride + row * p.row_bytes_out;
-    reinterpret_cast<V*>(dst)[v] = reinterpret_cast<const V*>(src)[v];
+    const V* src = reinterpret_cast<const V*>(p.in[kv] + layer * p.in_stride_layer + b * p.in_stride_seq +
+                                              h * p.in_stride_head + t * p.in_stride_tok);
+    V* dst = reinterpret_cast<V*>(p.pool[kv] + layer * p.pool_layer_stride + row * p.row_bytes_out);
+    for (int v = sl; v < vpr; v += team) dst[v] = src[v];
   }
 }
 
@@ -525,8 +530,10 @@ int snapmind_kv_append(void* k_pool, void* v_pool, int pool_dtype, int64_t pool_
                              reinterpret_cast<uintptr_t>(k_pool), reinterpret_cast<uintptr_t>(v_pool),
                              p.pool_layer_stride);
     const int vw = w < w2 ? w : w2;
-    const int64_t total = rows * (p.row_bytes_out / (vw > 1 ? vw : 1));
-    const int grid = (int)((total + 255) / 256 < max_grid ? (total + 255) / 256 : max_grid);
+    const int vpr = p.row_bytes_out / (vw > 1 ? vw : 1);
+    const int per_warp = (vpr < 32 && 32 % vpr == 0) ? 32 / vpr : 1;
+    const int64_t blocks = (rows + 8 * per_warp - 1) / (8 * per_warp);  // 8 warps per block
+    const int grid = (int)(blocks < max_grid ? blocks : max_grid);
     switch (vw) {
       case 16: kv_append_copy_kernel<16><<<grid, 256, 0, s>>>(p); break;
       case 8: kv_append_copy_kernel<8><<<grid, 256, 0, s>>>(p); break;

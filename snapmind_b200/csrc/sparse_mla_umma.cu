@@ -71,9 +71,10 @@ constexpr int kR = 512, kP = 64;
 constexpr int kKB = (kR + kP) / 64;                     // 9 k-blocks of 64 elements
 constexpr int kBs = 64;                                 // block (chunk) size
 constexpr int kPair = 2 * kBs;                          // tokens per pair = MMA M
-constexpr int kSoftmaxThreads = 128;
-constexpr int kProducerWarp = 4, kMmaWarp = 5;
-constexpr int kThreads = 192;
+constexpr int kGroupHeads = 32;                         // heads of one softmax group
+constexpr int kSoftmaxThreads = 256;                    // two groups of 4 warps (128 token lanes each)
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
+constexpr int kThreads = 320;
 constexpr uint32_t kQBlock = kHC * 128;                 // one k-block of Q^T: 8 KB
 constexpr uint32_t kQBytes = kKB * kQBlock;             // 72 KB
 constexpr uint32_t kHalfBlock = kBs * 128;              // one chunk's rows of a k-block: 8 KB
@@ -102,7 +103,7 @@ struct Ctrl {
   uint32_t tmem_base;
   int32_t abort;
   int32_t count;
-  int32_t rescale;              // a raise step must rescale some head's O columns
+  int32_t rescale[2];           // per softmax group: a raise step must rescale some head's O columns
   int32_t ring_c[kRing];        // chunk id and block of chunk j of the split at j % kRing
   int32_t ring_p[kRing];
   uint32_t sel_bits[kBits / 32];
@@ -110,7 +111,7 @@ struct Ctrl {
   int32_t word_pre[kBits / 32 + 1];
   float m_ref[kHC];             // per-head reference maximum (log2 units of score * scale)
   float alpha[kHC];             // per-head rescale factor of a raise step; 1 / sum in the epilogue
-  float red[4][kHC];            // per-warp partial maxima / sums
+  float red[8][kGroupHeads];    // per softmax warp: partial maxima / sums of its group's heads
 };
 
 constexpr size_t kSmemBytes = 1024 + kQBytes + kStageBytes + sizeof(Ctrl);
@@ -164,28 +165,40 @@ __device__ __forceinline__ void give_up(Ctrl& C, int32_t* err) {
   flag_error(err, SNAPMIND_DEVERR_TIMEOUT);
 }
 
-// Named barrier 1 over the 128 softmax threads (the producer and MMA warps do not take part).
-__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-// The same barrier, returning whether `v` holds in any of the 128 threads.
+// Named barriers of the softmax threads (the producer and MMA warps do not take part):
+// 1 + g over the 128 threads of group g, 3 over both groups.
+__device__ __forceinline__ void group_sync(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
+// The group barrier, returning whether `v` holds in any of its 128 threads.
+__device__ __forceinline__ bool group_any(int g, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.or.pred q, %2, 128, p; selp.u32 %0, 1, 0, q; }"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(1 + g)
+      : "memory");
+  return r != 0;
+}
+// Barrier 3 over all 256 softmax threads, returning whether `v` holds in any of them.
 __device__ __forceinline__ bool softmax_any(bool v) {
   uint32_t r;
   asm volatile(
-      "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.or.pred q, 1, 128, p; selp.u32 %0, 1, 0, q; }"
+      "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.or.pred q, 3, 256, p; selp.u32 %0, 1, 0, q; }"
       : "=r"(r)
       : "r"((uint32_t)v)
       : "memory");
   return r != 0;
 }
 
-// Reduces 64 values per lane over the warp's 32 lanes by a transposing butterfly
-// (62 shuffles): afterwards lane l holds, in v[0] and v[1], the sum (or maximum)
-// over the warp of values 2 l and 2 l + 1.
-template <bool kMax>
-__device__ __forceinline__ void warp_transpose_reduce(float (&v)[64], int lane) {
+// Reduces N (32 or 64) values per lane over the warp's 32 lanes by a transposing
+// butterfly (N - 2 or N - 1 shuffles): afterwards lane l holds the sum (or maximum)
+// over the warp of value l in v[0] (N = 32), or of values 2 l and 2 l + 1 in v[0] and
+// v[1] (N = 64).
+template <int N, bool kMax>
+__device__ __forceinline__ void warp_transpose_reduce(float (&v)[N], int lane) {
 #pragma unroll
   for (int step = 0; step < 5; ++step) {
-    const int mask = 16 >> step;  // partner distance
-    const int n = 32 >> step;     // this lane keeps n of its current 2 n values
+    const int mask = 16 >> step;        // partner distance
+    const int n = (N / 2) >> step;      // this lane keeps n of its current 2 n values
     const bool upper = (lane & mask) != 0;
 #pragma unroll
     for (int i = 0; i < n; ++i) {
@@ -226,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(&C.o_done), 1);
     mbar_init(smem_u32(&C.q_full), 1);
     C.abort = 0;
-    C.rescale = 0;
+    C.rescale[0] = C.rescale[1] = 0;
     mbar_init_fence();
     // Q depends only on the sequence: its copy overlaps the selection set-up below
     const uint32_t qb = smem_u32(&C.q_full);
@@ -447,17 +460,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (last_bar) mbar_wait(last_bar, last_parity);  // MMAs in flight finish (bounded) before TMEM goes
       }
     } else {
-      // ---------------------------------------------------------------- softmax warps 0-3
-      // thread t = token t of the pair (TMEM lane t): chunk 2 q + t / 64, row t % 64
-      const int t = tid;
-      const uint32_t t_w = tmem + ((uint32_t)(warp * 32) << 16);
+      // ---------------------------------------------------------------- softmax warps 0-7
+      // thread = token t of the pair (TMEM lane t, warp w reads lanes 32 (w % 4) ..) and
+      // head group hg: heads [32 hg, 32 hg + 32) of the CTA's 64; token t is row t % 64 of
+      // chunk 2 q + t / 64
+      const int t = tid & (kPair - 1);
+      const int hg = tid >> 7;
+      const int h0 = hg * kGroupHeads;
+      const uint32_t t_w = tmem + ((uint32_t)((warp & 3) * 32) << 16);
       const float c2 = p.scale * 1.4426950408889634f;
       uint8_t* prow = st_s + kPOff + t * 128;
       const uint32_t psw = (uint32_t)(t & 7);
-      float l0 = 0.f, l1 = 0.f;  // sums of P over this warp's tokens for heads 2 lane, 2 lane + 1
+      float lsum = 0.f;  // sum of P over this warp's tokens for head h0 + lane
       bool ok = true;
       for (int q = 0; q < n_pairs; ++q) {
-        ok = role_wait(C, smem_u32(&C.s_full), q & 1);  // S^T done: every group of the pair landed
+        // S^T done: every group of the pair landed (both groups take this check every pair)
+        ok = ok && role_wait(C, smem_u32(&C.s_full), q & 1);
         if (softmax_any(!ok)) {
           ok = false;
           break;
@@ -473,77 +491,78 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool att =
             real && ((((C.sel_bits[c >> 5] >> (c & 31)) & 1u) != 0u) || pos < sink || pos >= wstart);
         tc_fence_after();
-        float v[64];
-        tmem_ld32(t_w + kColS, v);
-        tmem_ld32(t_w + kColS + 32, v + 32);
+        float v[kGroupHeads];
+        tmem_ld32(t_w + kColS + h0, v);
         tmem_wait_ld();
         // raise step: an attended score exceeds its head's reference maximum by 2^8
         bool need = false;
         if (att) {
 #pragma unroll
-          for (int h = 0; h < kHC; ++h) need |= v[h] * c2 > C.m_ref[h] + kRescale;
+          for (int h = 0; h < kGroupHeads; ++h) need |= v[h] * c2 > C.m_ref[h0 + h] + kRescale;
         }
-        if (softmax_any(need)) {
-          float mx[64];
+        if (group_any(hg, need)) {
+          // the scores are reduced in place (fewer live registers) and reloaded from TMEM below
 #pragma unroll
-          for (int h = 0; h < kHC; ++h) mx[h] = att ? v[h] * c2 : -INFINITY;
-          warp_transpose_reduce<true>(mx, lane);
-          C.red[warp][2 * lane] = mx[0];
-          C.red[warp][2 * lane + 1] = mx[1];
-          softmax_sync();
-          if (t < kHC) {
-            const float m = fmaxf(fmaxf(C.red[0][t], C.red[1][t]), fmaxf(C.red[2][t], C.red[3][t]));
-            const float old = C.m_ref[t];
+          for (int h = 0; h < kGroupHeads; ++h) v[h] = att ? v[h] * c2 : -INFINITY;
+          warp_transpose_reduce<kGroupHeads, true>(v, lane);
+          C.red[warp][lane] = v[0];
+          group_sync(hg);
+          if (t < kGroupHeads) {
+            const int w0 = hg * 4;
+            const float m = fmaxf(fmaxf(C.red[w0][t], C.red[w0 + 1][t]), fmaxf(C.red[w0 + 2][t], C.red[w0 + 3][t]));
+            const float old = C.m_ref[h0 + t];
             float a = 1.f;
             if (m > old + kRescale) {
-              C.m_ref[t] = m;
+              C.m_ref[h0 + t] = m;
               if (old != -INFINITY) {
                 a = exp2f(old - m);
-                C.rescale = 1;
+                C.rescale[hg] = 1;
               }
             }
-            C.alpha[t] = a;
+            C.alpha[h0 + t] = a;
           }
-          softmax_sync();
-          if (C.rescale) {  // O^T columns of the raised heads (O^T += V^T P^T of pair q - 1 is done)
+          group_sync(hg);
+          if (C.rescale[hg]) {  // O^T columns of the raised heads (O^T += V^T P^T of pair q - 1 is done)
+            // A failed wait does not leave the loop here: the other group is not in this
+            // branch, and both groups must meet at every barrier over all softmax threads.
+            // The abort flag makes the next shared check end the loop for both.
             ok = role_wait(C, smem_u32(&C.o_done), (q - 1) & 1);
-            if (softmax_any(!ok)) {
+            if (group_any(hg, !ok)) {
+              if (t == 0) give_up(C, dp.err);
               ok = false;
-              break;
-            }
-            tc_fence_after();
+            } else {
+              tc_fence_after();
 #pragma unroll 1
-            for (int j = 0; j < 4; ++j) {
-#pragma unroll 1
-              for (int hc = 0; hc < kHC; hc += 32) {
-                float o[32];
-                tmem_ld32(t_w + kColO + j * kHC + hc, o);
+              for (int j = 0; j < 4; ++j) {
+                float o[kGroupHeads];
+                tmem_ld32(t_w + kColO + j * kHC + h0, o);
                 tmem_wait_ld();
 #pragma unroll
-                for (int e = 0; e < 32; ++e) o[e] *= C.alpha[hc + e];
-                tmem_st32(t_w + kColO + j * kHC + hc, o);
+                for (int e = 0; e < kGroupHeads; ++e) o[e] *= C.alpha[h0 + e];
+                tmem_st32(t_w + kColO + j * kHC + h0, o);
               }
+              tmem_wait_st();
             }
-            tmem_wait_st();
-            l0 *= C.alpha[2 * lane];
-            l1 *= C.alpha[2 * lane + 1];
-            softmax_sync();  // every thread has read the factors before the flag is cleared
-            if (t == 0) C.rescale = 0;
+            lsum *= C.alpha[h0 + lane];
+            group_sync(hg);  // every thread has read the factors before the flag is cleared
+            if (t == 0) C.rescale[hg] = 0;
           }
+          tmem_ld32(t_w + kColS + h0, v);  // the scores again (S^T stays until the next pair's scores)
+          tmem_wait_ld();
         }
-        // P = 2^(s c2 - m) for an attended token, 0 otherwise; row t of P^T (128-byte
-        // swizzle: 16-byte piece j of the row at j ^ (t & 7))
+        // P = 2^(s c2 - m) for an attended token, 0 otherwise; this group's half of row t
+        // of P^T (128-byte swizzle: 16-byte piece j of the row at j ^ (t & 7))
 #pragma unroll
-        for (int h = 0; h < kHC; ++h) v[h] = att ? ex2_approx(fmaf(v[h], c2, -C.m_ref[h])) : 0.f;
+        for (int h = 0; h < kGroupHeads; ++h) v[h] = att ? ex2_approx(fmaf(v[h], c2, -C.m_ref[h0 + h])) : 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 4; ++j) {
           const uint4 w4 = make_uint4(pack2<T>(v[8 * j], v[8 * j + 1]), pack2<T>(v[8 * j + 2], v[8 * j + 3]),
                                       pack2<T>(v[8 * j + 4], v[8 * j + 5]), pack2<T>(v[8 * j + 6], v[8 * j + 7]));
-          *reinterpret_cast<uint4*>(prow + (((uint32_t)j ^ psw) << 4)) = w4;
+          *reinterpret_cast<uint4*>(prow + (((uint32_t)(4 * hg + j) ^ psw) << 4)) = w4;
         }
-        if (!real) {  // a row without a token: zero it in the latent k-blocks (V^T of P V)
+        if (!real) {  // a row without a token: zero it in the latent k-blocks (V^T of P V), half per group
 #pragma unroll
-          for (int kb = 0; kb < kKB - 1; ++kb) {
+          for (int kb = 4 * hg; kb < 4 * hg + 4; ++kb) {
             uint4* row = reinterpret_cast<uint4*>(st_s + kb * kStBlock + t * 128);
 #pragma unroll
             for (int e = 0; e < 8; ++e) row[e] = make_uint4(0, 0, 0, 0);
@@ -553,53 +572,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(smem_u32(&C.p_full));
         // the per-head sums of P over this warp's tokens, while O^T += V^T P^T runs
-        warp_transpose_reduce<false>(v, lane);
-        l0 += v[0];
-        l1 += v[1];
+        warp_transpose_reduce<kGroupHeads, false>(v, lane);
+        lsum += v[0];
       }
-      if (ok) {
-        ok = role_wait(C, smem_u32(&C.o_done), (n_pairs - 1) & 1);
-        ok = !softmax_any(!ok);
+      {  // every softmax thread takes this shared check, whichever way its loop ended
+        const bool fine = ok && role_wait(C, smem_u32(&C.o_done), (n_pairs - 1) & 1);
+        ok = !softmax_any(!fine);
       }
       if (!ok) {
         give_up(C, dp.err);
       } else {
-        // ---- epilogue: per-head totals, then O^T rows d = 128 j + t
+        // ---- epilogue: per-head totals, then O^T rows d = 128 j + t of this group's heads
         tc_fence_after();
-        C.red[warp][2 * lane] = l0;
-        C.red[warp][2 * lane + 1] = l1;
-        softmax_sync();
+        C.red[warp][lane] = lsum;
+        group_sync(hg);
         const int64_t bs_ = (int64_t)b * p.n_splits + s;
-        if (t < kHC) {
-          const float l = C.red[0][t] + C.red[1][t] + C.red[2][t] + C.red[3][t];
-          C.alpha[t] = l > 0.f ? 1.f / l : 0.f;
+        if (t < kGroupHeads) {
+          const int w0 = hg * 4;
+          const float l = C.red[w0][t] + C.red[w0 + 1][t] + C.red[w0 + 2][t] + C.red[w0 + 3][t];
+          C.alpha[h0 + t] = l > 0.f ? 1.f / l : 0.f;
           if (!direct) {
             // max and sum [sequence][split][2][head]
-            float* ml = dp.partials + (int64_t)p.batch * p.n_splits * kR * kH + bs_ * 2 * kH + hh * kHC;
-            const float m = C.m_ref[t];
+            float* ml = dp.partials + (int64_t)p.batch * p.n_splits * kR * kH + bs_ * 2 * kH + hh * kHC + h0;
+            const float m = C.m_ref[h0 + t];
             ml[t] = m == -INFINITY ? -INFINITY : m * 0.6931471805599453f;  // natural-log units
             ml[kH + t] = l;
           }
         }
-        softmax_sync();
+        group_sync(hg);
 #pragma unroll 1
         for (int j = 0; j < 4; ++j) {
           const int d = j * kPair + t;
-          float o[64];
-          tmem_ld32(t_w + kColO + j * kHC, o);
-          tmem_ld32(t_w + kColO + j * kHC + 32, o + 32);
+          float o[kGroupHeads];
+          tmem_ld32(t_w + kColO + j * kHC + h0, o);
           tmem_wait_ld();
           if (direct) {
             T* out = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq +
-                     (int64_t)hh * kHC * dp.out_stride_head + d;
+                     (int64_t)(hh * kHC + h0) * dp.out_stride_head + d;
 #pragma unroll
-            for (int h = 0; h < kHC; ++h) out[(int64_t)h * dp.out_stride_head] = to_elem<T>(o[h] * C.alpha[h]);
+            for (int h = 0; h < kGroupHeads; ++h)
+              out[(int64_t)h * dp.out_stride_head] = to_elem<T>(o[h] * C.alpha[h0 + h]);
           } else {
             // partials [sequence][split][head][dim]: the warp's 32 dims of each head are one
             // 128-byte line
-            float* part = dp.partials + (bs_ * kH + hh * kHC) * kR + d;
+            float* part = dp.partials + (bs_ * kH + hh * kHC + h0) * kR + d;
 #pragma unroll
-            for (int h = 0; h < kHC; ++h) part[(int64_t)h * kR] = o[h];
+            for (int h = 0; h < kGroupHeads; ++h) part[(int64_t)h * kR] = o[h];
           }
         }
       }
