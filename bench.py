@@ -1074,6 +1074,25 @@ def run_append_gather(args, dev, seed, dist, world) -> dict:
     total_bytes = (append_bytes + gather_bytes) * steps
     append_ms = statistics.fmean(e[0].elapsed_time(e[1]) for e in evs)
     gather_ms = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
+    # the append kernel alone: an eager call's event pair also spans the host's launch path
+    # (the device waits for it), so replay 20 appends of the step's token (each rewrites the
+    # same rows with the same bytes) from one CUDA graph and time the replay
+    pool.append(None, k_new, v_new)
+    torch.cuda.synchronize()
+    g_app = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_app):
+        for _ in range(20):
+            pool.append(None, k_new, v_new)
+    g_app.replay()
+    torch.cuda.synchronize()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    g_app.replay()
+    a1.record()
+    torch.cuda.synchronize()
+    append_kernel_ms = a0.elapsed_time(a1) / 20
+    del g_app
+    pool.check()
     pk = peaks()
     gather_gbs = gather_bytes / (gather_ms * 1e-3) / 1e9
     traffic = profile_traffic("kv_gather")
@@ -1086,6 +1105,9 @@ def run_append_gather(args, dev, seed, dist, world) -> dict:
         "append_ms": round(append_ms, 4),
         "gather_ms": round(gather_ms, 4),
         "append_gbs": round(append_bytes / (append_ms * 1e-3) / 1e9, 1),
+        "append_kernel_us": round(append_kernel_ms * 1e3, 2),
+        "append_kernel_gbs": round(append_bytes / (append_kernel_ms * 1e-3) / 1e9, 1),
+        "append_kernel_frac": round(append_bytes / (append_kernel_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
         "roofline": {
             "kernel": "kv_gather",
             "bound": "hbm",
