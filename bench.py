@@ -916,6 +916,7 @@ def run_mla_sparse(args, dev, seed, dist, world, cpu_baseline: bool = False) -> 
         return e0_.elapsed_time(e1_) * 1e3 / reps
 
     select_us = graph_us(lambda: sel.select(qsel, n_chunks_dev, k=MLA_TOPK))
+    query_us = graph_us(lambda: sel.query(hidden))
     sparse_us = graph_us(lambda: pool.sparse_decode(0, q_lat, q_pe, idx0, sink=4, window=1024, scale=scale))
     # the dominant kernel (sparse attention + its split merge), each launch timed alone on the
     # launching stream after an L2 flush: the ~29 MB it reads would otherwise stay in the 126 MB L2.
@@ -1000,6 +1001,7 @@ def run_mla_sparse(args, dev, seed, dist, world, cpu_baseline: bool = False) -> 
         "chunk_pool_frac": round(pool_bytes / (pool_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
         "gpu_launches": launches[0],
         "select_us": round(select_us, 2),
+        "query_us": round(query_us, 2),
         "select_key_gbs": round(key_bytes / (select_us * 1e-6) / 1e9, 1),
         "sparse_attn_us": round(sparse_us, 2),
         "sparse_attn_gbs": round(sparse_bytes / (sparse_us * 1e-6) / 1e9, 1),

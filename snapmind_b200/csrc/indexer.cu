@@ -907,14 +907,15 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
 // ---------------------------------------------------------------------------
 // query projection q[b] = W . h[b] (fp32 out): one read of W, HBM-bound
 // ---------------------------------------------------------------------------
-constexpr int kQueryRows = 2;    // output rows per CTA
-constexpr int kQueryParts = 8;   // warps splitting d_model for one output row
+constexpr int kQueryRows = 1;    // output rows per CTA
+constexpr int kQueryParts = 16;  // warps splitting d_model for one output row
 constexpr int kQueryBatch = 8;   // sequences per CTA (grid.y covers the rest)
 
-// CTA = (2 output rows, up to 8 sequences), 16 warps: warp (row, part) sums
-// part `part` of d_model for its row over the CTA's sequences with 16-byte
-// loads, two vectors per lane in flight (W read once; the hidden rows are
-// shared by every CTA through L2), then the 8 parts meet in shared memory.
+// CTA = (1 output row, up to 8 sequences), 16 warps: warp `part` sums part `part`
+// of d_model for the row over the CTA's sequences with 16-byte loads, two vectors
+// per lane in flight (W read once; the hidden rows are shared by every CTA through
+// L2), then the 16 parts meet in shared memory.  At d_model 7168 a lane's loads are
+// all in flight at once, and one CTA per output row spreads the 128 rows over the SMs.
 template <typename T>
 __global__ void __launch_bounds__(32 * kQueryRows * kQueryParts) indexer_query_kernel(
     const T* hidden, const T* w, float* out, int batch, int d_model, int out_dim, int vec) {
