@@ -69,7 +69,8 @@ __global__ void __launch_bounds__(kThreads) sparse_mla_kernel(SparseParams p) {
   }
   const int sink = min(p.sink, len);
   const int wstart = max(0, len - p.window);
-  if (tid == 0 && sink > 0) atomicOr(&inc_bits[0], 1u);
+  for (int c = tid; c < min((sink + bs - 1) / bs, n_chunks); c += kThreads)  // every chunk the sink touches
+    atomicOr(&inc_bits[c >> 5], 1u << (c & 31));
   for (int c = wstart / bs + tid; c < n_chunks; c += kThreads) {
     if (len > wstart) atomicOr(&inc_bits[c >> 5], 1u << (c & 31));
   }

@@ -157,7 +157,8 @@ __global__ void __launch_bounds__(32 * kWPM * MT, 1) sparse_mla_tc_kernel(Sparse
   }
   const int sink = min(p.sink, len);
   const int wstart = max(0, len - p.window);
-  if (tid == 0 && sink > 0) atomicOr(&S.inc_bits[0], 1u);
+  for (int c = tid; c < min((sink + bs - 1) / bs, n_chunks); c += kThreads)  // every chunk the sink touches
+    atomicOr(&S.inc_bits[c >> 5], 1u << (c & 31));
   if (len > wstart)
     for (int c = wstart / bs + tid; c < n_chunks; c += kThreads) atomicOr(&S.inc_bits[c >> 5], 1u << (c & 31));
   __syncthreads();

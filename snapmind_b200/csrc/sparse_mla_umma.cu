@@ -80,9 +80,8 @@ constexpr uint32_t kQBytes = kKB * kQBlock;             // 72 KB
 constexpr uint32_t kHalfBlock = kBs * 128;              // one chunk's rows of a k-block: 8 KB
 constexpr uint32_t kStBlock = kPair * 128;              // one k-block of the pair: 16 KB
 constexpr uint32_t kStageBytes = kKB * kStBlock;        // 144 KB
-constexpr uint32_t kChunkBytes = kKB * kHalfBlock;      // bytes one chunk brings: 72 KB
 constexpr uint32_t kPOff = (kKB - 1) * kStBlock;        // P^T in the rope k-block
-constexpr int kBits = 3072;                             // chunks per sequence (bitmaps; longer tables take the mma.sync kernel)
+constexpr int kMaxSelected = 256;                       // selected chunk ids per sequence (more take the mma.sync kernel)
 constexpr uint32_t kTmemCols = 512, kColO = 0, kColS = 256;
 constexpr float kRescale = 8.f;                         // log2 headroom of the reference maximum
 constexpr int kPrefetch = 4;                            // chunks prefetched into L2 ahead of the load
@@ -104,11 +103,12 @@ struct Ctrl {
   int32_t abort;
   int32_t count;
   int32_t rescale[2];           // per softmax group: a raise step must rescale some head's O columns
-  int32_t ring_c[kRing];        // chunk id and block of chunk j of the split at j % kRing
+  int32_t n_extra;               // selected chunks outside the window and the sink chunks
+  int32_t sel_wfirst, sel_slast; // the first window chunk / the last sink chunk is among the selected
+  int32_t ring_c[kRing];        // chunk id, block and "selected" flag of chunk j of the split at j % kRing
   int32_t ring_p[kRing];
-  uint32_t sel_bits[kBits / 32];
-  uint32_t inc_bits[kBits / 32];
-  int32_t word_pre[kBits / 32 + 1];
+  int32_t ring_s[kRing];
+  int32_t extra[kMaxSelected];  // those chunks, in selected order
   float m_ref[kHC];             // per-head reference maximum (log2 units of score * scale)
   float alpha[kHC];             // per-head rescale factor of a raise step; 1 / sum in the epilogue
   float red[8][kGroupHeads];    // per softmax warp: partial maxima / sums of its group's heads
@@ -117,16 +117,29 @@ struct Ctrl {
 constexpr size_t kSmemBytes = 1024 + kQBytes + kStageBytes + sizeof(Ctrl);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-__device__ __forceinline__ int chunk_of_rank(const Ctrl& C, int words, int rank) {
-  int lo = 0, hi = words;  // last word w with word_pre[w] <= rank
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (C.word_pre[mid] <= rank) lo = mid; else hi = mid;
+// The attended chunks of a sequence, in the order the splits share them out:
+// the window chunks [wfirst, n_chunks) ascending, then the chunks the sink touches
+// [0, sink_chunks) that the window does not hold, then the selected chunks outside
+// both (first occurrence, in selected order).  Chunk of list position r and whether
+// that chunk is among the selected (which decides its positions outside the sink and
+// the window: only the first window chunk and the last sink chunk can have such).
+struct ChunkList {
+  int wfirst, n_win, sink_chunks, n_sink;
+};
+__device__ __forceinline__ void chunk_at(const Ctrl& C, const ChunkList& L, int r, int& c, int& sel) {
+  if (r < L.n_win) {
+    c = L.wfirst + r;
+    sel = r == 0 ? C.sel_wfirst : 1;  // later window chunks lie wholly inside the window
+    return;
   }
-  uint32_t word = C.inc_bits[lo];
-  int k = rank - C.word_pre[lo];
-  while (k-- > 0) word &= word - 1;
-  return lo * 32 + __ffs(word) - 1;
+  r -= L.n_win;
+  if (r < L.n_sink) {
+    c = r;
+    sel = c == L.sink_chunks - 1 ? C.sel_slast : 1;  // earlier sink chunks lie wholly inside the sink
+    return;
+  }
+  c = C.extra[r - L.n_sink];
+  sel = 1;
 }
 
 // 2^x by the hardware approximation (MUFU.EX2); -inf -> 0.
@@ -253,59 +266,71 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (tid < kHC) C.m_ref[tid] = -INFINITY;
 
-  // ---- attended chunks of sequence b: bitmaps and the prefix of their counts
-  // (the length and the first selected ids are loaded together)
-  const int sel0 = tid < p.k ? p.selected[(int64_t)b * p.k + tid] : -1;
+  // ---- the attended chunks of sequence b (the same list in every CTA of the sequence)
   int len = p.seq_lens[b];
   if (len < 0) len = 0;
-  int n_chunks = (len + kBs - 1) / kBs;
-  if (n_chunks > kBits) {
-    if (tid == 0 && s == 0 && blockIdx.x == 0) flag_error(dp.err, SNAPMIND_DEVERR_TABLE);
-    n_chunks = kBits;
-    len = kBits * kBs;
-  }
-  const int words = (n_chunks + 31) / 32;
-  for (int i = tid; i < words; i += kThreads) {
-    C.sel_bits[i] = 0u;
-    C.inc_bits[i] = 0u;
-  }
-  __syncthreads();
-  for (int i = tid; i < p.k; i += kThreads) {
-    const int c = i == tid ? sel0 : p.selected[(int64_t)b * p.k + i];
-    if (c >= 0 && c < n_chunks) {
-      atomicOr(&C.sel_bits[c >> 5], 1u << (c & 31));
-      atomicOr(&C.inc_bits[c >> 5], 1u << (c & 31));
-    }
-  }
+  const int n_chunks = (len + kBs - 1) / kBs;
   const int sink = min(p.sink, len);
   const int wstart = max(0, len - p.window);
-  if (tid == 0 && sink > 0) atomicOr(&C.inc_bits[0], 1u);
-  if (len > wstart)
-    for (int c = wstart / kBs + tid; c < n_chunks; c += kThreads) atomicOr(&C.inc_bits[c >> 5], 1u << (c & 31));
-  __syncthreads();
-  if (warp == 0) {
-    int carry = 0;
-    for (int w0 = 0; w0 < words; w0 += 32) {
-      const int cnt = (w0 + lane < words) ? __popc(C.inc_bits[w0 + lane]) : 0;
-      int pre = cnt;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, pre, off);
-        if (lane >= off) pre += y;
+  ChunkList L;
+  L.wfirst = len > wstart ? wstart / kBs : n_chunks;
+  L.n_win = n_chunks - L.wfirst;
+  L.sink_chunks = (sink + kBs - 1) / kBs;
+  L.n_sink = min(L.sink_chunks, L.wfirst);
+  if (warp == kProducerWarp) {
+    // The selected ids outside the window and the sink chunks (first occurrences, in
+    // order), then this split's first list entries with their block-table entries, so
+    // the first copies can go out as soon as the CTA-wide barrier below opens.
+    int n_extra = 0;
+    bool sw = false, sz = false;
+    for (int i0 = 0; i0 < p.k; i0 += 32) {  // warp-uniform
+      const int i = i0 + lane;
+      int c = i < p.k ? p.selected[(int64_t)b * p.k + i] : -1;
+      if (c >= n_chunks) c = -1;
+      sw |= __any_sync(0xffffffffu, c >= 0 && c == L.wfirst);
+      sz |= __any_sync(0xffffffffu, c >= 0 && c == L.sink_chunks - 1);
+      bool keep = c >= L.sink_chunks && c < L.wfirst;
+#pragma unroll 1
+      for (int d = 1; d < 32; ++d) {  // a repeat of an id in an earlier lane
+        const int o = __shfl_up_sync(0xffffffffu, c, d);
+        if (lane >= d && o == c) keep = false;
       }
-      if (w0 + lane < words) C.word_pre[w0 + lane] = carry + pre - cnt;
-      carry += __shfl_sync(0xffffffffu, pre, 31);
+      if (keep)
+        for (int e = 0; e < n_extra; ++e)  // or of an id kept from an earlier batch
+          if (C.extra[e] == c) {
+            keep = false;
+            break;
+          }
+      const uint32_t m = __ballot_sync(0xffffffffu, keep);
+      if (keep) C.extra[n_extra + __popc(m & ((1u << lane) - 1u))] = c;
+      n_extra += __popc(m);
+      __syncwarp();
     }
     if (lane == 0) {
-      C.word_pre[words] = carry;
-      C.count = carry;
+      C.n_extra = n_extra;
+      C.sel_wfirst = sw;
+      C.sel_slast = sz;
+    }
+    __syncwarp();
+    const int count = L.n_win + L.n_sink + n_extra;
+    int per = (count + p.n_splits - 1) / max(p.n_splits, 1);
+    per += per & 1;
+    const int c_lo = min(count, s * per), c_hi = min(count, c_lo + per);
+    if (lane < c_hi - c_lo) {  // list entries c_lo .. c_lo + 31 of this split
+      int c, sel;
+      chunk_at(C, L, c_lo + lane, c, sel);
+      int32_t phys = c < p.table_width ? p.tables[(int64_t)b * p.table_stride + c] : -1;
+      if (phys >= p.num_blocks) phys = -1;
+      C.ring_c[lane] = c;
+      C.ring_p[lane] = phys;
+      C.ring_s[lane] = sel;
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = C.tmem_base;
-  const int count = C.count;
+  const int count = L.n_win + L.n_sink + C.n_extra;
 
   // chunks of this split (the same for both head halves): an even count per split, so
   // only the last split can end in a half-empty pair
@@ -319,14 +344,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (n_ck > 0) {
     if (warp == kProducerWarp) {
       // ---------------------------------------------------------------- TMA producer
-      // The warp resolves the blocks of 32 chunks at a time (one table read per lane)
-      // into a ring.  Then, with every lane running the loop and one elected lane
+      // The warp resolves the list entries 32 at a time (one table read per lane) into a
+      // ring (the first 32 before the set-up barrier).  Then, with every lane running the
+      // loop and one elected lane
       // issuing, it loads group g of pair q into the stage once O^T block g += V^T P^T
       // of pair q - 1 is done (the rope group once all of P V is done), and keeps the
       // chunks up to 2 q + 2 + kPrefetch prefetched into L2, so the refill finds its
       // rows there.
       const uint32_t leader = elect_one_sync();
-      int located = 0, prefetched = min(n_ck, 2);
+      int located = 32, prefetched = min(n_ck, 2);
       int armed[kGroups];  // the last pair whose copies group g's full barrier counts (-1: none)
 #pragma unroll
       for (int g = 0; g < kGroups; ++g) armed[g] = -1;
@@ -335,11 +361,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         while (min(n_ck, 2 * q + 2 + kPrefetch) > located) {  // warp-uniform
           const int j = located + lane;
           if (j < n_ck) {
-            const int c = chunk_of_rank(C, words, c_lo + j);
+            int c, sel;
+            chunk_at(C, L, c_lo + j, c, sel);
             int32_t phys = c < p.table_width ? p.tables[(int64_t)b * p.table_stride + c] : -1;
             if (phys >= p.num_blocks) phys = -1;
             C.ring_c[j % kRing] = c;
             C.ring_p[j % kRing] = phys;
+            C.ring_s[j % kRing] = sel;
           }
           __syncwarp();
           located += 32;
@@ -481,15 +509,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const int i = 2 * q + (t >> 6);
-        int c = 0, phys = -1;
+        int c = 0, phys = -1, sel = 0;
         if (i < n_ck) {
           c = C.ring_c[i % kRing];  // kept until chunk i + 64 is resolved
           phys = C.ring_p[i % kRing];
+          sel = C.ring_s[i % kRing];
         }
         const int pos = c * kBs + (t & 63);
         const bool real = phys >= 0 && pos < len;  // the row holds a token
-        const bool att =
-            real && ((((C.sel_bits[c >> 5] >> (c & 31)) & 1u) != 0u) || pos < sink || pos >= wstart);
+        const bool att = real && (sel != 0 || pos < sink || pos >= wstart);
         tc_fence_after();
         float v[kGroupHeads];
         tmem_ld32(t_w + kColS + h0, v);
@@ -639,6 +667,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- every role is done with shared memory and TMEM
   tc_fence_before();
   __syncthreads();
+  // the merge kernel may launch now; it still waits for this whole grid before reading
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -658,6 +688,9 @@ template <typename T>
 __global__ void __launch_bounds__(kR / 4) sparse_mla_merge_kernel(DecodeParams dp, int n_splits) {
   const int b = blockIdx.x / kH, h = blockIdx.x % kH;
   const int d = threadIdx.x * 4;
+  // launched as a programmatic dependent of the attention kernel: its partials are
+  // complete and visible once this returns
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (b >= dp.batch) return;
   const float* ml = dp.partials + (int64_t)dp.batch * n_splits * kR * kH + (int64_t)b * n_splits * 2 * kH + h;
   const float* part = dp.partials + ((int64_t)b * n_splits * kH + h) * kR + d;
@@ -714,7 +747,7 @@ int sparse_mla_umma_splits(int batch) {
 bool sparse_mla_umma_supported(const SparseParams& p, int dtype) {
   const auto a16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
   return (dtype == SNAPMIND_DTYPE_BF16 || dtype == SNAPMIND_DTYPE_F16) && p.n_heads == kH && p.R == kR &&
-         p.P == kP && p.bs == kBs && p.table_width <= kBits && p.batch <= 65535 && a16(p.q_lat) && a16(p.q_pe) &&
+         p.P == kP && p.bs == kBs && p.k <= kMaxSelected && p.batch <= 65535 && a16(p.q_lat) && a16(p.q_pe) &&
          a16(p.latent) && a16(p.rope) && a16(p.dp.out) && encode_tiled() != nullptr;
 }
 
@@ -746,8 +779,18 @@ int launch_sparse_mla_umma(const SparseParams& p, int dtype, cudaStream_t st) {
     kernel<<<dim3(2, p.n_splits, p.batch), kThreads, kSmemBytes, st>>>(qlat, qpe, lat, lat3, rope, p);
     int rc = cuda_status(cudaGetLastError(), "sparse_mla_umma launch");
     if (rc != SNAPMIND_OK || p.n_splits == 1) return rc;
-    merge<<<dim3(p.batch * kH), kR / 4, 0, st>>>(p.dp, p.n_splits);
-    return cuda_status(cudaGetLastError(), "sparse_mla_merge launch");
+    // a programmatic dependent launch: the merge's launch overlaps the attention kernel's tail
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.batch * kH);
+    cfg.blockDim = dim3(kR / 4);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, merge, p.dp, p.n_splits), "sparse_mla_merge launch");
   };
   return bf16 ? go(sparse_mla_umma_kernel<__nv_bfloat16>, sparse_mla_merge_kernel<__nv_bfloat16>)
               : go(sparse_mla_umma_kernel<__half>, sparse_mla_merge_kernel<__half>);

@@ -214,7 +214,8 @@ def test_topk_sliced_equals_single_cta(cuda_device, k, n_chunks):
 
 
 @pytest.mark.parametrize("H", [32, 128])  # mma.sync kernel (32 heads), tcgen05 kernel (128 heads)
-@pytest.mark.parametrize("sink,window,n_splits", [(4, 1024, 4), (0, 0, 1), (4, 200, 3), (70, 5000, 2)])
+@pytest.mark.parametrize("sink,window,n_splits", [(4, 1024, 4), (0, 0, 1), (4, 200, 3), (70, 5000, 2),
+                                                   (150, 100, 3), (130, 0, 2), (64, 64, 1)])  # sinks past chunk 0
 def test_sparse_mla_decode_matches_oracle(cuda_device, sink, window, n_splits, H):
     B, R, P, bs, k = 4, 512, 64, 64, 8
     lens = [64 * 30 + 5, 700, 64 * 20, 1]
