@@ -68,14 +68,18 @@ def profile_traffic(kernel: str) -> dict | None:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    """nvidia-smi clock / throttle-reason samples during the timed region.
+
+    One sampler per node: under torchrun local rank 0 samples every local GPU in one
+    nvidia-smi process and the other ranks sample nothing, so N processes do not each
+    poll the driver while the timed region runs."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, gpu_indices: list[int]):
+        self.gpus = list(gpu_indices)
         self.proc = None
         self.lines: list[str] = []
         self._first = None
@@ -91,10 +95,16 @@ class ClockSampler:
         import threading
 
         self._first = threading.Event()
+        if not self.gpus:
+            return self
         try:
+            # nvidia-smi counts every GPU of the node: map CUDA's visible indices through
+            # CUDA_VISIBLE_DEVICES (indices or UUIDs, both of which --id accepts)
+            visible = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+            ids = [visible[g] if g < len(visible) else str(g) for g in self.gpus]
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "50"],
+                ["nvidia-smi", "--id=" + ",".join(ids), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -272,7 +282,9 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(dist)
     torch.cuda.synchronize()
-    with ClockSampler(dev.index) as clocks:
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+    with ClockSampler(list(range(local_world)) if local_rank == 0 else []) as clocks:
         t0.record()
         for s in range(steps):
             decode_step(ev[s])
@@ -290,6 +302,7 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
     bytes_per_launch = (mean_ctx_tokens * H * D * ELEM * 2 + 2 * DECODE_BATCH * HQ * D * ELEM
                         + 2 * 2 * DECODE_BATCH * H * D * ELEM)
     kernel_avg_ms = statistics.fmean(kernel_ms)
+    kernel_avg_ms_slowest = reduce_max(dist, kernel_avg_ms, dev)  # every rank takes this collective
     achieved_gbs = bytes_per_launch / (kernel_avg_ms * 1e-3) / 1e9
     pk = peaks()
     traffic = profile_traffic("paged_decode")
@@ -391,6 +404,7 @@ def run_b200(args, rank: int, world: int, dist) -> dict | None:
             "traffic": None if traffic is None else traffic.get("bytes_per_launch_scaled"),
             "algorithmic_bytes_per_launch": int(bytes_per_launch),
             "kernel_ms_avg": round(kernel_avg_ms, 4),
+            "kernel_ms_avg_slowest_rank": round(kernel_avg_ms_slowest, 4),
         },
         "e2e": {
             "value": round(DECODE_BATCH * world / (e2e_ms * 1e-3), 2),

@@ -688,6 +688,7 @@ __global__ void __launch_bounds__(kTopkThreads) indexer_topk_kernel(
     const T* q, const T* keys, const int32_t* n_chunks_arr, int n_chunks0, int max_chunks, int dim, float scale,
     float bias, int k, int sort_n, int32_t* out_idx, float* out_score, float* all_scores, int vec) {
   extern __shared__ unsigned long long skeys[];  // [sort_n]
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // as in the sliced kernel
   const int b = blockIdx.x;
   int nc = n_chunks_arr ? n_chunks_arr[b] : n_chunks0;
   nc = max(0, min(nc, max_chunks));
@@ -761,6 +762,9 @@ __global__ void __launch_bounds__(kSliceThreads) indexer_topk_sliced_kernel(
     int32_t* out_idx, float* out_score, float* all_scores, int vec) {
   extern __shared__ unsigned long long sk[];  // [max(kSliceChunks, merge_n)]
   __shared__ int s_last;
+  // a kernel launched as this one's programmatic dependent (the sparse attention) may be
+  // scheduled once every CTA here has started; it still waits for this grid to complete
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int slice = blockIdx.x, b = blockIdx.y;
   int nc = n_chunks_arr ? n_chunks_arr[b] : n_chunks0;
   nc = max(0, min(nc, max_chunks));

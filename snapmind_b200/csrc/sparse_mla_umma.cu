@@ -254,17 +254,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     C.abort = 0;
     C.rescale[0] = C.rescale[1] = 0;
     mbar_init_fence();
-    // Q depends only on the sequence: its copy overlaps the selection set-up below
-    const uint32_t qb = smem_u32(&C.q_full);
-    mbar_arrive_expect_tx(qb, kQBytes);
-    tma_load_3d(smem_u32(q_s), &qlat_map, 0, q_row0, 0, qb);  // the 8 latent k-blocks
-    tma_load_2d(smem_u32(q_s + (kKB - 1) * kQBlock), &qpe_map, 0, q_row0, qb);
   }
   if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(&C.tmem_base), kTmemCols);
     tmem_relinquish();
   }
   if (tid < kHC) C.m_ref[tid] = -INFINITY;
+  // The kernel is launched as a programmatic dependent of the previous kernel on the
+  // stream (the top-k selection that writes `selected`): everything above is on-chip,
+  // and no input is read before this wait for that grid to complete.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (tid == 0) {
+    // Q depends only on the sequence: its copy overlaps the selection set-up below
+    const uint32_t qb = smem_u32(&C.q_full);
+    mbar_arrive_expect_tx(qb, kQBytes);
+    tma_load_3d(smem_u32(q_s), &qlat_map, 0, q_row0, 0, qb);  // the 8 latent k-blocks
+    tma_load_2d(smem_u32(q_s + (kKB - 1) * kQBlock), &qpe_map, 0, q_row0, qb);
+  }
 
   // ---- the attended chunks of sequence b (the same list in every CTA of the sequence)
   int len = p.seq_lens[b];
@@ -775,21 +781,24 @@ int launch_sparse_mla_umma(const SparseParams& p, int dtype, cudaStream_t st) {
       if (e != cudaSuccess) return cuda_status(e, "sparse_mla_umma smem attribute");
       attr = true;
     }
-    // x = head half
-    kernel<<<dim3(2, p.n_splits, p.batch), kThreads, kSmemBytes, st>>>(qlat, qpe, lat, lat3, rope, p);
-    int rc = cuda_status(cudaGetLastError(), "sparse_mla_umma launch");
-    if (rc != SNAPMIND_OK || p.n_splits == 1) return rc;
-    // a programmatic dependent launch: the merge's launch overlaps the attention kernel's tail
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.batch * kH);
-    cfg.blockDim = dim3(kR / 4);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = st;
+    // Both kernels are programmatic dependent launches: each one's launch and on-chip
+    // set-up overlap the tail of the kernel before it, and each waits (griddepcontrol.wait)
+    // for that kernel to complete before it reads any input.
     cudaLaunchAttribute pdl[1];
     pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, p.n_splits, p.batch);  // x = head half
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = st;
     cfg.attrs = pdl;
     cfg.numAttrs = 1;
+    int rc = cuda_status(cudaLaunchKernelEx(&cfg, kernel, qlat, qpe, lat, lat3, rope, p), "sparse_mla_umma launch");
+    if (rc != SNAPMIND_OK || p.n_splits == 1) return rc;
+    cfg.gridDim = dim3(p.batch * kH);
+    cfg.blockDim = dim3(kR / 4);
+    cfg.dynamicSmemBytes = 0;
     return cuda_status(cudaLaunchKernelEx(&cfg, merge, p.dp, p.n_splits), "sparse_mla_merge launch");
   };
   return bf16 ? go(sparse_mla_umma_kernel<__nv_bfloat16>, sparse_mla_merge_kernel<__nv_bfloat16>)
