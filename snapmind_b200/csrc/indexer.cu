@@ -938,15 +938,25 @@ __global__ void __launch_bounds__(32 * kQueryRows * kQueryParts) indexer_query_k
       constexpr int V = 16 / (int)sizeof(T);
       const int nv = d_model / V;
       const int v0 = part * nv / kQueryParts, v1 = (part + 1) * nv / kQueryParts;
-#pragma unroll 2
-      for (int v = v0 + lane; v < v1; v += 32) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(wr + (int64_t)v * V);
-        const T* wt = reinterpret_cast<const T*>(&wv);
+      // two vectors per lane at a time: every load of the pair (W and the rows of the
+      // CTA's sequences) is issued before any of them is used, so they are in flight together
+      for (int v = v0 + lane; v < v1; v += 64) {
+        const bool two = v + 32 < v1;
+        uint4 wv[2], hv[2][kQueryBatch];
+        wv[0] = __ldg(reinterpret_cast<const uint4*>(wr + (int64_t)v * V));
+        wv[1] = two ? __ldg(reinterpret_cast<const uint4*>(wr + (int64_t)(v + 32) * V)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
         for (int j = 0; j < kQueryBatch; ++j) {
-          if (j < nb) {
-            const uint4 hv = *reinterpret_cast<const uint4*>(hidden + (int64_t)(b0 + j) * d_model + (int64_t)v * V);
-            const T* ht = reinterpret_cast<const T*>(&hv);
+          const T* hr = hidden + (int64_t)(b0 + (j < nb ? j : 0)) * d_model;
+          hv[0][j] = *reinterpret_cast<const uint4*>(hr + (int64_t)v * V);
+          hv[1][j] = two ? *reinterpret_cast<const uint4*>(hr + (int64_t)(v + 32) * V) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const T* wt = reinterpret_cast<const T*>(&wv[u]);
+#pragma unroll
+          for (int j = 0; j < kQueryBatch; ++j) {
+            const T* ht = reinterpret_cast<const T*>(&hv[u][j]);
 #pragma unroll
             for (int e = 0; e < V; ++e) acc[j] = fmaf(Conv<T>::to_f(wt[e]), Conv<T>::to_f(ht[e]), acc[j]);
           }
