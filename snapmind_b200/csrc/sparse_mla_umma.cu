@@ -609,8 +609,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         warp_transpose_reduce<kGroupHeads, false>(v, lane);
         lsum += v[0];
       }
-      {  // every softmax thread takes this shared check, whichever way its loop ended
-        const bool fine = ok && role_wait(C, smem_u32(&C.o_done), (n_pairs - 1) & 1);
+      {  // every softmax thread takes this shared check, whichever way its loop ended:
+         // block 0 of the last pair's P V is done (blocks 1-3 are waited for one by one
+         // below, so the first stores overlap the rest of P V)
+        const bool fine = ok && role_wait(C, smem_u32(&C.empty[0]), (n_pairs - 1) & 1);
         ok = !softmax_any(!fine);
       }
       if (!ok) {
@@ -636,6 +638,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         group_sync(hg);
 #pragma unroll 1
         for (int j = 0; j < 4; ++j) {
+          if (j > 0) {  // O^T block j is final once the last pair's block j has completed
+            if (!role_wait(C, smem_u32(&C.empty[j]), (n_pairs - 1) & 1)) {
+              give_up(C, dp.err);
+              break;
+            }
+            tc_fence_after();
+          }
           const int d = j * kPair + t;
           float o[kGroupHeads];
           tmem_ld32(t_w + kColO + j * kHC + h0, o);
