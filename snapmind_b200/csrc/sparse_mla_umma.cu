@@ -15,8 +15,10 @@
 // CTA = (head half hh, split, sequence): heads [64 hh, 64 hh + 64), every
 // output dim, the split's attended chunks two at a time ("pairs").  No
 // product is computed twice and nothing crosses between CTAs.
-// CTA = 6 warps: warps 0-3 softmax (thread = token of the pair = TMEM lane),
-// warp 4 TMA producer, warp 5 MMA issuer.
+// CTA = 10 warps: warps 0-7 softmax in two groups of 32 heads (warp w reads TMEM
+// lanes 32 (w % 4) ..: thread = token of the pair, both groups on the same lanes),
+// warp 8 TMA producer, warp 9 MMA issuer.  The producer and MMA warps run their
+// loops with every lane and one elected lane issues each copy, MMA and commit.
 //   Shared memory (1024-aligned, 128-byte swizzle):
 //     Q^T: 9 k-blocks x [64 heads x 64] = 72 KB, resident;
 //     one pair stage: 9 k-blocks x [128 tokens x 64] = 144 KB (chunk 2q in
@@ -25,22 +27,23 @@
 //       is free and holds P^T [128 tokens x 64 heads] for P V.
 //   TMEM (M = 128: row m in lane m): O^T as 4 blocks [128 dims x 64 heads] at
 //     columns 0-255, S^T [128 tokens x 64 heads] at column 256.
-//   Per pair: S^T over the 9 k-blocks (K-major operands); softmax: thread t
-//     loads its token's 64 scores (tcgen05.ld 32x32b) and masks the token if
+//   Per pair: S^T over the 9 k-blocks (K-major operands); softmax: each group
+//     loads its token's 32 scores (tcgen05.ld 32x32b) and masks the token if
 //     it is not attended; the scores are checked against a per-head reference
 //     maximum that is raised only when a score exceeds it by 2^8 (then the
-//     exact per-head maximum of the pair is reduced across the 128 threads and
-//     O's columns are rescaled in TMEM); P = exp2(s - m) is written as a bf16
-//     row of P^T; a row that holds no token is zeroed in the latent k-blocks
-//     (0 x garbage must not reach O); O^T += V^T P^T (V^T read MN-major from
-//     the staged rows, P^T MN-major); meanwhile the per-head sums of P are
-//     reduced across each warp by a transposing butterfly.
+//     exact per-head maximum of the pair is reduced across the group and O's
+//     columns are rescaled in TMEM); P = exp2(s - m) is written as the group's
+//     half of a bf16 row of P^T; a row that holds no token is zeroed in the
+//     latent k-blocks (0 x garbage must not reach O); O^T += V^T P^T (V^T read
+//     MN-major from the staged rows, P^T MN-major); meanwhile the per-head
+//     sums of P are reduced across each warp by a transposing butterfly.
 //   The producer refills the stage in five groups (latent k-blocks 2 g, 2 g + 1
 //   for g < 4, then rope): group g of the next pair loads as soon as O^T block
 //   g += V^T P^T of this pair is done, so the refill runs under the rest of
 //   P V and the next scores start on the groups already landed.  It keeps the
 //   next kPrefetch chunks prefetched into L2 (TMA prefetch, no shared memory),
-//   so the refill is served from L2.
+//   so the refill is served from L2.  The epilogue stores O^T block j as soon
+//   as the last pair's block j is done.
 //   Handshakes are mbarriers (tcgen05.commit for the tensor core), every wait
 //   is bounded (about a second) and ends early once another role gave up, and
 //   TMEM is released on every path.
@@ -101,7 +104,6 @@ struct Ctrl {
   uint64_t q_full;
   uint32_t tmem_base;
   int32_t abort;
-  int32_t count;
   int32_t rescale[2];           // per softmax group: a raise step must rescale some head's O columns
   int32_t n_extra;               // selected chunks outside the window and the sink chunks
   int32_t sel_wfirst, sel_slast; // the first window chunk / the last sink chunk is among the selected
