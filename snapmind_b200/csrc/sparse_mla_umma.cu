@@ -694,15 +694,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Merge of the split partials: CTA = (sequence, head), thread = 4 output dims, so
 // every load of a warp is 512 contiguous bytes of one (split, head).  The splits are
-// taken kMergeBatch at a time: each thread first issues the loads of every split of
-// the batch (its max, sum and four partial dims), all independent, so they are in
-// flight together; then it folds them in with a running maximum.  Splits without
-// attended tokens (max -inf, weight 0) may hold stale rows: their terms are
-// selected away, never multiplied.
-constexpr int kMergeBatch = 16;
+// taken kMergeBatch at a time: each thread first issues the loads of its four dims of
+// every split of the batch, all independent, then the first threads stage the splits'
+// max and sum in shared memory, and the rows are folded in with a running maximum.
+// At most 64 registers a thread, so a batch of 128 sequences x heads fits in one wave.
+// Splits without attended tokens (max -inf, weight 0) may hold stale rows: their
+// terms are selected away, never multiplied.
+constexpr int kMergeBatch = 10;
 
 template <typename T>
-__global__ void __launch_bounds__(kR / 4) sparse_mla_merge_kernel(DecodeParams dp, int n_splits) {
+__global__ void __launch_bounds__(kR / 4, 8) sparse_mla_merge_kernel(DecodeParams dp, int n_splits) {
+  __shared__ float s_m[kMergeBatch], s_l[kMergeBatch];
   const int b = blockIdx.x / kH, h = blockIdx.x % kH;
   const int d = threadIdx.x * 4;
   // launched as a programmatic dependent of the attention kernel: its partials are
@@ -713,41 +715,42 @@ __global__ void __launch_bounds__(kR / 4) sparse_mla_merge_kernel(DecodeParams d
   const float* part = dp.partials + ((int64_t)b * n_splits * kH + h) * kR + d;
   float M = -INFINITY, L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s0 = 0; s0 < n_splits; s0 += kMergeBatch) {
-    float m[kMergeBatch], l[kMergeBatch];
+  for (int s0 = 0; s0 < n_splits; s0 += kMergeBatch) {  // uniform over the CTA
     float4 v[kMergeBatch];
 #pragma unroll
-    for (int i = 0; i < kMergeBatch; ++i) {
-      const int sp = s0 + i;
-      m[i] = -INFINITY;
-      if (sp < n_splits) {
-        m[i] = __ldcg(ml + sp * 2 * kH);
-        l[i] = __ldcg(ml + sp * 2 * kH + kH);
-        v[i] = __ldcg(reinterpret_cast<const float4*>(part + (int64_t)sp * kH * kR));
-      }
+    for (int i = 0; i < kMergeBatch; ++i)
+      if (s0 + i < n_splits) v[i] = __ldcg(reinterpret_cast<const float4*>(part + (int64_t)(s0 + i) * kH * kR));
+    if (threadIdx.x < kMergeBatch) {
+      const int sp = s0 + threadIdx.x;
+      s_m[threadIdx.x] = sp < n_splits ? __ldcg(ml + sp * 2 * kH) : -INFINITY;
+      s_l[threadIdx.x] = sp < n_splits ? __ldcg(ml + sp * 2 * kH + kH) : 0.f;
     }
+    __syncthreads();
     float mb = M;
 #pragma unroll
-    for (int i = 0; i < kMergeBatch; ++i) mb = fmaxf(mb, m[i]);
-    if (mb == -INFINITY) continue;  // nothing attended so far
-    const float r = M == -INFINITY ? 0.f : expf(M - mb);
-    L *= r;
-    acc.x *= r;
-    acc.y *= r;
-    acc.z *= r;
-    acc.w *= r;
-    M = mb;
+    for (int i = 0; i < kMergeBatch; ++i) mb = fmaxf(mb, s_m[i]);
+    if (mb != -INFINITY) {  // something attended so far
+      const float r = M == -INFINITY ? 0.f : expf(M - mb);
+      L *= r;
+      acc.x *= r;
+      acc.y *= r;
+      acc.z *= r;
+      acc.w *= r;
+      M = mb;
 #pragma unroll
-    for (int i = 0; i < kMergeBatch; ++i) {
-      if (m[i] != -INFINITY) {
-        const float f = expf(m[i] - M);
-        L = fmaf(l[i], f, L);
-        acc.x = fmaf(v[i].x, f, acc.x);
-        acc.y = fmaf(v[i].y, f, acc.y);
-        acc.z = fmaf(v[i].z, f, acc.z);
-        acc.w = fmaf(v[i].w, f, acc.w);
+      for (int i = 0; i < kMergeBatch; ++i) {
+        const float m = s_m[i];
+        if (m != -INFINITY) {
+          const float f = expf(m - M);
+          L = fmaf(s_l[i], f, L);
+          acc.x = fmaf(v[i].x, f, acc.x);
+          acc.y = fmaf(v[i].y, f, acc.y);
+          acc.z = fmaf(v[i].z, f, acc.z);
+          acc.w = fmaf(v[i].w, f, acc.w);
+        }
       }
     }
+    __syncthreads();  // the next batch overwrites s_m / s_l
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
   T* o = reinterpret_cast<T*>(dp.out) + (int64_t)b * dp.out_stride_seq + (int64_t)h * dp.out_stride_head + d;
