@@ -321,8 +321,8 @@ SNAPMIND_API int64_t snapmind_indexer_topk_workspace_bytes(int32_t batch, int32_
 /*
  * Split count the sparse MLA kernels run best with for this batch (CTAs per
  * sequence along the attended positions): the tcgen05 kernel (128 heads,
- * kv_lora_rank 512, rope 64, block 64, bf16/f16) fills the SMs with
- * (split, output half) CTAs; the other shapes with (split, 32-head group) CTAs.
+ * kv_lora_rank 512, rope 64, block 64, bf16/f16, k <= 256) fills the SMs with
+ * (split, head half) CTAs; the other shapes with (split, 32-head group) CTAs.
  * No reference counterpart (the reference has no GPU path).
  */
 SNAPMIND_API int32_t snapmind_sparse_mla_default_splits(int32_t batch, int32_t n_heads, int32_t kv_lora_rank,
